@@ -1,0 +1,307 @@
+// SPDX-License-Identifier: MIT OR Apache-2.0
+//
+// The backward: dQ, dK, dV of O = softmax(Q K^T * scale) V from dO, the forward's O and its row
+// log-sum-exp L, written into ONE [b, s, 3, h, 64] buffer (a fused qkv projection's gradient).
+// Replaces fattn_bwd_dot_f32_d64 and fattn_bwd_f32_d64 (kernels/fused_attn.cu:45-63, :213-426).
+//
+// Step 1 (prep kernel): D[b, h, i] = sum_d dO[i, d] O[i, d], 16 lanes per row, one float4 each,
+// then the 16-lane butterfly; the same kernel clears the work ticket, the error flag and the dQ
+// turn counters that step 2 uses (the stream orders it before step 2).
+//
+// Step 2 (main kernel): one block per key block of BWD_BN = 64 keys of one (batch, head); K and
+// V stay in shared memory, dK and dV in registers. The block walks query tiles of BWD_BM = 64:
+//   phase 1: warps 0-3 compute S = Q K^T and P = exp(S * scale - L) (masked), warps 4-7 compute
+//            dP = dO V^T; each thread an 8 x 4 tile (rows 16(w%4) + ty + 2i, keys tx + 16jj).
+//            Then warps 4-7 form dS = P o (dP - D) at the same positions.
+//   phase 2: warps 0-3 accumulate dV += P^T dO, warps 4-7 dK += dS^T Q; each thread 8 keys x 4
+//            dims (keys 16(w%4) + 8ty .. +8, dims 4tx .. +4), summed over the tile's queries in
+//            index order.
+//   phase 3: all warps compute the tile's dQ partial dS K (rows 8w + ty + 2i, dims 4tx .. +4)
+//            and add it into dQ in KEY-BLOCK ORDER: key block 0 stores, each later one reads
+//            (through L2), adds and stores, the last contributor multiplies by `scale`. A turn
+//            counter per (batch, head, query tile) hands the tile from one key block to the next.
+//   Five products per tile, S and dP computed once (the reference's split: kernels/fused_attn.cu
+//   :178-205), no atomics on data: dQ = ((p0 + p1) + p2) + ... for every schedule.
+//
+// Forward progress without dispatch-order assumptions: a block takes its (batch, head, key block)
+// from a global ticket (atomicAdd), key blocks of one (batch, head) on consecutive tickets, so a
+// block only ever waits on blocks holding smaller tickets, which are already running or done.
+// Every wait is bounded (cfa::WAIT_TIMEOUT_NS); on expiry the error flag is set and the host
+// reads it with cfa_bwd_status. No GPU hangs on a broken invariant.
+#include "cfa_common.cuh"
+
+namespace cfa {
+namespace {
+
+constexpr int BWD_SMEM_FLOATS = 4 * 64 * LD + 2 * 64 * LDP + 2 * 64 + 4;
+
+__global__ void __launch_bounds__(PREP_THREADS) bwd_prep_kernel(const PrepArgs a) {
+  const int64_t gtid = static_cast<int64_t>(blockIdx.x) * PREP_THREADS + threadIdx.x;
+  const int64_t gstride = static_cast<int64_t>(gridDim.x) * PREP_THREADS;
+  for (int64_t z = gtid; z < a.n_zero; z += gstride) a.zero[z] = 0;
+
+  const int64_t rows = static_cast<int64_t>(a.B) * a.H * a.S;
+  const int64_t row = gtid >> 4;  // row = (b * H + h) * S + i
+  const int c = threadIdx.x & 15;
+  float x = 0.0f;
+  if (row < rows) {
+    const int i = static_cast<int>(row % a.S);
+    const int64_t bhr = row / a.S;
+    const int h = static_cast<int>(bhr % a.H), b = static_cast<int>(bhr / a.H);
+    const float4 ov = ld4(a.o + ((static_cast<int64_t>(b) * a.S + i) * a.H + h) * 64 + 4 * c);
+    const float4 gv = ld4(a.d_o + b * a.do_sb + h * a.do_sh + i * a.do_ss + 4 * c);
+    x = dot4(ov, gv, 0.0f);
+  }
+  // DETERMINISM: four products per lane in d order, then the butterfly 1, 2, 4, 8.
+  x = half_warp_sum(x);
+  if (row < rows && c == 0) a.dsum[row] = x;
+}
+
+template <bool CAUSAL>
+__global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs a) {
+  extern __shared__ float4 smem4[];
+  float* Ks = reinterpret_cast<float*>(smem4);  // [64][LD]
+  float* Vs = Ks + 64 * LD;                     // [64][LD]
+  float* Qs = Vs + 64 * LD;                     // [64][LD]
+  float* dOs = Qs + 64 * LD;                    // [64][LD]
+  float* Ps = dOs + 64 * LD;                    // [64][LDP] query-major
+  float* dSs = Ps + 64 * LDP;                   // [64][LDP] query-major
+  float* Lt = dSs + 64 * LDP;                   // [64] L of this tile (0 past S)
+  float* Dt = Lt + 64;                          // [64] D of this tile (0 past S)
+  int* s_int = reinterpret_cast<int*>(Dt + 64); // [0]: ticket, [1]: turn came
+
+  const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  const int ty = lane >> 4, tx = lane & 15;
+  const int grp = w >> 2, wg = w & 3;  // grp 0: S, P, dV; grp 1: dP, dS, dK (warp-uniform)
+  const int S = a.S;
+
+  if (tid == 0) s_int[0] = atomicAdd(a.ticket, 1);
+  __syncthreads();
+  const int ticket = s_int[0];
+  const int kb = ticket % a.n_kblocks;
+  const int bh = ticket / a.n_kblocks;
+  const int b = bh / a.H, h = bh % a.H;
+  const int k0 = kb * BWD_BN;
+
+  const float* qp = a.q + b * a.q_sb + h * a.q_sh;
+  const float* gp = a.d_o + b * a.do_sb + h * a.do_sh;
+  const float* lp = a.lse + static_cast<int64_t>(bh) * S;
+  const float* dp = a.dsum + static_cast<int64_t>(bh) * S;
+  int* turn = a.turn + static_cast<int64_t>(bh) * a.n_qtiles;
+  const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * 64;  // dqkv floats per (b, s)
+  float* dq_base = a.dqkv + static_cast<int64_t>(b) * S * row_stride + h * 64;
+
+  load_tile_async<64, BWD_THREADS>(Ks, a.k + b * a.k_sb + h * a.k_sh, a.k_ss, k0, S);
+  load_tile_async<64, BWD_THREADS>(Vs, a.v + b * a.v_sb + h * a.v_sh, a.v_ss, k0, S);
+  cp_async_commit();
+
+  float acc[8][4];  // grp 0: dV, grp 1: dK (unscaled); [a][e]: key 16wg + 8ty + a, dim 4tx + e
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
+
+  const int rb1 = 16 * wg + ty;       // phase 1 rows: rb1 + 2i
+  const int kb2 = 16 * wg + 8 * ty;   // phase 2 keys: kb2 .. kb2 + 7
+  const int rb3 = 8 * w + ty;         // phase 3 rows: rb3 + 2i
+
+  // Causal: queries before the block's first key never see it.
+  const int t_begin = CAUSAL ? k0 / BWD_BM : 0;
+  for (int t = t_begin; t < a.n_qtiles; ++t) {
+    const int q0 = t * BWD_BM;
+    // Every thread is done with the previous tile's Q, dO, P, dS.
+    __syncthreads();
+    load_tile_async<64, BWD_THREADS>(Qs, qp, a.q_ss, q0, S);
+    load_tile_async<64, BWD_THREADS>(dOs, gp, a.do_ss, q0, S);
+    cp_async_commit();
+    if (tid < 64) {
+      const int i = q0 + tid;
+      Lt[tid] = i < S ? lp[i] : 0.0f;
+    } else if (tid < 128) {
+      const int i = q0 + tid - 64;
+      Dt[tid - 64] = i < S ? dp[i] : 0.0f;
+    }
+    cp_async_wait_all();
+    __syncthreads();
+
+    // Phase 1. grp 0: s = Q K^T; grp 1: s = dO V^T (dP).
+    {
+      const float* As = grp ? dOs : Qs;
+      const float* Bs = grp ? Vs : Ks;
+      float s[8][4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) s[i][jj] = 0.0f;
+#pragma unroll 2
+      for (int c = 0; c < 64; c += 4) {
+        float4 bv[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) bv[jj] = ld4(Bs + (tx + 16 * jj) * LD + c);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 av = ld4(As + (rb1 + 2 * i) * LD + c);
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) s[i][jj] = dot4(av, bv[jj], s[i][jj]);
+        }
+      }
+      if (grp == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int il = rb1 + 2 * i, qi = q0 + il;
+          const float li = Lt[il];
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const int jl = tx + 16 * jj, j = k0 + jl;
+            const bool live = qi < S && j < S && !(CAUSAL && j > qi);
+            Ps[il * LDP + jl] = live ? expf(fmaf(s[i][jj], a.scale, -li)) : 0.0f;
+          }
+        }
+      }
+      __syncthreads();
+      if (grp == 1) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int il = rb1 + 2 * i;
+          const float di = Dt[il];
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const int jl = tx + 16 * jj;
+            dSs[il * LDP + jl] = Ps[il * LDP + jl] * (s[i][jj] - di);
+          }
+        }
+      }
+      __syncthreads();
+    }
+
+    // Phase 2. grp 0: dV[j] += sum_i P[i][j] dO[i]; grp 1: dK[j] += sum_i dS[i][j] Q[i].
+    // DETERMINISM: each dK, dV element is one thread's register, summed over query tiles and
+    // then queries in index order.
+    {
+      const float* Xs = grp ? dSs : Ps;
+      const float* Ys = grp ? Qs : dOs;
+#pragma unroll 4
+      for (int i = 0; i < BWD_BM; ++i) {
+        const float4 xa = ld4(Xs + i * LDP + kb2), xb = ld4(Xs + i * LDP + kb2 + 4);
+        const float4 y = ld4(Ys + i * LD + 4 * tx);
+        const float xs[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          acc[r][0] = fmaf(xs[r], y.x, acc[r][0]);
+          acc[r][1] = fmaf(xs[r], y.y, acc[r][1]);
+          acc[r][2] = fmaf(xs[r], y.z, acc[r][2]);
+          acc[r][3] = fmaf(xs[r], y.w, acc[r][3]);
+        }
+      }
+    }
+
+    // Phase 3: the dQ partial pq[r][e] = sum_j dS[rb3 + 2r][j] K[j][4tx + e], keys in order.
+    float pq[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) pq[r][e] = 0.0f;
+#pragma unroll 2
+    for (int j = 0; j < BWD_BN; j += 4) {
+      float4 k4[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) k4[u] = ld4(Ks + (j + u) * LD + 4 * tx);
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float4 d4 = ld4(dSs + (rb3 + 2 * r) * LDP + j);
+        const float ds[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          pq[r][0] = fmaf(ds[u], k4[u].x, pq[r][0]);
+          pq[r][1] = fmaf(ds[u], k4[u].y, pq[r][1]);
+          pq[r][2] = fmaf(ds[u], k4[u].z, pq[r][2]);
+          pq[r][3] = fmaf(ds[u], k4[u].w, pq[r][3]);
+        }
+      }
+    }
+
+    // This tile's contributors are key blocks 0 .. last (causal: those holding a key <= the
+    // tile's last query); each adds on its turn.
+    const int last = CAUSAL ? min(a.n_kblocks - 1, min(S - 1, q0 + BWD_BM - 1) / BWD_BN)
+                            : a.n_kblocks - 1;
+    bool go = true;
+    if (kb > 0) {
+      if (tid == 0) {
+        s_int[1] = wait_turn_bounded(turn + t, kb, a.err, a.timeout_ns) ? 1 : 0;
+        // ORDER: with the barrier below, extends thread 0's acquire to the whole block.
+        __threadfence();
+      }
+      __syncthreads();
+      go = s_int[1] != 0;
+    }
+    if (go) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int qi = q0 + rb3 + 2 * r;
+        if (qi >= S) continue;
+        float4* dst = reinterpret_cast<float4*>(dq_base + qi * row_stride + 4 * tx);
+        float4 v = make_float4(pq[r][0], pq[r][1], pq[r][2], pq[r][3]);
+        if (kb > 0) {
+          // Through L2 (__ldcg / __stcg): L1 is not coherent across SMs.
+          const float4 prev = __ldcg(dst);
+          v = make_float4(prev.x + v.x, prev.y + v.y, prev.z + v.z, prev.w + v.w);
+        }
+        if (kb == last)
+          v = make_float4(v.x * a.scale, v.y * a.scale, v.z * a.scale, v.w * a.scale);
+        __stcg(dst, v);
+      }
+    }
+    if (kb < last) {
+      // ORDER: every thread's dQ stores are visible GPU-wide before thread 0 hands the tile to
+      // key block kb + 1 (its acquire in wait_turn_bounded).
+      __threadfence();
+      __syncthreads();
+      if (tid == 0) st_release_gpu(turn + t, kb + 1);
+    }
+  }
+
+  // grp 0 stores dV into slot 2, grp 1 stores dK * scale into slot 1.
+  float* dst0 = a.dqkv + static_cast<int64_t>(b) * S * row_stride + (grp ? 1 : 2) * a.H * 64 +
+                h * 64 + 4 * tx;
+  const float f = grp ? a.scale : 1.0f;
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const int j = k0 + kb2 + r;
+    if (j >= S) continue;
+    *reinterpret_cast<float4*>(dst0 + j * row_stride) =
+        make_float4(acc[r][0] * f, acc[r][1] * f, acc[r][2] * f, acc[r][3] * f);
+  }
+}
+
+}  // namespace
+
+size_t bwd_smem_bytes() { return BWD_SMEM_FLOATS * sizeof(float); }
+
+cudaError_t setup_bwd_attributes() {
+  const int bytes = static_cast<int>(bwd_smem_bytes());
+  cudaError_t e = cudaFuncSetAttribute(bwd_ffma_kernel<false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(bwd_ffma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              bytes);
+}
+
+cudaError_t launch_bwd_prep(const PrepArgs& a, cudaStream_t stream) {
+  const int64_t rows = static_cast<int64_t>(a.B) * a.H * a.S;
+  int64_t blocks = (rows * 16 + PREP_THREADS - 1) / PREP_THREADS;
+  if (blocks < 1) blocks = 1;
+  bwd_prep_kernel<<<static_cast<unsigned>(blocks), PREP_THREADS, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bwd(const BwdArgs& a, int causal, cudaStream_t stream) {
+  const int64_t blocks = static_cast<int64_t>(a.n_kblocks) * a.B * a.H;
+  const dim3 grid(static_cast<unsigned>(blocks));
+  if (causal)
+    bwd_ffma_kernel<true><<<grid, BWD_THREADS, bwd_smem_bytes(), stream>>>(a);
+  else
+    bwd_ffma_kernel<false><<<grid, BWD_THREADS, bwd_smem_bytes(), stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace cfa

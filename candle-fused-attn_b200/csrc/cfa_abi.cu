@@ -1,0 +1,218 @@
+// SPDX-License-Identifier: MIT OR Apache-2.0
+//
+// The C ABI (include/cfa.h): argument checks, the once-per-device kernel attribute set-up, and
+// the launches. This is the B200 replacement of the reference's launch layer, src/cuda.rs: the
+// same inputs, the same outputs and layouts, the same stream discipline (everything on the
+// caller's stream, no synchronisation), with the checks the reference makes in Rust
+// (src/cuda.rs:69-93, src/lib.rs:431-435, :533-538) repeated here so a C caller gets them too.
+#include <mutex>
+
+#include "cfa_internal.h"
+
+namespace {
+
+using cfa::BwdArgs;
+using cfa::FwdArgs;
+using cfa::PrepArgs;
+
+constexpr int kMaxDevices = 64;
+
+// Per-device once flags: cudaFuncSetAttribute applies to the current device's context.
+struct DeviceOnce {
+  std::once_flag flag;
+  cudaError_t result = cudaSuccess;
+};
+DeviceOnce g_fwd_once[kMaxDevices];
+DeviceOnce g_bwd_once[kMaxDevices];
+
+int setup(DeviceOnce* table, cudaError_t (*fn)()) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CFA_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return CFA_ERR_CUDA;
+  DeviceOnce& d = table[dev];
+  std::call_once(d.flag, [&] { d.result = fn(); });
+  return d.result == cudaSuccess ? CFA_OK : CFA_ERR_LAUNCH;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool strides_ok(const int64_t* s) {
+  return s[0] % 4 == 0 && s[1] % 4 == 0 && s[2] % 4 == 0;
+}
+
+// Common shape checks. Returns CFA_OK with *empty set when there is nothing to do.
+int check_dims(int64_t B, int64_t H, int64_t S, int64_t D, bool* empty) {
+  *empty = false;
+  if (B < 0 || H < 0 || S < 0 || D < 0) return CFA_ERR_SHAPE;
+  if (D != CFA_HEAD_DIM) return CFA_ERR_HEAD_DIM;
+  if (B == 0 || H == 0 || S == 0) {
+    *empty = true;
+    return CFA_OK;
+  }
+  // Kernel indices: (b * H + h) and its tiles fit int32; element offsets are int64.
+  const int64_t lim = (int64_t(1) << 31) - 1;
+  if (B > lim || H > lim || S > lim) return CFA_ERR_OVERFLOW;
+  if (B * H > lim / ((S + 63) / 64)) return CFA_ERR_OVERFLOW;  // grid size
+  if (B * H * S > lim) return CFA_ERR_OVERFLOW;                 // row index of L, D
+  return CFA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cfa_abi_version(void) { return (1 << 16) | 0; }
+
+const char* cfa_strerror(int status) {
+  switch (status) {
+    case CFA_OK: return "fused_attention: ok";
+    case CFA_ERR_HEAD_DIM: return "fused_attention: the CUDA kernels take head_dim 64";
+    case CFA_ERR_ALIGNMENT: return "fused_attention: rows must be 16-byte aligned";
+    case CFA_ERR_SHAPE: return "fused_attention: negative dimension";
+    case CFA_ERR_OVERFLOW: return "fused_attention: problem size exceeds the kernels' index range";
+    case CFA_ERR_NULL: return "fused_attention: null pointer";
+    case CFA_ERR_WORKSPACE: return "fused_attention: workspace too small or misaligned";
+    case CFA_ERR_LAUNCH: return "fused_attention: kernel launch failed";
+    case CFA_ERR_TIMEOUT: return "fused_attention: a bounded device wait expired (results invalid)";
+    case CFA_ERR_CUDA: return "fused_attention: CUDA runtime error";
+    default: return "fused_attention: unknown status";
+  }
+}
+
+int cfa_fwd_f32_d64(const float* q, const int64_t q_strides[3], const float* k,
+                    const int64_t k_strides[3], const float* v, const int64_t v_strides[3],
+                    float* o, float* lse, int64_t batch, int64_t heads, int64_t seq,
+                    int64_t head_dim, float scale, int causal, void* stream) {
+  bool empty = false;
+  int st = check_dims(batch, heads, seq, head_dim, &empty);
+  if (st != CFA_OK || empty) return st;
+  if (!q || !k || !v || !o || !lse || !q_strides || !k_strides || !v_strides) return CFA_ERR_NULL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return CFA_ERR_ALIGNMENT;
+  if (!strides_ok(q_strides) || !strides_ok(k_strides) || !strides_ok(v_strides))
+    return CFA_ERR_ALIGNMENT;
+  st = setup(g_fwd_once, cfa::setup_fwd_attributes);
+  if (st != CFA_OK) return st;
+
+  FwdArgs a;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.o = o;
+  a.lse = lse;
+  a.q_sb = q_strides[0];
+  a.q_sh = q_strides[1];
+  a.q_ss = q_strides[2];
+  a.k_sb = k_strides[0];
+  a.k_sh = k_strides[1];
+  a.k_ss = k_strides[2];
+  a.v_sb = v_strides[0];
+  a.v_sh = v_strides[1];
+  a.v_ss = v_strides[2];
+  a.B = static_cast<int>(batch);
+  a.H = static_cast<int>(heads);
+  a.S = static_cast<int>(seq);
+  a.scale = scale;
+  a.n_qtiles = static_cast<int>((seq + cfa::FWD_BM - 1) / cfa::FWD_BM);
+  const cudaError_t e = cfa::launch_fwd(a, causal != 0, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CFA_OK : CFA_ERR_LAUNCH;
+}
+
+size_t cfa_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq) {
+  if (batch <= 0 || heads <= 0 || seq <= 0) return 256;
+  return cfa::bwd_workspace_layout(batch, heads, seq).total;
+}
+
+int cfa_bwd_f32_d64(const float* q, const int64_t q_strides[3], const float* k,
+                    const int64_t k_strides[3], const float* v, const int64_t v_strides[3],
+                    const float* o, const float* lse, const float* d_o,
+                    const int64_t do_strides[3], float* dqkv, void* workspace,
+                    size_t workspace_bytes, int64_t batch, int64_t heads, int64_t seq,
+                    int64_t head_dim, float scale, int causal, void* stream) {
+  bool empty = false;
+  int st = check_dims(batch, heads, seq, head_dim, &empty);
+  if (st != CFA_OK || empty) return st;
+  if (!q || !k || !v || !o || !lse || !d_o || !dqkv || !workspace || !q_strides || !k_strides ||
+      !v_strides || !do_strides)
+    return CFA_ERR_NULL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(d_o) ||
+      !aligned16(dqkv))
+    return CFA_ERR_ALIGNMENT;
+  if (!strides_ok(q_strides) || !strides_ok(k_strides) || !strides_ok(v_strides) ||
+      !strides_ok(do_strides))
+    return CFA_ERR_ALIGNMENT;
+  const cfa::BwdWorkspace lay = cfa::bwd_workspace_layout(batch, heads, seq);
+  if (workspace_bytes < lay.total || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return CFA_ERR_WORKSPACE;
+  st = setup(g_bwd_once, cfa::setup_bwd_attributes);
+  if (st != CFA_OK) return st;
+
+  char* ws = static_cast<char*>(workspace);
+  int* ticket = reinterpret_cast<int*>(ws + lay.ticket_off);
+  int* turn = reinterpret_cast<int*>(ws + lay.turn_off);
+  float* dsum = reinterpret_cast<float*>(ws + lay.dsum_off);
+  const int nqt = static_cast<int>((seq + cfa::BWD_BM - 1) / cfa::BWD_BM);
+  const int nkb = static_cast<int>((seq + cfa::BWD_BN - 1) / cfa::BWD_BN);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  PrepArgs p;
+  p.o = o;
+  p.d_o = d_o;
+  p.dsum = dsum;
+  // ticket and error flag are the first two ints; the turn counters start at turn_off. Clear
+  // the header and the counters as one range.
+  p.zero = ticket;
+  p.n_zero = static_cast<int64_t>(lay.turn_off / sizeof(int)) + batch * heads * nqt;
+  p.do_sb = do_strides[0];
+  p.do_sh = do_strides[1];
+  p.do_ss = do_strides[2];
+  p.B = static_cast<int>(batch);
+  p.H = static_cast<int>(heads);
+  p.S = static_cast<int>(seq);
+  cudaError_t e = cfa::launch_bwd_prep(p, s);
+  if (e != cudaSuccess) return CFA_ERR_LAUNCH;
+
+  BwdArgs a;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.d_o = d_o;
+  a.lse = lse;
+  a.dsum = dsum;
+  a.dqkv = dqkv;
+  a.turn = turn;
+  a.ticket = ticket;
+  a.err = ticket + 1;
+  a.q_sb = q_strides[0];
+  a.q_sh = q_strides[1];
+  a.q_ss = q_strides[2];
+  a.k_sb = k_strides[0];
+  a.k_sh = k_strides[1];
+  a.k_ss = k_strides[2];
+  a.v_sb = v_strides[0];
+  a.v_sh = v_strides[1];
+  a.v_ss = v_strides[2];
+  a.do_sb = do_strides[0];
+  a.do_sh = do_strides[1];
+  a.do_ss = do_strides[2];
+  a.B = static_cast<int>(batch);
+  a.H = static_cast<int>(heads);
+  a.S = static_cast<int>(seq);
+  a.scale = scale;
+  a.n_qtiles = nqt;
+  a.n_kblocks = nkb;
+  a.timeout_ns = cfa::WAIT_TIMEOUT_NS;
+  e = cfa::launch_bwd(a, causal != 0, s);
+  return e == cudaSuccess ? CFA_OK : CFA_ERR_LAUNCH;
+}
+
+int cfa_bwd_status(const void* workspace, void* stream) {
+  if (!workspace) return CFA_ERR_NULL;
+  int flags[2] = {0, 0};
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(flags, workspace, sizeof(flags), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return CFA_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return CFA_ERR_CUDA;
+  return flags[1] != 0 ? flags[1] : CFA_OK;
+}
+
+}  // extern "C"

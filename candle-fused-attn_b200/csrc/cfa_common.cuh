@@ -1,0 +1,128 @@
+// SPDX-License-Identifier: MIT OR Apache-2.0
+//
+// Device helpers shared by the sm_100a attention kernels: asynchronous 16-byte global->shared
+// copies, padded tile loads, row reductions over 16 lanes, and the bounded GPU-scope wait that
+// orders the backward's dQ accumulation.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "cfa_internal.h"
+
+namespace cfa {
+
+// Shared-memory row strides, in floats. LD pads a 64-float row to 68: rows stay 16-byte aligned
+// for float4 reads and consecutive rows start 4 banks apart, so the two rows read by the two
+// half-warps of one float4 load never share a bank. LDP = 80 pads the probability / dS tiles so
+// that the scalar stores of two half-warps (rows r and r + 1, 16 consecutive columns each) land
+// in disjoint bank halves.
+constexpr int LD = 68;
+constexpr int LDP = 80;
+
+__device__ __forceinline__ float4 ld4(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+
+// acc + a.b over four products, in x, y, z, w order (one fixed order: the bitwise gate).
+__device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
+  acc = fmaf(a.x, b.x, acc);
+  acc = fmaf(a.y, b.y, acc);
+  acc = fmaf(a.z, b.z, acc);
+  return fmaf(a.w, b.w, acc);
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem),
+               "r"(src_bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+}
+
+// ROWS rows of a strided [seq, 64] slice, starting at row `row0`, into a [ROWS][LD] tile by
+// NTHREADS threads, 16 bytes per copy. Rows at or past `seq` are zero-filled (source size 0; the
+// address given is row0's, which the caller guarantees is < seq, so no copy reads out of range).
+template <int ROWS, int NTHREADS>
+__device__ __forceinline__ void load_tile_async(float* dst, const float* __restrict__ src,
+                                                int64_t s_stride, int row0, int seq) {
+#pragma unroll
+  for (int idx = threadIdx.x; idx < ROWS * 16; idx += NTHREADS) {
+    const int r = idx >> 4, c4 = idx & 15;
+    const int row = row0 + r;
+    const bool ok = row < seq;
+    const float* g = src + static_cast<int64_t>(ok ? row : row0) * s_stride + 4 * c4;
+    cp_async16(dst + r * LD + 4 * c4, g, ok ? 16 : 0);
+  }
+}
+
+// Max / sum over the 16 lanes that share bits 4.. of the lane index (one half-warp), by the xor
+// butterfly 1, 2, 4, 8: the max is order-free and the sum's order is fixed.
+__device__ __forceinline__ float half_warp_max(float x) {
+  x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
+  x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
+  x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 4));
+  return fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 8));
+}
+
+__device__ __forceinline__ float half_warp_sum(float x) {
+  x += __shfl_xor_sync(0xffffffffu, x, 1);
+  x += __shfl_xor_sync(0xffffffffu, x, 2);
+  x += __shfl_xor_sync(0xffffffffu, x, 4);
+  return x + __shfl_xor_sync(0xffffffffu, x, 8);
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ int ld_relaxed_gpu(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Wait (one thread) until *turn == want, at most `timeout_ns` of GPU time. Returns true when the
+// turn came. On expiry it records CFA_ERR_TIMEOUT in *err and returns false; it also returns
+// false as soon as any other waiter has recorded an error, so one expired wait ends every chain
+// quickly instead of each waiter spending its own full limit.
+// ORDER: the acquire pairs with the release in pass_turn by the previous contributor: once this
+// returns true, that block's dQ stores are visible to the caller (extended to the whole block by
+// the caller's fence + barrier).
+__device__ __forceinline__ bool wait_turn_bounded(const int* turn, int want, int* err,
+                                                  uint64_t timeout_ns) {
+  if (ld_acquire_gpu(turn) == want) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t spin = 1;; ++spin) {
+    __nanosleep(64);
+    if (ld_acquire_gpu(turn) == want) return true;
+    if ((spin & 15u) == 0u) {
+      if (ld_relaxed_gpu(err) != 0) return false;
+      if (global_timer_ns() - t0 > timeout_ns) {
+        atomicCAS(err, 0, CFA_ERR_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+}  // namespace cfa

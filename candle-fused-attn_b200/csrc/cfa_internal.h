@@ -1,0 +1,108 @@
+// SPDX-License-Identifier: MIT OR Apache-2.0
+//
+// Internal launch interface between the C ABI (cfa_abi.cu) and the kernel translation units.
+// Host-only types; no torch, no candle.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "cfa.h"
+
+namespace cfa {
+
+// The forward's tile: FWD_BM queries per block, FWD_BN keys per step.
+constexpr int FWD_BM = 64;
+constexpr int FWD_BN = 64;
+constexpr int FWD_THREADS = 128;
+
+// The backward's tile: BWD_BN keys per block (one key block; fixes dQ's summation order, so it
+// depends on nothing but this constant), BWD_BM queries per step (one dQ turn counter each).
+constexpr int BWD_BN = 64;
+constexpr int BWD_BM = 64;
+constexpr int BWD_THREADS = 256;
+constexpr int PREP_THREADS = 256;
+
+// A bounded wait gives up after this much GPU time (ns) and flags CFA_ERR_TIMEOUT.
+constexpr uint64_t WAIT_TIMEOUT_NS = 2000000000ull;
+
+struct FwdArgs {
+  const float* q;
+  const float* k;
+  const float* v;
+  float* o;
+  float* lse;
+  int64_t q_sb, q_sh, q_ss;
+  int64_t k_sb, k_sh, k_ss;
+  int64_t v_sb, v_sh, v_ss;
+  int B, H, S;
+  float scale;
+  int n_qtiles;
+};
+
+struct BwdArgs {
+  const float* q;
+  const float* k;
+  const float* v;
+  const float* d_o;
+  const float* lse;
+  const float* dsum;
+  float* dqkv;
+  int* turn;
+  int* ticket;
+  int* err;
+  int64_t q_sb, q_sh, q_ss;
+  int64_t k_sb, k_sh, k_ss;
+  int64_t v_sb, v_sh, v_ss;
+  int64_t do_sb, do_sh, do_ss;
+  int B, H, S;
+  float scale;
+  int n_qtiles;  // ceil(S / BWD_BM)
+  int n_kblocks; // ceil(S / BWD_BN)
+  uint64_t timeout_ns;
+};
+
+struct PrepArgs {
+  const float* o;
+  const float* d_o;
+  float* dsum;
+  int* zero;  // ints cleared before the main backward kernel: ticket, error flag, turn counters
+  int64_t n_zero;
+  int64_t do_sb, do_sh, do_ss;
+  int B, H, S;
+};
+
+// Workspace layout of the backward (all offsets 256-byte aligned).
+struct BwdWorkspace {
+  size_t ticket_off;  // int ticket, int err (first 256 bytes)
+  size_t turn_off;    // int turn[B * H * n_qtiles]
+  size_t dsum_off;    // float D[B * H * S]
+  size_t total;
+};
+
+inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+inline BwdWorkspace bwd_workspace_layout(int64_t B, int64_t H, int64_t S) {
+  BwdWorkspace w;
+  const int64_t nqt = (S + BWD_BM - 1) / BWD_BM;
+  w.ticket_off = 0;
+  w.turn_off = 256;
+  w.dsum_off = w.turn_off + align256(static_cast<size_t>(B * H * nqt) * sizeof(int));
+  w.total = w.dsum_off + align256(static_cast<size_t>(B * H * S) * sizeof(float));
+  return w;
+}
+
+size_t fwd_smem_bytes();
+size_t bwd_smem_bytes();
+
+// Launchers (return a cudaError_t from the launch).
+cudaError_t launch_fwd(const FwdArgs& a, int causal, cudaStream_t stream);
+cudaError_t launch_bwd_prep(const PrepArgs& a, cudaStream_t stream);
+cudaError_t launch_bwd(const BwdArgs& a, int causal, cudaStream_t stream);
+
+// One-time per-device attribute set-up (dynamic shared memory limits).
+cudaError_t setup_fwd_attributes();
+cudaError_t setup_bwd_attributes();
+
+}  // namespace cfa

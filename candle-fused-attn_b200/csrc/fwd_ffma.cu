@@ -1,0 +1,191 @@
+// SPDX-License-Identifier: MIT OR Apache-2.0
+//
+// The forward: O = softmax(Q K^T * scale [+ causal mask]) V over fp32, head_dim 64, with the
+// online softmax of FlashAttention-2 (Dao 2023), saving only O and the row log-sum-exp L.
+// Replaces fattn_fwd_f32_d64 (kernels/fused_attn.cu:469-598); same inputs, outputs, layouts.
+//
+// Block: FWD_THREADS = 128 threads (4 warps) own FWD_BM = 64 queries of one (batch, head) and walk
+// key tiles of FWD_BN = 64. Warp w owns query rows 16w .. 16w + 15; within it, lane (ty, tx) =
+// (lane / 16, lane % 16) owns rows 16w + ty + 2i (i = 0..7) and
+//   - scores for keys tx + 16jj (jj = 0..3): an 8 x 4 register tile, so the row max / sum of the
+//     online softmax is a 16-lane butterfly inside one half-warp;
+//   - output dims 4tx .. 4tx + 3 of the same 8 rows: the rescale by exp(m_old - m_new) and the
+//     final 1 / l never leave the thread.
+// Each k-step of 4 reads 8 float4 of Q and 4 of K from shared memory for 128 FFMA (and the same
+// for P V), against the reference's 8 loads per 16 FFMA: the FFMA pipe, not the shared-memory
+// pipe, is the bound. Three blocks per SM (72.7 KB shared memory each, <= 168 registers).
+//
+// Loads: cp.async (16 B, L2-only) into padded tiles. V(n) travels while S(n) is computed, K(n+1)
+// while P V(n) is; Q once. Tiles past `seq` are zero-filled.
+//
+// DETERMINISM: every sum has one order fixed by the code alone: S over d = 0..63; the row max /
+// sum by the butterfly 1, 2, 4, 8; l and O over key tiles in index order, keys 0..63 within one.
+#include "cfa_common.cuh"
+
+namespace cfa {
+namespace {
+
+constexpr int FWD_SMEM_FLOATS = 3 * FWD_BM * LD + FWD_BM * LDP;
+
+template <bool CAUSAL>
+__global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs a) {
+  extern __shared__ float4 smem4[];
+  float* Qs = reinterpret_cast<float*>(smem4);  // [64][LD]
+  float* Ks = Qs + FWD_BM * LD;                 // [64][LD]
+  float* Vs = Ks + FWD_BN * LD;                 // [64][LD]
+  float* Ps = Vs + FWD_BN * LD;                 // [64][LDP], query-major; warp w uses rows 16w..
+
+  const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  const int ty = lane >> 4, tx = lane & 15;
+  const int BH = a.B * a.H;
+  int qt, bh;
+  if (CAUSAL) {
+    // Longest tiles first (tile t sees t + 1 key tiles): the last wave is the short ones.
+    qt = a.n_qtiles - 1 - static_cast<int>(blockIdx.x / BH);
+    bh = static_cast<int>(blockIdx.x % BH);
+  } else {
+    // The query tiles of one (batch, head) run side by side and share K, V through L2.
+    qt = static_cast<int>(blockIdx.x % a.n_qtiles);
+    bh = static_cast<int>(blockIdx.x / a.n_qtiles);
+  }
+  const int b = bh / a.H, h = bh % a.H;
+  const int q0 = qt * FWD_BM;
+  const int S = a.S;
+  const float* qp = a.q + b * a.q_sb + h * a.q_sh;
+  const float* kp = a.k + b * a.k_sb + h * a.k_sh;
+  const float* vp = a.v + b * a.v_sb + h * a.v_sh;
+
+  const int k_end = CAUSAL ? min(S, q0 + FWD_BM) : S;
+
+  load_tile_async<FWD_BM, FWD_THREADS>(Qs, qp, a.q_ss, q0, S);
+  load_tile_async<FWD_BN, FWD_THREADS>(Ks, kp, a.k_ss, 0, S);
+  cp_async_commit();
+
+  const int rb = 16 * w + ty;  // this thread's rows: rb + 2i
+  float m[8], l[8], acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
+  }
+
+  for (int k0 = 0; k0 < k_end; k0 += FWD_BN) {
+    // K(k0) (and the first time Q) has landed for every thread, and every thread is done with
+    // the previous tile's V and P: V(k0) may overwrite Vs.
+    cp_async_wait_all();
+    __syncthreads();
+    load_tile_async<FWD_BN, FWD_THREADS>(Vs, vp, a.v_ss, k0, S);
+    cp_async_commit();
+
+    float s[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) s[i][jj] = 0.0f;
+#pragma unroll 4
+    for (int c = 0; c < 64; c += 4) {
+      float4 kv[4];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) kv[jj] = ld4(Ks + (tx + 16 * jj) * LD + c);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 qv = ld4(Qs + (rb + 2 * i) * LD + c);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) s[i][jj] = dot4(qv, kv[jj], s[i][jj]);
+      }
+    }
+
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int qi = q0 + rb + 2 * i;
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int j = k0 + tx + 16 * jj;
+        const bool live = j < S && !(CAUSAL && j > qi);
+        s[i][jj] = live ? s[i][jj] * a.scale : -INFINITY;
+        tmax = fmaxf(tmax, s[i][jj]);
+      }
+      tmax = half_warp_max(tmax);
+      const float m_new = fmaxf(m[i], tmax);
+      // A row whose keys are all masked so far keeps m = -inf; exp(-inf - -inf) would be NaN.
+      const float alpha = m_new == -INFINITY ? 1.0f : expf(m[i] - m_new);
+      float psum = 0.0f;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const float pr = m_new == -INFINITY ? 0.0f : expf(s[i][jj] - m_new);
+        Ps[(rb + 2 * i) * LDP + tx + 16 * jj] = pr;
+        psum += pr;
+      }
+      l[i] = fmaf(l[i], alpha, half_warp_sum(psum));
+      m[i] = m_new;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[i][e] *= alpha;
+    }
+    // V(k0) has landed, every P is written, and every thread is done with Ks: K(k0 + 64) may
+    // overwrite Ks while P V runs.
+    cp_async_wait_all();
+    __syncthreads();
+    if (k0 + FWD_BN < k_end) {
+      load_tile_async<FWD_BN, FWD_THREADS>(Ks, kp, a.k_ss, k0 + FWD_BN, S);
+      cp_async_commit();
+    }
+
+#pragma unroll 2
+    for (int j = 0; j < FWD_BN; j += 4) {
+      float4 vv[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) vv[t] = ld4(Vs + (j + t) * LD + 4 * tx);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 pv = ld4(Ps + (rb + 2 * i) * LDP + j);
+        const float pr[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          acc[i][0] = fmaf(pr[t], vv[t].x, acc[i][0]);
+          acc[i][1] = fmaf(pr[t], vv[t].y, acc[i][1]);
+          acc[i][2] = fmaf(pr[t], vv[t].z, acc[i][2]);
+          acc[i][3] = fmaf(pr[t], vv[t].w, acc[i][3]);
+        }
+      }
+    }
+  }
+
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int qi = q0 + rb + 2 * i;
+    if (qi >= S) continue;
+    const float inv = 1.0f / l[i];
+    float4* dst = reinterpret_cast<float4*>(
+        a.o + ((static_cast<int64_t>(b) * S + qi) * a.H + h) * 64 + 4 * tx);
+    *dst = make_float4(acc[i][0] * inv, acc[i][1] * inv, acc[i][2] * inv, acc[i][3] * inv);
+    if (tx == 0) a.lse[static_cast<int64_t>(bh) * S + qi] = m[i] + logf(l[i]);
+  }
+}
+
+}  // namespace
+
+size_t fwd_smem_bytes() { return FWD_SMEM_FLOATS * sizeof(float); }
+
+cudaError_t setup_fwd_attributes() {
+  const int bytes = static_cast<int>(fwd_smem_bytes());
+  cudaError_t e = cudaFuncSetAttribute(fwd_ffma_kernel<false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(fwd_ffma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              bytes);
+}
+
+cudaError_t launch_fwd(const FwdArgs& a, int causal, cudaStream_t stream) {
+  const int64_t blocks = static_cast<int64_t>(a.n_qtiles) * a.B * a.H;
+  const dim3 grid(static_cast<unsigned>(blocks));
+  if (causal)
+    fwd_ffma_kernel<true><<<grid, FWD_THREADS, fwd_smem_bytes(), stream>>>(a);
+  else
+    fwd_ffma_kernel<false><<<grid, FWD_THREADS, fwd_smem_bytes(), stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace cfa

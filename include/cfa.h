@@ -1,0 +1,106 @@
+/* SPDX-License-Identifier: MIT OR Apache-2.0
+ *
+ * cfa.h -- the C ABI of the B200 (sm_100a) fused fp32 attention, head_dim 64.
+ *
+ * This is the drop-in boundary under candle-fused-attn's public API. The Rust crate's launch layer
+ * (`src/cuda.rs`) loads a PTX module and launches three kernels with fixed argument lists; these
+ * entry points replace that layer one for one, so the crate's `src/lib.rs` (alignment gate, qkv
+ * geometry, saved log-sum-exp, candle CustomOp glue) stays as it is and only swaps its two calls:
+ *
+ *   cfa_fwd_f32_d64            replaces  cuda::forward   (src/cuda.rs:140-185), which launched
+ *                                        fattn_fwd_f32_d64 (kernels/fused_attn.cu:469-475)
+ *   cfa_bwd_workspace_bytes    replaces  the three `dev.alloc` calls of cuda::backward
+ *                                        (src/cuda.rs:203-209): D, the dQ turn counters
+ *   cfa_bwd_f32_d64            replaces  cuda::backward  (src/cuda.rs:190-260), which launched
+ *                                        fattn_bwd_dot_f32_d64 (kernels/fused_attn.cu:45-48) and
+ *                                        fattn_bwd_f32_d64 (kernels/fused_attn.cu:213-221)
+ *   cfa_bwd_status             has no kernel counterpart: reads the device error flag that the
+ *                                        bounded waits of the backward set (the reference spins
+ *                                        without a bound, kernels/fused_attn.cu:161-170)
+ *   cfa_strerror               replaces  the `Error::Msg` strings of src/cuda.rs:69-93
+ *
+ * Conventions (the reference's, src/cuda.rs:60-67 and src/lib.rs:165-188):
+ *  - Every pointer is a device pointer at the operand's first element, on the current device.
+ *  - A [b, h, s, d] operand is described by its (batch, head, seq) strides in floats; d is
+ *    contiguous. Pointers and strides must be multiples of 4 floats (16-byte rows), which the
+ *    caller establishes (src/lib.rs:112, :165-168); violations return CFA_ERR_ALIGNMENT.
+ *  - Outputs are dense: O [b, s, h, 64] (merge-heads layout), L [b, h, s],
+ *    dqkv [b, s, 3, h, 64] (dQ, dK, dV interleaved: a fused qkv projection's gradient).
+ *  - Everything is asynchronous on `stream` (a cudaStream_t; NULL = the legacy default stream).
+ *    No entry point allocates memory, synchronises, or keeps state besides a once-per-device
+ *    kernel attribute set-up. Calls on different streams may run concurrently.
+ *  - Zero batch, heads or seq is a valid empty problem: CFA_OK and nothing is launched (the
+ *    reference panics there, its audit item B2).
+ *  - Results are bit-identical across reruns and independent of the GPU's SM count and of how
+ *    the batch is split over GPUs.
+ */
+#ifndef CFA_H
+#define CFA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CFA_HEAD_DIM 64 /* src/lib.rs:91 CUDA_HEAD_DIM */
+
+enum cfa_status {
+  CFA_OK = 0,
+  CFA_ERR_HEAD_DIM = 1,   /* head_dim != 64 (src/cuda.rs:85-93) */
+  CFA_ERR_ALIGNMENT = 2,  /* a pointer or stride is not a multiple of 4 floats */
+  CFA_ERR_SHAPE = 3,      /* a negative dimension */
+  CFA_ERR_OVERFLOW = 4,   /* an index or grid size past the kernels' 32/64-bit range */
+  CFA_ERR_NULL = 5,       /* a null pointer for a non-empty problem */
+  CFA_ERR_WORKSPACE = 6,  /* workspace smaller than cfa_bwd_workspace_bytes or misaligned */
+  CFA_ERR_LAUNCH = 7,     /* the CUDA launch failed */
+  CFA_ERR_TIMEOUT = 8,    /* a bounded device-side wait of the backward expired */
+  CFA_ERR_CUDA = 9        /* another CUDA runtime error (device query, copy, sync) */
+};
+
+/* Forward: O = softmax(q k^T * scale [+ causal mask]) v and L = rowwise log-sum-exp.
+ * q, k, v: [batch, heads, seq, 64] through (batch, head, seq) strides `*_strides[3]`.
+ * o: [batch, seq, heads, 64] dense.  lse: [batch, heads, seq] dense.
+ * Replaces src/cuda.rs:140-185 (launch of kernels/fused_attn.cu:469). */
+int cfa_fwd_f32_d64(const float* q, const int64_t q_strides[3],
+                    const float* k, const int64_t k_strides[3],
+                    const float* v, const int64_t v_strides[3],
+                    float* o, float* lse,
+                    int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                    float scale, int causal, void* stream);
+
+/* Bytes of device scratch the backward needs (D = rowsum(dO o O), the dQ turn counters, a work
+ * ticket and the error flag). The caller allocates it (256-byte aligned); its contents need no
+ * initialisation. Replaces the allocations at src/cuda.rs:203-209. */
+size_t cfa_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq);
+
+/* Backward from dO to one dqkv [batch, seq, 3, heads, 64] buffer (dQ, dK, dV interleaved).
+ * o, lse: the forward's outputs (dense, as cfa_fwd_f32_d64 writes them).
+ * d_o: [batch, heads, seq, 64] through `do_strides[3]`.
+ * dQ is summed over key blocks in key-block order, so reruns are bit-identical.
+ * Replaces src/cuda.rs:190-260 (launches of kernels/fused_attn.cu:45 and :213). */
+int cfa_bwd_f32_d64(const float* q, const int64_t q_strides[3],
+                    const float* k, const int64_t k_strides[3],
+                    const float* v, const int64_t v_strides[3],
+                    const float* o, const float* lse,
+                    const float* d_o, const int64_t do_strides[3],
+                    float* dqkv, void* workspace, size_t workspace_bytes,
+                    int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                    float scale, int causal, void* stream);
+
+/* Synchronises `stream` and returns CFA_ERR_TIMEOUT if a bounded wait of the last backward that
+ * used `workspace` expired (its results are then invalid), else CFA_OK (or CFA_ERR_CUDA). */
+int cfa_bwd_status(const void* workspace, void* stream);
+
+/* A static description of a status code. */
+const char* cfa_strerror(int status);
+
+/* ABI version: (major << 16) | minor. */
+int cfa_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CFA_H */

@@ -1,0 +1,100 @@
+# SPDX-License-Identifier: MIT OR Apache-2.0
+"""The C ABI on the CPU: libcfa.so loads, exports every symbol include/cfa.h declares, and rejects
+bad arguments before touching a device (so these run without a GPU)."""
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from candle_fused_attn import _abi
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "cfa.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\**\s+\**(cfa_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_abi():
+    assert declared_functions() == sorted(_abi.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _abi.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_abi.LIB_PATH)],
+                         capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r" T (cfa_\w+)", out))
+    assert set(declared_functions()) <= exported
+
+
+def test_version_and_strerror():
+    lib = _abi.load()
+    assert lib.cfa_abi_version() >> 16 == 1
+    for code in range(10):
+        msg = _abi.strerror(code)
+        assert msg.startswith("fused_attention:")
+    assert "head_dim 64" in _abi.strerror(_abi.CFA_ERR_HEAD_DIM)
+    assert "unknown" in _abi.strerror(12345)
+
+
+def test_workspace_formula():
+    # ticket/err header 256 B + turn counters + D, each 256-aligned
+    b, h, s = 64, 6, 240
+    nqt = (s + 63) // 64
+    turn = (b * h * nqt * 4 + 255) // 256 * 256
+    dsum = (b * h * s * 4 + 255) // 256 * 256
+    assert _abi.bwd_workspace_bytes(b, h, s) == 256 + turn + dsum
+    assert _abi.bwd_workspace_bytes(0, 6, 240) == 256
+
+
+FAKE = 1 << 20  # a 16-byte aligned non-null "device pointer" never dereferenced by these checks
+
+
+def fwd(ptrs=(FAKE,) * 5, strides=((64 * 240, 64, 64),) * 3, dims=(2, 3, 240, 64)):
+    q, k, v, o, lse = ptrs
+    return _abi.fwd(q, strides[0], k, strides[1], v, strides[2], o, lse, *dims, 0.125, 0, None)
+
+
+def test_rejects_head_dim():
+    assert fwd(dims=(2, 3, 240, 32)) == _abi.CFA_ERR_HEAD_DIM
+    assert fwd(dims=(2, 3, 240, 128)) == _abi.CFA_ERR_HEAD_DIM
+
+
+def test_empty_problem_is_ok_and_launches_nothing():
+    # audit B2: the reference panics on empty inputs; here they are a no-op.
+    assert fwd(ptrs=(None,) * 5, dims=(0, 3, 240, 64)) == _abi.CFA_OK
+    assert fwd(ptrs=(None,) * 5, dims=(2, 0, 240, 64)) == _abi.CFA_OK
+    assert fwd(ptrs=(None,) * 5, dims=(2, 3, 0, 64)) == _abi.CFA_OK
+
+
+def test_rejects_negative_null_misaligned_overflow():
+    assert fwd(dims=(-1, 3, 240, 64)) == _abi.CFA_ERR_SHAPE
+    assert fwd(ptrs=(FAKE, None, FAKE, FAKE, FAKE)) == _abi.CFA_ERR_NULL
+    assert fwd(ptrs=(FAKE + 4, FAKE, FAKE, FAKE, FAKE)) == _abi.CFA_ERR_ALIGNMENT
+    assert fwd(strides=((64 * 240, 64, 66),) * 3) == _abi.CFA_ERR_ALIGNMENT
+    assert fwd(dims=(1 << 20, 1 << 10, 1 << 10, 64)) == _abi.CFA_ERR_OVERFLOW
+
+
+def test_bwd_rejects_small_or_misaligned_workspace():
+    s3 = (64 * 240, 64, 64)
+    need = _abi.bwd_workspace_bytes(2, 3, 240)
+    args = dict(b=2, h=3, s=240, d=64, scale=0.125, causal=0, stream=None)
+
+    def call(ws, nbytes):
+        return _abi.bwd(FAKE, s3, FAKE, s3, FAKE, s3, FAKE, FAKE, FAKE, s3, FAKE, ws, nbytes,
+                        **args)
+
+    assert call(FAKE, need - 1) == _abi.CFA_ERR_WORKSPACE
+    assert call(FAKE + 16, need) == _abi.CFA_ERR_WORKSPACE
+    assert call(None, need) == _abi.CFA_ERR_NULL
+
+
+def test_null_status_query():
+    assert _abi.bwd_status(None, None) == _abi.CFA_ERR_NULL

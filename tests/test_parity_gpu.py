@@ -1,0 +1,197 @@
+# SPDX-License-Identifier: MIT OR Apache-2.0
+"""Parity of the sm_100a kernels with the CPU oracle, through the public API and the C ABI.
+
+Ports tests/parity.rs's CUDA tests: `cuda_matches_cpu` (:210-221, band 5e-6 max-abs, both paths,
+causal and not), `cuda_backward_is_deterministic` (:226-242, 8 reruns compared bit for bit),
+`outputs_are_merge_heads_ready` (:169-183), `backward_twice_over_one_graph` (:185-204); and adds
+the north star's band (1e-5 normwise against the fp32 composed path), odd lengths, strided views,
+misaligned inputs, and the golden fixtures made by the reference's own kernel.
+"""
+
+from pathlib import Path
+
+import pytest
+import torch
+
+import candle_fused_attn as cfa
+from candle_fused_attn import _abi
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+BAND_MAXABS = 5e-6  # tests/parity.rs:218
+BAND_NORMWISE = 1e-5  # the north star's parity bound against the CPU composed path
+
+
+def run(path, qkv, w, h, scale, causal, dev):
+    """Output [b, s, h*d] and d(sum(out * w))/d(qkv) through `path` (tests/parity.rs:78-123)."""
+    b, s, _ = qkv.shape
+    x = qkv.to(dev).requires_grad_(True)
+    if path == "fused":
+        q, k, v = oracle.qkv_views(x, h)
+        out = cfa.fused_attention(q, k, v, scale, causal).transpose(1, 2).reshape(b, s, -1)
+    else:
+        out = cfa.fused_attention_qkv(x, h, scale, causal)
+    (out * w.to(dev)).sum().backward()
+    torch.cuda.synchronize()
+    return out.detach().cpu(), x.grad.detach().cpu()
+
+
+def check(o, g, o_ref, g_ref, band=BAND_MAXABS):
+    eo, eg = (o - o_ref).abs().max().item(), (g - g_ref).abs().max().item()
+    assert eo < band and eg < band, f"max-abs O {eo:.2e} dqkv {eg:.2e}"
+    no, ng = oracle.normwise(o, o_ref), oracle.normwise(g, g_ref)
+    assert no < BAND_NORMWISE and ng < BAND_NORMWISE, f"normwise O {no:.2e} dqkv {ng:.2e}"
+
+
+@pytest.mark.parametrize("path", ["fused", "fused_qkv"])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("shape", [(2, 7, 3, 64), (2, 240, 6, 64), (1, 97, 2, 64)])
+def test_cuda_matches_cpu(cuda, shape, causal, path):
+    b, s, h, d = shape
+    qkv, w = oracle.closed_form_inputs(b, s, h, d)
+    o_ref, _, g_ref = oracle.qkv_forward_backward(qkv, w, h, 1 / d ** 0.5, causal)
+    o, g = run(path, qkv, w, h, 1 / d ** 0.5, causal, cuda)
+    check(o, g, o_ref, g_ref)
+
+
+@pytest.mark.parametrize("s", [1, 2, 31, 63, 64, 65, 127, 128, 129, 200, 257])
+@pytest.mark.parametrize("causal", [False, True])
+def test_odd_lengths(cuda, s, causal):
+    qkv, dout = oracle.seeded_inputs(2, 2, s, 7)
+    o_ref, _, g_ref = oracle.qkv_forward_backward(qkv, dout, 2, 0.125, causal)
+    o, g = run("fused_qkv", qkv, dout, 2, 0.125, causal, cuda)
+    check(o, g, o_ref, g_ref)
+
+
+def test_general_config(cuda):
+    """q, k, v [2, 4, 128, 64] contiguous N(0, 1), scale 1/8, non-causal, dO
+    N(0, 1); forward + backward against the CPU composed path and bit-identical reruns."""
+    g = torch.Generator().manual_seed(0)
+    q, k, v, do = (torch.randn(2, 4, 128, 64, generator=g) for _ in range(4))
+    o_ref, lse_ref = oracle.forward(q, k, v, 0.125, False)
+    dqkv_ref = oracle.backward(q, k, v, o_ref, lse_ref, do, 0.125, False)
+
+    def once():
+        qd, kd, vd = (t.to(cuda).requires_grad_(True) for t in (q, k, v))
+        o = cfa.fused_attention(qd, kd, vd, 0.125, False)
+        (o * do.to(cuda)).sum().backward()
+        torch.cuda.synchronize()
+        return o.detach().cpu(), qd.grad.cpu(), kd.grad.cpu(), vd.grad.cpu()
+
+    o, dq, dk, dv = once()
+    assert oracle.normwise(o, o_ref.transpose(1, 2)) < BAND_NORMWISE
+    for got, i in ((dq, 0), (dk, 1), (dv, 2)):
+        assert oracle.normwise(got, dqkv_ref[:, :, i].transpose(1, 2)) < BAND_NORMWISE
+    for _ in range(3):
+        again = once()
+        for x, y in zip(again, (o, dq, dk, dv)):
+            assert torch.equal(x.view(torch.int32), y.view(torch.int32))
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_strided_views(cuda, causal):
+    """BASELINE config 2 in small: q/k/v permuted non-contiguous views of [b, s, 3, h, 64], read
+    in place (float4-aligned strides)."""
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(2, 200, 3, 4, 64, generator=g)
+    do = torch.randn(2, 4, 200, 64, generator=g)
+    q, k, v = (x[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+    o_ref, lse_ref = oracle.forward(q, k, v, 0.125, causal)
+    dqkv_ref = oracle.backward(q, k, v, o_ref, lse_ref, do, 0.125, causal)
+    xd = x.to(cuda).requires_grad_(True)
+    qd, kd, vd = (xd[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+    assert all(cfa.float4_aligned(t) for t in (qd, kd, vd))
+    o = cfa.fused_attention(qd, kd, vd, 0.125, causal)
+    (o * do.to(cuda)).sum().backward()
+    assert oracle.normwise(o.detach().cpu(), o_ref.transpose(1, 2)) < BAND_NORMWISE
+    # x's gradient [b, s, 3, h, d] is exactly dqkv's layout
+    assert oracle.normwise(xd.grad.cpu(), dqkv_ref) < BAND_NORMWISE
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("path", ["fused", "fused_qkv"])
+def test_backward_is_deterministic(cuda, path, causal):
+    """tests/parity.rs:226-242: (4, 240, 6, 64), 8 reruns compared with to_bits()."""
+    qkv, w = oracle.closed_form_inputs(4, 240, 6, 64)
+    _, g1 = run(path, qkv, w, 6, 0.125, causal, cuda)
+    for rerun in range(8):
+        _, g2 = run(path, qkv, w, 6, 0.125, causal, cuda)
+        assert torch.equal(g1.view(torch.int32), g2.view(torch.int32)), f"rerun {rerun}"
+
+
+def test_outputs_are_merge_heads_ready(cuda):
+    """tests/parity.rs:169-183."""
+    qkv, _ = oracle.closed_form_inputs(2, 5, 3, 64)
+    x = qkv.to(cuda)
+    q, k, v = oracle.qkv_views(x, 3)
+    o = cfa.fused_attention(q, k, v, 0.3, False)
+    assert tuple(o.shape) == (2, 3, 5, 64)
+    assert o.transpose(1, 2).is_contiguous()
+    o = cfa.fused_attention_qkv(x, 3, 0.3, False)
+    assert tuple(o.shape) == (2, 5, 192) and o.is_contiguous() and o.dtype == torch.float32
+
+
+def test_backward_twice_over_one_graph(cuda):
+    """tests/parity.rs:185-204: the saved L is read, not consumed."""
+    qkv, w = oracle.closed_form_inputs(1, 9, 2, 64)
+    x = qkv.to(cuda).requires_grad_(True)
+    loss = (cfa.fused_attention_qkv(x, 2, 0.125, False) * w.to(cuda)).sum()
+    g1 = torch.autograd.grad(loss, x, retain_graph=True)[0]
+    g2 = torch.autograd.grad(loss, x)[0]
+    assert torch.equal(g1.view(torch.int32), g2.view(torch.int32))
+
+
+def test_misaligned_input_is_copied(cuda):
+    """src/lib.rs:111-118: a misaligned projection is copied to a contiguous one first."""
+    qkv, w = oracle.closed_form_inputs(2, 33, 2, 64)
+    buf = torch.zeros(qkv.numel() + 1, device=cuda)
+    buf[1:] = qkv.to(cuda).flatten()
+    x = buf[1:].view(qkv.shape)
+    assert x.storage_offset() == 1
+    o = cfa.fused_attention_qkv(x, 2, 0.125, True)
+    o_ref = cfa.fused_attention_qkv(qkv.to(cuda), 2, 0.125, True)
+    assert torch.equal(o, o_ref)
+
+
+def test_c_abi_direct(cuda):
+    """The C ABI with raw device pointers, as a Rust/C caller uses it (no autograd layer)."""
+    b, h, s = 3, 2, 150
+    qkv, dout = oracle.seeded_inputs(b, h, s, 11)
+    o_ref, lse_ref, g_ref = oracle.qkv_forward_backward(qkv, dout, h, 0.125, False)
+    x, gd = qkv.to(cuda), dout.to(cuda)
+    st = (x.stride(0), 64, x.stride(1))
+    base = x.data_ptr()
+    ptrs = (base, base + 4 * h * 64, base + 4 * 2 * h * 64)
+    o = torch.empty(b, s, h, 64, device=cuda)
+    lse = torch.empty(b, h, s, device=cuda)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert _abi.fwd(ptrs[0], st, ptrs[1], st, ptrs[2], st, o.data_ptr(), lse.data_ptr(), b, h, s,
+                    64, 0.125, 0, stream) == _abi.CFA_OK
+    nbytes = _abi.bwd_workspace_bytes(b, h, s)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=cuda)
+    dqkv = torch.empty(b, s, 3, h, 64, device=cuda)
+    assert _abi.bwd(ptrs[0], st, ptrs[1], st, ptrs[2], st, o.data_ptr(), lse.data_ptr(),
+                    gd.data_ptr(), (gd.stride(0), 64, gd.stride(1)), dqkv.data_ptr(),
+                    ws.data_ptr(), nbytes, b, h, s, 64, 0.125, 0, stream) == _abi.CFA_OK
+    assert _abi.bwd_status(ws.data_ptr(), stream) == _abi.CFA_OK
+    check(o.reshape(b, s, -1).cpu(), dqkv.reshape(b, s, -1).cpu(), o_ref, g_ref)
+    assert (lse.cpu() - lse_ref).abs().max() < BAND_MAXABS
+
+
+def _golden():
+    return sorted(GOLDEN.glob("*.pt"))
+
+
+@pytest.mark.parametrize("path", _golden(), ids=lambda p: p.stem)
+def test_matches_reference_kernel_golden(cuda, path):
+    """Against the reference's own kernel's outputs on the same inputs (tests/golden/)."""
+    fx = torch.load(path)
+    m = fx["meta"]
+    if m["inputs"] == "closed_form":
+        qkv, dout = oracle.closed_form_inputs(m["b"], m["s"], m["h"], 64)
+    else:
+        qkv, dout = oracle.seeded_inputs(m["b"], m["h"], m["s"], m["seed"])
+    o, g = run("fused_qkv", qkv, dout, m["h"], m["scale"], m["causal"], cuda)
+    check(o, g, fx["o"], fx["dqkv"])
