@@ -98,6 +98,12 @@ class Clocks:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def wait_first(self, timeout: float = 5.0) -> None:
+        """Block until nvidia-smi has produced a sample (it needs ~0.1-0.5 s to start)."""
+        t_end = time.time() + timeout
+        while self.proc is not None and not self.lines and time.time() < t_end:
+            time.sleep(0.05)
+
     def __exit__(self, *exc):
         if self.proc is not None:
             self.proc.terminate()
@@ -223,6 +229,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-ref-kernel", action="store_true")
+    ap.add_argument("--mode", choices=["full", "kernels"], default="full",
+                    help="kernels: warm-up + `steps` plain steps, no timing (for ncu)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -263,8 +271,24 @@ def main():
         step(i)
     torch.cuda.synchronize()
 
-    # device-resident throughput, K steps between barriers, max over ranks
+    if args.mode == "kernels":  # a fixed, short launch sequence for ncu
+        for i in range(args.steps):
+            step(i)
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
+    # device-resident throughput, K steps between barriers, max over ranks. The clock sampler
+    # runs through a >= 1 s loaded lead-in and the timed region (which alone can be ~10 ms).
     with Clocks(local) as clk:
+        clk.wait_first()
+        t_end, i = time.time() + 1.0, 0
+        while time.time() < t_end:
+            step(i)
+            i += 1
+            if i % 64 == 0:
+                torch.cuda.synchronize()
         ms = timed(step, args.steps, stream, sync=barrier)
     ms_t = torch.tensor([ms], device=dev)
     if dist is not None:

@@ -144,15 +144,26 @@ def test_backward_twice_over_one_graph(cuda):
 
 
 def test_misaligned_input_is_copied(cuda):
-    """src/lib.rs:111-118: a misaligned projection is copied to a contiguous one first."""
+    """src/lib.rs:111-118: a projection whose rows are not float4-aligned is copied first."""
     qkv, w = oracle.closed_form_inputs(2, 33, 2, 64)
-    buf = torch.zeros(qkv.numel() + 1, device=cuda)
-    buf[1:] = qkv.to(cuda).flatten()
-    x = buf[1:].view(qkv.shape)
-    assert x.storage_offset() == 1
+    buf = torch.zeros(2, 33, 3 * 2 * 64 + 2, device=cuda)
+    buf[..., :384] = qkv.to(cuda)
+    x = buf[..., :384]  # seq stride 386: not a multiple of 4
+    assert x.stride(1) % 4 != 0
     o = cfa.fused_attention_qkv(x, 2, 0.125, True)
     o_ref = cfa.fused_attention_qkv(qkv.to(cuda), 2, 0.125, True)
     assert torch.equal(o, o_ref)
+
+
+def test_contiguous_misaligned_offset_errors(cuda):
+    """As the reference: `contiguous()` of an already contiguous tensor is the tensor itself, so
+    a contiguous projection at an offset of 1 float reaches the op and is rejected
+    (src/lib.rs:114-118 then :533-538)."""
+    qkv, _ = oracle.closed_form_inputs(2, 33, 2, 64)
+    buf = torch.zeros(qkv.numel() + 1, device=cuda)
+    x = buf[1:].view(qkv.shape)
+    with pytest.raises(cfa.FusedAttentionError, match="16-byte aligned"):
+        cfa.fused_attention_qkv(x, 2, 0.125, True)
 
 
 def test_c_abi_direct(cuda):
