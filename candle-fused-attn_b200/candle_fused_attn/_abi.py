@@ -32,6 +32,7 @@ EXPORTS = (
     "cfa_fwd_f32_d64",
     "cfa_bwd_workspace_bytes",
     "cfa_bwd_f32_d64",
+    "cfa_bwd_f32_d64_noalloc",
     "cfa_bwd_status",
     "cfa_strerror",
     "cfa_abi_version",
@@ -119,3 +120,20 @@ def bwd(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, do_ptr, dos, dqkv_ptr, 
 
 def bwd_status(ws_ptr, stream) -> int:
     return load().cfa_bwd_status(ws_ptr, stream)
+
+
+NOALLOC_SCRATCH_BYTES = 4 << 20  # include/cfa.h CFA_NOALLOC_SCRATCH_BYTES
+
+
+def bwd_noalloc(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, do_ptr, dos, dqkv_ptr,
+                b, h, s, d, scale, causal, stream) -> int:
+    """cfa_bwd_f32_d64_noalloc: the backward with its scratch in the library's static device
+    array, for callers that cannot allocate device memory. Returns the status."""
+    fn = load().cfa_bwd_f32_d64_noalloc
+    if fn.argtypes is None:
+        fn.restype = ctypes.c_int
+        fn.argtypes = [_p, _strides, _p, _strides, _p, _strides, _p, _p, _p, _strides, _p,
+                       _i64, _i64, _i64, _i64, ctypes.c_float, ctypes.c_int, _p]
+    return fn(q_ptr, strides3(qs), k_ptr, strides3(ks), v_ptr, strides3(vs), o_ptr, lse_ptr,
+              do_ptr, strides3(dos), dqkv_ptr, b, h, s, d, ctypes.c_float(scale),
+              int(bool(causal)), stream)

@@ -1,0 +1,68 @@
+// SPDX-License-Identifier: MIT OR Apache-2.0
+//
+// cfa_bwd_f32_d64_noalloc: the backward for callers that cannot allocate device memory.
+//
+// Who needs it: code that runs where cudaMalloc is off limits -- inside a CUDA-graph-captured
+// region that must not allocate, under a framework whose allocator owns all device memory and
+// gives plugins no scratch, in a real-time or embedded loop where an allocation's latency or
+// failure is not acceptable, or behind an FFI that only passes tensors it was given. Such a caller
+// can still supply the inputs and outputs of the backward, but not the scratch that
+// cfa_bwd_f32_d64 asks for (D = rowsum(dO o O), the dQ turn counters, the work ticket and the
+// error flag). This entry point keeps that scratch in a file-scope static device array instead.
+//
+// Limits and rules:
+//  - The array holds CFA_NOALLOC_SCRATCH_BYTES (4 MiB). Every GPU that loads this library holds
+//    it until the process exits. A problem that needs more (cfa_bwd_workspace_bytes(b, h, s) >
+//    4 MiB, i.e. b*h*s above about one million rows) is rejected with CFA_ERR_WORKSPACE before
+//    anything runs; use cfa_bwd_f32_d64 with your own workspace for those.
+//  - The first call on each device looks up the array's device address (cudaGetSymbolAddress)
+//    with that device current and caches it; make that first call before any stream capture.
+//  - Every call on a device shares the one array, which keeps the last call's contents. The
+//    backward's first kernel clears the ticket, error flag and turn counters itself, and writes
+//    all of D, so no state carries over between calls. Calls whose kernels can overlap on the
+//    GPU (different streams without ordering between them) race on the array: order them.
+//  - No cudaMalloc, cudaFree or allocating library routine is called.
+//  - The bounded-wait error flag lives in the array and is not exposed; a caller that needs
+//    cfa_bwd_status must use cfa_bwd_f32_d64 with its own workspace.
+#include <mutex>
+
+#include "cfa_internal.h"
+
+namespace {
+
+// The scratch. In host code this name is a host-side stand-in, not a device address: kernels
+// get the address cfa_bwd_f32_d64_noalloc looks up with cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[CFA_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+
+struct ScratchAddress {
+  std::once_flag once;
+  void* ptr = nullptr;
+  cudaError_t err = cudaSuccess;
+};
+ScratchAddress g_addr[kMaxDevices];
+
+}  // namespace
+
+extern "C" int cfa_bwd_f32_d64_noalloc(const float* q, const int64_t q_strides[3],
+                                       const float* k, const int64_t k_strides[3],
+                                       const float* v, const int64_t v_strides[3],
+                                       const float* o, const float* lse, const float* d_o,
+                                       const int64_t do_strides[3], float* dqkv, int64_t batch,
+                                       int64_t heads, int64_t seq, int64_t head_dim, float scale,
+                                       int causal, void* stream) {
+  if (batch > 0 && heads > 0 && seq > 0 &&
+      cfa_bwd_workspace_bytes(batch, heads, seq) > CFA_NOALLOC_SCRATCH_BYTES)
+    return CFA_ERR_WORKSPACE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CFA_ERR_CUDA;
+  ScratchAddress& a = g_addr[dev];
+  std::call_once(a.once, [&a] {
+    a.err = cudaGetSymbolAddress(&a.ptr, g_noalloc_scratch);
+  });
+  if (a.err != cudaSuccess || a.ptr == nullptr) return CFA_ERR_CUDA;
+  return cfa_bwd_f32_d64(q, q_strides, k, k_strides, v, v_strides, o, lse, d_o, do_strides, dqkv,
+                         a.ptr, CFA_NOALLOC_SCRATCH_BYTES, batch, heads, seq, head_dim, scale,
+                         causal, stream);
+}

@@ -89,6 +89,31 @@ int cfa_bwd_f32_d64(const float* q, const int64_t q_strides[3],
                     int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                     float scale, int causal, void* stream);
 
+/* Size of the static scratch of cfa_bwd_f32_d64_noalloc (4 MiB per GPU that loads the library). */
+#define CFA_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* The backward without any allocation, for callers that cannot call cudaMalloc (a captured graph
+ * region that must not allocate, a host framework that owns all device memory, a real-time loop).
+ * Same arguments and results as cfa_bwd_f32_d64 minus the workspace: the scratch is a file-scope
+ * static device array of CFA_NOALLOC_SCRATCH_BYTES, held by every GPU that loads the library
+ * until exit. Has no counterpart in the reference (its launch layer always allocates,
+ * src/cuda.rs:203-209).
+ *  - Problems needing more scratch than that (cfa_bwd_workspace_bytes > 4 MiB) return
+ *    CFA_ERR_WORKSPACE before anything runs.
+ *  - The first call on a device looks up the array's device address; make it before any stream
+ *    capture.
+ *  - All calls on a device share the array (each call resets what must start at zero); calls
+ *    that can overlap on the GPU race and must be ordered by the caller.
+ *  - The device error flag is not exposed: use cfa_bwd_f32_d64 to query cfa_bwd_status. */
+int cfa_bwd_f32_d64_noalloc(const float* q, const int64_t q_strides[3],
+                            const float* k, const int64_t k_strides[3],
+                            const float* v, const int64_t v_strides[3],
+                            const float* o, const float* lse,
+                            const float* d_o, const int64_t do_strides[3],
+                            float* dqkv,
+                            int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                            float scale, int causal, void* stream);
+
 /* Synchronises `stream` and returns CFA_ERR_TIMEOUT if a bounded wait of the last backward that
  * used `workspace` expired (its results are then invalid), else CFA_OK (or CFA_ERR_CUDA). */
 int cfa_bwd_status(const void* workspace, void* stream);
