@@ -1,0 +1,114 @@
+# SPDX-License-Identifier: MIT OR Apache-2.0
+"""Measurement tooling (CPU): a numerical model of split-precision tensor-core GEMMs inside the
+attention forward + backward, against plain sequential-FFMA fp32, both scored normwise against
+fp64 on canvas-shaped slices (s = 240, d = 64, seeded N(0,1)*0.5 inputs).
+
+Schemes: bf16 x3 split with 6 or 9 products, tf32 x2 (3 products) / x3 (6 products); the MMA
+accumulation modelled as round-to-nearest or truncating, into one accumulator or separate
+high/low-order accumulators.
+
+    python baseline/split_precision_model.py
+"""
+import sys
+from pathlib import Path
+
+import torch
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+from oracle import oracle  # noqa: E402  (the seeded input generator)
+torch.manual_seed(0)
+
+def rz32(x):  # round float64 -> float32 toward zero
+    y = x.float().double()
+    over = y.abs() > x.abs()
+    y2 = torch.nextafter(y.float(), torch.zeros_like(y.float())).double()
+    return torch.where(over, y2, y)
+
+def rn32(x): return x.float().double()
+
+def split_bf16(x, n):
+    parts = []; r = x.double()
+    for _ in range(n):
+        p = r.to(torch.bfloat16).double(); parts.append(p); r = r - p
+    return parts
+
+def split_tf32(x, n):
+    parts=[]; r=x.double()
+    for _ in range(n):
+        # tf32: 10 explicit mantissa bits, RN
+        f = r.float(); i = f.view(torch.int32)
+        i = ((i + 0x1000) & ~0x1FFF)
+        p = i.view(torch.float32).double(); parts.append(p); r = r - p
+    return parts
+
+def tc_gemm(A, B, scheme, rnd, K=16, sep=True):
+    # A [m,k], B [k,n] fp32 values (as float64). returns fp32 values (float64 container)
+    kind, n = scheme
+    sp = split_bf16 if kind == 'bf16' else split_tf32
+    As, Bs = sp(A, n), sp(B, n)
+    if kind == 'bf16' and n == 3: pairs = [(0,0),(0,1),(1,0),(0,2),(1,1),(2,0)]
+    elif kind == 'bf16' and n == 2: pairs = [(0,0),(0,1),(1,0)]
+    elif kind == 'tf32' and n == 2: pairs = [(0,0),(0,1),(1,0)]
+    elif kind == 'bf16' and n == 9: pairs = [(i,j) for i in range(3) for j in range(3)]; As, Bs = sp(A,3), sp(B,3)
+    elif kind == 'tf32' and n == 3: pairs = [(0,0),(0,1),(1,0),(0,2),(1,1),(2,0)]
+    m, kk = A.shape; nn = B.shape[1]
+    big = torch.zeros(m, nn, dtype=torch.float64); small = torch.zeros(m, nn, dtype=torch.float64)
+    for c in range(0, kk, K):
+        for (i, j) in pairs:
+            part = As[i][:, c:c+K] @ Bs[j][c:c+K, :]   # exact-ish in fp64
+            if sep and (i, j) != (0, 0): small = rnd(small + part)
+            else: big = rnd(big + part)
+    return rnd(big + small) if sep else big
+
+def ffma_gemm(A, B):  # sequential fp32 fma over k: emulate with float64 product + rn32 each step
+    m, kk = A.shape; nn = B.shape[1]; acc = torch.zeros(m, nn, dtype=torch.float64)
+    for c in range(kk):
+        acc = rn32(acc + A[:, c:c+1] * B[c:c+1, :])
+    return acc
+
+def attention(q, k, v, do, scale, gemm):
+    # composed math with fp32 elementwise, GEMMs by `gemm`. all [s,d] float64 holding fp32 values
+    S = rn32(gemm(q, k.T) * scale)
+    m = S.max(dim=1, keepdim=True).values
+    P = rn32(torch.exp(rn32(S - m)).float().double())
+    l = rn32(P.sum(1, keepdim=True))
+    P = rn32(P / l)
+    O = gemm(P, v)
+    L = rn32(m + torch.log(l))
+    # backward (recompute P from L)
+    P2 = rn32(torch.exp(rn32(rn32(gemm(q, k.T) * scale) - L)))
+    dV = gemm(P2.T.contiguous(), do)
+    dP = gemm(do, v.T.contiguous())
+    D = rn32((do * O).sum(1, keepdim=True))
+    dS = rn32(P2 * rn32(dP - D))
+    dQ = rn32(gemm(dS, k) * scale)
+    dK = rn32(gemm(dS.T.contiguous(), q) * scale)
+    return O, dQ, dK, dV
+
+qkv, dout = oracle.seeded_inputs(2, 2, 240, 0, 0.5)
+q4, k4, v4 = oracle.qkv_views(qkv, 2); g4 = oracle.heads_view(dout, 2)
+res = {}
+for bh in range(4):
+    b, h = divmod(bh, 2)
+    q, k, v, do = (t[b, h].double() for t in (q4, k4, v4, g4))
+    ref = attention(q, k, v, do, 0.125, lambda A, B: A @ B)   # fp64 reference (rn32 elementwise though)
+    # true fp64 everything:
+    def f64(A,B): return A@B
+    import math
+    S = (q@k.T)*0.125; m=S.max(1,keepdim=True).values; P=torch.exp(S-m); l=P.sum(1,keepdim=True); P=P/l; O=P@v; L=m+torch.log(l)
+    dV=P.T@do; dP=do@v.T; D=(do*O).sum(1,keepdim=True); dS=P*(dP-D); dQ=dS@k*0.125; dK=dS.T@q*0.125
+    truth=(O,dQ,dK,dV)
+    for name, gemm in [('ffma', ffma_gemm),
+                       ('bf16x3(6) RN sep', lambda A,B: tc_gemm(A,B,('bf16',3),rn32)),
+                       ('bf16x3(6) RZ sep', lambda A,B: tc_gemm(A,B,('bf16',3),rz32)),
+                       ('bf16x3(6) RZ onеacc', lambda A,B: tc_gemm(A,B,('bf16',3),rz32,sep=False)),
+                       ('bf16x9 RZ sep', lambda A,B: tc_gemm(A,B,('bf16',9),rz32)),
+                       ('tf32x2(3) RN sep', lambda A,B: tc_gemm(A,B,('tf32',2),rn32,K=8)),
+                       ('tf32x3(6) RZ sep', lambda A,B: tc_gemm(A,B,('tf32',3),rz32,K=8)),
+                       ]:
+        out = attention(q, k, v, do, 0.125, gemm)
+        acc = res.setdefault(name, [[0,0] for _ in range(4)])
+        for i in range(4):
+            acc[i][0] += float(((out[i]-truth[i])**2).sum()); acc[i][1] += float((truth[i]**2).sum())
+for name, acc in res.items():
+    print(f"{name:22s} " + " ".join(f"{p}={ (a/b)**0.5:.2e}" for p,(a,b) in zip("O dQ dK dV".split(), acc)))
