@@ -4,8 +4,8 @@
 // log-sum-exp L, written into ONE [b, s, 3, h, 64] buffer (a fused qkv projection's gradient).
 // Replaces fattn_bwd_dot_f32_d64 and fattn_bwd_f32_d64 (kernels/fused_attn.cu:45-63, :213-426).
 //
-// Step 1 (prep kernel): D[b, h, i] = sum_d dO[i, d] O[i, d], 16 lanes per row, one float4 each,
-// then the 16-lane butterfly; the same kernel clears the work ticket, the error flag and the dQ
+// Step 1 (prep kernel): D[b, h, i] = sum_d dO[i, d] O[i, d] in fp64, 16 lanes per row, one float4
+// each, then the 16-lane butterfly, rounded once to fp32; the same kernel clears the work ticket, the error flag and the dQ
 // turn counters that step 2 uses (the stream orders it before step 2).
 //
 // Step 2 (main kernel): one block per key block of BWD_BN = 64 keys of one (batch, head); K and
@@ -43,18 +43,24 @@ __global__ void __launch_bounds__(PREP_THREADS) bwd_prep_kernel(const PrepArgs a
   const int64_t rows = static_cast<int64_t>(a.B) * a.H * a.S;
   const int64_t row = gtid >> 4;  // row = (b * H + h) * S + i
   const int c = threadIdx.x & 15;
-  float x = 0.0f;
+  double x = 0.0;
   if (row < rows) {
     const int i = static_cast<int>(row % a.S);
     const int64_t bhr = row / a.S;
     const int h = static_cast<int>(bhr % a.H), b = static_cast<int>(bhr / a.H);
     const float4 ov = ld4(a.o + ((static_cast<int64_t>(b) * a.S + i) * a.H + h) * 64 + 4 * c);
     const float4 gv = ld4(a.d_o + b * a.do_sb + h * a.do_sh + i * a.do_ss + 4 * c);
-    x = dot4(ov, gv, 0.0f);
+    // In fp64 (the kernel is bound by HBM, not arithmetic): D feeds the cancellation dP - D of
+    // every dS, so its error matters more than one product's. Products of two floats are exact
+    // in fp64.
+    x = __fma_rn(static_cast<double>(ov.w), gv.w,
+            __fma_rn(static_cast<double>(ov.z), gv.z,
+                __fma_rn(static_cast<double>(ov.y), gv.y, static_cast<double>(ov.x) * gv.x)));
   }
   // DETERMINISM: four products per lane in d order, then the butterfly 1, 2, 4, 8.
-  x = half_warp_sum(x);
-  if (row < rows && c == 0) a.dsum[row] = x;
+#pragma unroll
+  for (int off = 1; off < 16; off <<= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+  if (row < rows && c == 0) a.dsum[row] = static_cast<float>(x);
 }
 
 template <bool CAUSAL>
@@ -93,7 +99,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
 
   load_tile_async<64, BWD_THREADS>(Ks, a.k + b * a.k_sb + h * a.k_sh, a.k_ss, k0, S);
   load_tile_async<64, BWD_THREADS>(Vs, a.v + b * a.v_sb + h * a.v_sh, a.v_ss, k0, S);
-  cp_async_commit();
 
   float acc[8][4];  // grp 0: dV, grp 1: dK (unscaled); [a][e]: key 16wg + 8ty + a, dim 4tx + e
 #pragma unroll
@@ -105,26 +110,31 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
   const int kb2 = 16 * wg + 8 * ty;   // phase 2 keys: kb2 .. kb2 + 7
   const int rb3 = 8 * w + ty;         // phase 3 rows: rb3 + 2i
 
-  // Causal: queries before the block's first key never see it.
-  const int t_begin = CAUSAL ? k0 / BWD_BM : 0;
-  for (int t = t_begin; t < a.n_qtiles; ++t) {
-    const int q0 = t * BWD_BM;
-    // Every thread is done with the previous tile's Q, dO, P, dS.
-    __syncthreads();
+  // Q, dO, L, D of query tile q0 into the (single) tile buffers, one cp.async group.
+  auto load_query_tile = [&](int q0) {
     load_tile_async<64, BWD_THREADS>(Qs, qp, a.q_ss, q0, S);
     load_tile_async<64, BWD_THREADS>(dOs, gp, a.do_ss, q0, S);
-    cp_async_commit();
-    if (tid < 64) {
-      const int i = q0 + tid;
-      Lt[tid] = i < S ? lp[i] : 0.0f;
-    } else if (tid < 128) {
-      const int i = q0 + tid - 64;
-      Dt[tid - 64] = i < S ? dp[i] : 0.0f;
+    if (tid < 128) {
+      const int r = tid & 63, i = q0 + r;
+      const bool ok = i < S;
+      const float* src = (tid < 64 ? lp : dp) + (ok ? i : q0);
+      cp_async4((tid < 64 ? Lt : Dt) + r, src, ok ? 4 : 0);
     }
+  };
+
+  // Causal: queries before the block's first key never see it.
+  const int t_begin = CAUSAL ? k0 / BWD_BM : 0;
+  load_query_tile(t_begin * BWD_BM);
+  cp_async_commit();
+  for (int t = t_begin; t < a.n_qtiles; ++t) {
+    const int q0 = t * BWD_BM;
+    // This tile (and the first time K, V) has landed, and every thread is done with the previous
+    // tile (its dS reads of phase 3 included).
     cp_async_wait_all();
     __syncthreads();
 
-    // Phase 1. grp 0: s = Q K^T; grp 1: s = dO V^T (dP).
+    // Phase 1. grp 0: s = Q K^T; grp 1: s = dO V^T (dP). Rows in two halves of 4, so each
+    // accumulator's dependent FMAs are 16 apart; every element sums d = 0..63 in order.
     {
       const float* As = grp ? dOs : Qs;
       const float* Bs = grp ? Vs : Ks;
@@ -139,13 +149,22 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) bv[jj] = ld4(Bs + (tx + 16 * jj) * LD + c);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 av = ld4(As + (rb1 + 2 * i) * LD + c);
+        for (int hh = 0; hh < 2; ++hh) {
+          float4 av[4];
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) s[i][jj] = dot4(av, bv[jj], s[i][jj]);
+          for (int i = 0; i < 4; ++i) av[i] = ld4(As + (rb1 + 2 * (4 * hh + i)) * LD + c);
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+              for (int jj = 0; jj < 4; ++jj)
+                s[4 * hh + i][jj] = fmaf(f4c(av[i], cc), f4c(bv[jj], cc), s[4 * hh + i][jj]);
         }
       }
       if (grp == 0) {
+        const bool edge = (q0 + BWD_BM > S) || (k0 + BWD_BN > S) ||
+                          (CAUSAL && k0 + BWD_BN - 1 > q0);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int il = rb1 + 2 * i, qi = q0 + il;
@@ -153,8 +172,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
             const int jl = tx + 16 * jj, j = k0 + jl;
-            const bool live = qi < S && j < S && !(CAUSAL && j > qi);
-            Ps[il * LDP + jl] = live ? expf(fmaf(s[i][jj], a.scale, -li)) : 0.0f;
+            // P = e^(s * scale - L): the argument in natural units with one rounding.
+            float pr = expf(fmaf(s[i][jj], a.scale, -li));
+            if (edge && !(qi < S && j < S && !(CAUSAL && j > qi))) pr = 0.0f;
+            Ps[il * LDP + jl] = pr;
           }
         }
       }
@@ -194,6 +215,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
         }
       }
     }
+    // Every thread is done with Q, dO, L, D of this tile: the next tile's copies travel during
+    // phase 3 and the ordered dQ add.
+    __syncthreads();
+    if (t + 1 < a.n_qtiles) {
+      load_query_tile(q0 + BWD_BM);
+      cp_async_commit();
+    }
 
     // Phase 3: the dQ partial pq[r][e] = sum_j dS[rb3 + 2r][j] K[j][4tx + e], keys in order.
     float pq[4][4];
@@ -203,21 +231,21 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
       for (int e = 0; e < 4; ++e) pq[r][e] = 0.0f;
 #pragma unroll 2
     for (int j = 0; j < BWD_BN; j += 4) {
-      float4 k4[4];
+      float4 k4[4], d4[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) k4[u] = ld4(Ks + (j + u) * LD + 4 * tx);
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const float4 d4 = ld4(dSs + (rb3 + 2 * r) * LDP + j);
-        const float ds[4] = {d4.x, d4.y, d4.z, d4.w};
+      for (int r = 0; r < 4; ++r) d4[r] = ld4(dSs + (rb3 + 2 * r) * LDP + j);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          pq[r][0] = fmaf(ds[u], k4[u].x, pq[r][0]);
-          pq[r][1] = fmaf(ds[u], k4[u].y, pq[r][1]);
-          pq[r][2] = fmaf(ds[u], k4[u].z, pq[r][2]);
-          pq[r][3] = fmaf(ds[u], k4[u].w, pq[r][3]);
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const float ds = f4c(d4[r], u);
+          pq[r][0] = fmaf(ds, k4[u].x, pq[r][0]);
+          pq[r][1] = fmaf(ds, k4[u].y, pq[r][1]);
+          pq[r][2] = fmaf(ds, k4[u].z, pq[r][2]);
+          pq[r][3] = fmaf(ds, k4[u].w, pq[r][3]);
         }
-      }
     }
 
     // This tile's contributors are key blocks 0 .. last (causal: those holding a key <= the

@@ -39,6 +39,14 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src
                : "memory");
 }
 
+// 4-byte asynchronous copy (L1-allocating), zero-filled when src_bytes == 0.
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, int src_bytes) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem),
+               "r"(src_bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;\n" ::: "memory");
 }
@@ -77,6 +85,30 @@ __device__ __forceinline__ float half_warp_sum(float x) {
   x += __shfl_xor_sync(0xffffffffu, x, 2);
   x += __shfl_xor_sync(0xffffffffu, x, 4);
   return x + __shfl_xor_sync(0xffffffffu, x, 8);
+}
+
+// log2(e) split into a float head and tail (head + tail = log2(e) to 4e-16).
+constexpr float LOG2E_HI = 1.4426950216293335f;
+constexpr float LOG2E_LO = 1.925963033500011e-08f;
+
+// 2^x by the SFU (ex2.approx.ftz.f32: max relative error about 2^-22 per the PTX ISA;
+// 2^-inf = +0).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// e^d for an argument d <= 0 already formed in natural units: d * log2(e) is taken with the
+// split constant (the product's own rounding only, no systematic error from rounding log2(e)),
+// then one SFU exp2. -inf gives +0. (Kept for comparison; the kernels use CUDA's expf, whose
+// smaller error keeps the outputs at or below the reference kernel's error against fp64.)
+__device__ __forceinline__ float exp_nat(float d) {
+  return ex2(fmaf(d, LOG2E_HI, d * LOG2E_LO));
+}
+
+__device__ __forceinline__ float f4c(const float4& v, int c) {
+  return c == 0 ? v.x : (c == 1 ? v.y : (c == 2 ? v.z : v.w));
 }
 
 __device__ __forceinline__ uint64_t global_timer_ns() {

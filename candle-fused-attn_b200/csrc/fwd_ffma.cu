@@ -62,11 +62,15 @@ __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs 
   cp_async_commit();
 
   const int rb = 16 * w + ty;  // this thread's rows: rb + 2i
-  float m[8], l[8], acc[8][4];
+  // x = (q.k) * scale (exact for a power-of-two scale, as in the composed path), p = e^(x - m)
+  // with CUDA's expf. lpart is this thread's share
+  // of the row sum (its 4 keys per tile, rescaled like O); the 16 shares of a row are added once,
+  // after the last tile.
+  float m[8], lpart[8], acc[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     m[i] = -INFINITY;
-    l[i] = 0.0f;
+    lpart[i] = 0.0f;
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
   }
@@ -79,47 +83,60 @@ __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs 
     load_tile_async<FWD_BN, FWD_THREADS>(Vs, vp, a.v_ss, k0, S);
     cp_async_commit();
 
+    // S = Q K^T: per 4-wide slice of d, the x components of all 32 products, then y, z, w, so
+    // dependent FMAs on one accumulator are 32 instructions apart (each element still sums
+    // d = 0..63 in order).
     float s[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) s[i][jj] = 0.0f;
-#pragma unroll 4
+#pragma unroll 2
     for (int c = 0; c < 64; c += 4) {
-      float4 kv[4];
+      float4 kv[4], qv[8];
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) kv[jj] = ld4(Ks + (tx + 16 * jj) * LD + c);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 qv = ld4(Qs + (rb + 2 * i) * LD + c);
+      for (int i = 0; i < 8; ++i) qv[i] = ld4(Qs + (rb + 2 * i) * LD + c);
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) s[i][jj] = dot4(qv, kv[jj], s[i][jj]);
-      }
+      for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj)
+            s[i][jj] = fmaf(f4c(qv[i], cc), f4c(kv[jj], cc), s[i][jj]);
     }
 
+    // Masks only where the tile crosses the sequence end or the causal diagonal (block-uniform).
+    const bool edge = (k0 + FWD_BN > S) || (CAUSAL && k0 + FWD_BN - 1 > q0);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const int qi = q0 + rb + 2 * i;
-      float tmax = -INFINITY;
+      float x[4];
 #pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const int j = k0 + tx + 16 * jj;
-        const bool live = j < S && !(CAUSAL && j > qi);
-        s[i][jj] = live ? s[i][jj] * a.scale : -INFINITY;
-        tmax = fmaxf(tmax, s[i][jj]);
+      for (int jj = 0; jj < 4; ++jj) x[jj] = s[i][jj] * a.scale;
+      if (edge) {
+        const int qi = q0 + rb + 2 * i;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int j = k0 + tx + 16 * jj;
+          if (!(j < S && !(CAUSAL && j > qi))) x[jj] = -INFINITY;
+        }
       }
+      float tmax = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
       tmax = half_warp_max(tmax);
       const float m_new = fmaxf(m[i], tmax);
-      // A row whose keys are all masked so far keeps m = -inf; exp(-inf - -inf) would be NaN.
-      const float alpha = m_new == -INFINITY ? 1.0f : expf(m[i] - m_new);
+      // Every row has a live key in its first tile, so m_new is finite; the guard keeps a fully
+      // masked row at p = 0 instead of NaN all the same.
+      const float mu = m_new == -INFINITY ? 0.0f : m_new;
+      const float alpha = expf(m[i] - mu);
       float psum = 0.0f;
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) {
-        const float pr = m_new == -INFINITY ? 0.0f : expf(s[i][jj] - m_new);
+        const float pr = expf(x[jj] - mu);
         Ps[(rb + 2 * i) * LDP + tx + 16 * jj] = pr;
         psum += pr;
       }
-      l[i] = fmaf(l[i], alpha, half_warp_sum(psum));
+      lpart[i] = fmaf(lpart[i], alpha, psum);
       m[i] = m_new;
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[i][e] *= alpha;
@@ -133,35 +150,39 @@ __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs 
       cp_async_commit();
     }
 
+    // O += P V, keys j = k0 .. k0 + 63 in order for every element.
 #pragma unroll 2
     for (int j = 0; j < FWD_BN; j += 4) {
-      float4 vv[4];
+      float4 vv[4], pv[8];
 #pragma unroll
       for (int t = 0; t < 4; ++t) vv[t] = ld4(Vs + (j + t) * LD + 4 * tx);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 pv = ld4(Ps + (rb + 2 * i) * LDP + j);
-        const float pr[4] = {pv.x, pv.y, pv.z, pv.w};
+      for (int i = 0; i < 8; ++i) pv[i] = ld4(Ps + (rb + 2 * i) * LDP + j);
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          acc[i][0] = fmaf(pr[t], vv[t].x, acc[i][0]);
-          acc[i][1] = fmaf(pr[t], vv[t].y, acc[i][1]);
-          acc[i][2] = fmaf(pr[t], vv[t].z, acc[i][2]);
-          acc[i][3] = fmaf(pr[t], vv[t].w, acc[i][3]);
+      for (int t = 0; t < 4; ++t)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float pr = f4c(pv[i], t);
+          acc[i][0] = fmaf(pr, vv[t].x, acc[i][0]);
+          acc[i][1] = fmaf(pr, vv[t].y, acc[i][1]);
+          acc[i][2] = fmaf(pr, vv[t].z, acc[i][2]);
+          acc[i][3] = fmaf(pr, vv[t].w, acc[i][3]);
         }
-      }
     }
   }
 
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
+    // DETERMINISM: the row sum is the butterfly of the 16 per-thread shares, in a fixed order.
+    const float l = half_warp_sum(lpart[i]);
     const int qi = q0 + rb + 2 * i;
     if (qi >= S) continue;
-    const float inv = 1.0f / l[i];
     float4* dst = reinterpret_cast<float4*>(
         a.o + ((static_cast<int64_t>(b) * S + qi) * a.H + h) * 64 + 4 * tx);
-    *dst = make_float4(acc[i][0] * inv, acc[i][1] * inv, acc[i][2] * inv, acc[i][3] * inv);
-    if (tx == 0) a.lse[static_cast<int64_t>(bh) * S + qi] = m[i] + logf(l[i]);
+    // O = acc / l with one rounding (IEEE division), once per output element.
+    *dst = make_float4(__fdiv_rn(acc[i][0], l), __fdiv_rn(acc[i][1], l), __fdiv_rn(acc[i][2], l),
+                       __fdiv_rn(acc[i][3], l));
+    if (tx == 0) a.lse[static_cast<int64_t>(bh) * S + qi] = m[i] + logf(l);
   }
 }
 
