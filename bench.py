@@ -143,7 +143,7 @@ class OursStep:
         self.o = torch.empty(b, S, H, D, device=dev)
         self.lse = torch.empty(b, H, S, device=dev)
         self.dqkv = torch.empty(b, S, 3, H, D, device=dev)
-        self.ws_bytes = _abi.bwd_workspace_bytes(b, H, S)
+        self.ws_bytes = _abi.bwd_workspace_bytes_fast(b, H, S)
         self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
         base = qkv.data_ptr()
         self.ptr = (base, base + 4 * H * D, base + 4 * 2 * H * D)

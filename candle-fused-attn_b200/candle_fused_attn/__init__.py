@@ -154,7 +154,9 @@ def attention_backward(q_ptr, qs, k_ptr, ks, v_ptr, vs, o, lse, do_ptr, dos, dim
     if not (o.is_contiguous() and lse.is_contiguous()):
         raise FusedAttentionError("fused_attention: O and L must be contiguous")
     dqkv = torch.empty((b, s, 3, h, d), dtype=torch.float32, device=device)
-    ws_bytes = _abi.bwd_workspace_bytes(b, h, s)
+    # The larger workspace enables the no-wait dQ path (same bits); torch's caching allocator
+    # recycles it across steps.
+    ws_bytes = _abi.bwd_workspace_bytes_fast(b, h, s)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
     with torch.cuda.device(device):
         stream = _stream(device)

@@ -31,6 +31,7 @@ CFA_ERR_CUDA = 9
 EXPORTS = (
     "cfa_fwd_f32_d64",
     "cfa_bwd_workspace_bytes",
+    "cfa_bwd_workspace_bytes_fast",
     "cfa_bwd_f32_d64",
     "cfa_bwd_f32_d64_noalloc",
     "cfa_bwd_status",
@@ -70,6 +71,8 @@ def load() -> ctypes.CDLL:
         _i64, _i64, _i64, _i64, ctypes.c_float, ctypes.c_int, _p]
     lib.cfa_bwd_workspace_bytes.restype = ctypes.c_size_t
     lib.cfa_bwd_workspace_bytes.argtypes = [_i64, _i64, _i64]
+    lib.cfa_bwd_workspace_bytes_fast.restype = ctypes.c_size_t
+    lib.cfa_bwd_workspace_bytes_fast.argtypes = [_i64, _i64, _i64]
     lib.cfa_bwd_f32_d64.restype = ctypes.c_int
     lib.cfa_bwd_f32_d64.argtypes = [
         _p, _strides, _p, _strides, _p, _strides, _p, _p, _p, _strides, _p, _p, ctypes.c_size_t,
@@ -107,6 +110,10 @@ def fwd(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, b, h, s, d, scale, caus
 
 def bwd_workspace_bytes(b, h, s) -> int:
     return int(load().cfa_bwd_workspace_bytes(b, h, s))
+
+
+def bwd_workspace_bytes_fast(b, h, s) -> int:
+    return int(load().cfa_bwd_workspace_bytes_fast(b, h, s))
 
 
 def bwd(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, do_ptr, dos, dqkv_ptr, ws_ptr, ws_bytes,

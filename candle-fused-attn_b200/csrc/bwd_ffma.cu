@@ -248,8 +248,20 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
         }
     }
 
-    // This tile's contributors are key blocks 0 .. last (causal: those holding a key <= the
-    // tile's last query); each adds on its turn.
+    if (a.dq_part != nullptr) {
+      // No-wait path: this key block's partial for the tile goes to its own scratch rows.
+      float* part = a.dq_part + (static_cast<int64_t>(bh) * a.n_kblocks + kb) * S * 64;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int qi = q0 + rb3 + 2 * r;
+        if (qi < S)
+          __stcg(reinterpret_cast<float4*>(part + static_cast<int64_t>(qi) * 64 + 4 * tx),
+                 make_float4(pq[r][0], pq[r][1], pq[r][2], pq[r][3]));
+      }
+      continue;
+    }
+    // Turn chain. This tile's contributors are key blocks 0 .. last (causal: those holding a key
+    // <= the tile's last query); each adds on its turn.
     const int last = CAUSAL ? min(a.n_kblocks - 1, min(S - 1, q0 + BWD_BM - 1) / BWD_BN)
                             : a.n_kblocks - 1;
     bool go = true;
@@ -285,6 +297,36 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
       __threadfence();
       __syncthreads();
       if (tid == 0) st_release_gpu(turn + t, kb + 1);
+    }
+  }
+
+  if (a.dq_part != nullptr) {
+    // ORDER: this block's partials are visible GPU-wide before it counts itself in; the block
+    // that counts last then reads every partial of its (batch, head).
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_int[1] = atomicAdd(a.turn + bh, 1);
+    __syncthreads();
+    if (s_int[1] == a.n_kblocks - 1) {
+      __threadfence();
+      const float* part = a.dq_part + static_cast<int64_t>(bh) * a.n_kblocks * S * 64;
+      // DETERMINISM: dQ = (((p0 + p1) + p2) + ...) * scale over the contributing key blocks in
+      // index order: the turn chain's sums, bit for bit, whichever block does them.
+      for (int idx = tid; idx < S * 16; idx += BWD_THREADS) {
+        const int i = idx >> 4, c4 = idx & 15;
+        const int t = i / BWD_BM;
+        const int last = CAUSAL ? min(a.n_kblocks - 1, min(S - 1, t * BWD_BM + BWD_BM - 1) / BWD_BN)
+                                : a.n_kblocks - 1;
+        const float* src = part + static_cast<int64_t>(i) * 64 + 4 * c4;
+        float4 v = __ldcg(reinterpret_cast<const float4*>(src));
+        for (int j = 1; j <= last; ++j) {
+          const float4 p =
+              __ldcg(reinterpret_cast<const float4*>(src + static_cast<int64_t>(j) * S * 64));
+          v = make_float4(v.x + p.x, v.y + p.y, v.z + p.z, v.w + p.w);
+        }
+        v = make_float4(v.x * a.scale, v.y * a.scale, v.z * a.scale, v.w * a.scale);
+        *reinterpret_cast<float4*>(dq_base + i * row_stride + 4 * c4) = v;
+      }
     }
   }
 

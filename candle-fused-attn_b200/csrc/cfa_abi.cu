@@ -122,6 +122,11 @@ size_t cfa_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq) {
   return cfa::bwd_workspace_layout(batch, heads, seq).total;
 }
 
+size_t cfa_bwd_workspace_bytes_fast(int64_t batch, int64_t heads, int64_t seq) {
+  if (batch <= 0 || heads <= 0 || seq <= 0) return 256;
+  return cfa::bwd_workspace_layout(batch, heads, seq).total_fast;
+}
+
 int cfa_bwd_f32_d64(const float* q, const int64_t q_strides[3], const float* k,
                     const int64_t k_strides[3], const float* v, const int64_t v_strides[3],
                     const float* o, const float* lse, const float* d_o,
@@ -201,6 +206,10 @@ int cfa_bwd_f32_d64(const float* q, const int64_t q_strides[3], const float* k,
   a.n_qtiles = nqt;
   a.n_kblocks = nkb;
   a.timeout_ns = cfa::WAIT_TIMEOUT_NS;
+  // The no-wait dQ path when the workspace holds the partials (same results, bit for bit).
+  a.dq_part = (lay.total_fast > lay.total && workspace_bytes >= lay.total_fast)
+                  ? reinterpret_cast<float*>(ws + lay.part_off)
+                  : nullptr;
   e = cfa::launch_bwd(a, causal != 0, s);
   return e == cudaSuccess ? CFA_OK : CFA_ERR_LAUNCH;
 }

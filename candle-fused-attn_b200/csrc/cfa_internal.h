@@ -24,6 +24,11 @@ constexpr int BWD_BM = 64;
 constexpr int BWD_THREADS = 256;
 constexpr int PREP_THREADS = 256;
 
+// Sequences of at most PART_MAX_KBLOCKS key blocks can take the backward's no-wait dQ path: each
+// key block stores its dQ partials to scratch and the last block of a (batch, head) to finish
+// sums them in key-block order (the same sums, bit for bit, as the turn chain).
+constexpr int PART_MAX_KBLOCKS = 8;
+
 // A bounded wait gives up after this much GPU time (ns) and flags CFA_ERR_TIMEOUT.
 constexpr uint64_t WAIT_TIMEOUT_NS = 2000000000ull;
 
@@ -49,9 +54,10 @@ struct BwdArgs {
   const float* lse;
   const float* dsum;
   float* dqkv;
-  int* turn;
+  int* turn;      // turn chain: [B * H * n_qtiles]; no-wait path: arrival counter per (b, h)
   int* ticket;
   int* err;
+  float* dq_part; // no-wait path: [B * H][n_kblocks][S][64] dQ partials; nullptr: turn chain
   int64_t q_sb, q_sh, q_ss;
   int64_t k_sb, k_sh, k_ss;
   int64_t v_sb, v_sh, v_ss;
@@ -78,7 +84,9 @@ struct BwdWorkspace {
   size_t ticket_off;  // int ticket, int err (first 256 bytes)
   size_t turn_off;    // int turn[B * H * n_qtiles]
   size_t dsum_off;    // float D[B * H * S]
-  size_t total;
+  size_t total;       // bytes of the turn-chain layout
+  size_t part_off;    // float partials[B * H * n_kblocks * S * 64] (no-wait dQ path)
+  size_t total_fast;  // bytes with the partials (== total when the path does not apply)
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -90,6 +98,11 @@ inline BwdWorkspace bwd_workspace_layout(int64_t B, int64_t H, int64_t S) {
   w.turn_off = 256;
   w.dsum_off = w.turn_off + align256(static_cast<size_t>(B * H * nqt) * sizeof(int));
   w.total = w.dsum_off + align256(static_cast<size_t>(B * H * S) * sizeof(float));
+  const int64_t nkb = (S + BWD_BN - 1) / BWD_BN;
+  w.part_off = w.total;
+  w.total_fast = nkb <= PART_MAX_KBLOCKS
+                     ? w.total + static_cast<size_t>(nkb * B * H * S) * 64 * sizeof(float)
+                     : w.total;
   return w;
 }
 

@@ -52,6 +52,10 @@ def test_workspace_formula():
     dsum = (b * h * s * 4 + 255) // 256 * 256
     assert _abi.bwd_workspace_bytes(b, h, s) == 256 + turn + dsum
     assert _abi.bwd_workspace_bytes(0, 6, 240) == 256
+    # the no-wait dQ path adds one partial per key block (s <= 512 only)
+    nkb = (s + 63) // 64
+    assert _abi.bwd_workspace_bytes_fast(b, h, s) == 256 + turn + dsum + nkb * b * h * s * 64 * 4
+    assert _abi.bwd_workspace_bytes_fast(4, 16, 8192) == _abi.bwd_workspace_bytes(4, 16, 8192)
 
 
 FAKE = 1 << 20  # a 16-byte aligned non-null "device pointer" never dereferenced by these checks

@@ -191,6 +191,35 @@ def test_c_abi_direct(cuda):
     assert (lse.cpu() - lse_ref).abs().max() < BAND_MAXABS
 
 
+@pytest.mark.parametrize("b,h,s,causal", [(64, 6, 240, False), (3, 2, 200, True),
+                                          (2, 2, 512, True), (2, 3, 65, False)])
+def test_no_wait_dq_path_equals_turn_chain(cuda, b, h, s, causal):
+    """The two dQ orderings (the key-block turn chain with the minimal workspace, the
+    store-then-last-block-sums path with cfa_bwd_workspace_bytes_fast) give the same bits."""
+    qkv, dout = oracle.seeded_inputs(b, h, s, 4)
+    x, g = qkv.to(cuda), dout.to(cuda)
+    st, gst = (x.stride(0), 64, x.stride(1)), (g.stride(0), 64, g.stride(1))
+    base = x.data_ptr()
+    ptrs = (base, base + 4 * h * 64, base + 8 * h * 64)
+    o = torch.empty(b, s, h, 64, device=cuda)
+    lse = torch.empty(b, h, s, device=cuda)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert _abi.fwd(ptrs[0], st, ptrs[1], st, ptrs[2], st, o.data_ptr(), lse.data_ptr(), b, h, s,
+                    64, 0.125, causal, stream) == _abi.CFA_OK
+    out = []
+    for nbytes in (_abi.bwd_workspace_bytes(b, h, s), _abi.bwd_workspace_bytes_fast(b, h, s)):
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=cuda)
+        dqkv = torch.full((b, s, 3, h, 64), float("nan"), device=cuda)
+        assert _abi.bwd(ptrs[0], st, ptrs[1], st, ptrs[2], st, o.data_ptr(), lse.data_ptr(),
+                        g.data_ptr(), gst, dqkv.data_ptr(), ws.data_ptr(), nbytes, b, h, s, 64,
+                        0.125, causal, stream) == _abi.CFA_OK
+        assert _abi.bwd_status(ws.data_ptr(), stream) == _abi.CFA_OK
+        out.append(dqkv)
+    assert _abi.bwd_workspace_bytes_fast(b, h, s) > _abi.bwd_workspace_bytes(b, h, s)
+    assert torch.isfinite(out[0]).all()
+    assert torch.equal(out[0].view(torch.int32), out[1].view(torch.int32))
+
+
 def _golden():
     return sorted(GOLDEN.glob("*.pt"))
 
