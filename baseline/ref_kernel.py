@@ -80,3 +80,37 @@ class RefQkv:
                             self.scale, self.causal, self.st, self.st, self.st, gs, s)
         if rc != 0:
             raise RuntimeError(f"ref_bwd failed ({rc})")
+
+
+class RefAttention:
+    """The reference kernels on [b, h, s, 64] views q, k, v (any float4-aligned strides) and dO
+    (same shape), buffers allocated once."""
+
+    def __init__(self, q, k, v, scale: float, causal: bool):
+        b, h, s, _ = q.shape
+        self.b, self.h, self.s = b, h, s
+        self.q, self.k, self.v = q, k, v
+        self.scale, self.causal = float(scale), int(bool(causal))
+        self.qs, self.ks, self.vs = (_s3(t.stride()[:3]) for t in (q, k, v))
+        dev = q.device
+        self.o = torch.empty(b, s, h, 64, device=dev)
+        self.lse = torch.empty(b, h, s, device=dev)
+        self.dqkv = torch.empty(b, s, 3, h, 64, device=dev)
+        self.ws = torch.empty(load().ref_bwd_workspace_bytes(b, h, s), dtype=torch.uint8,
+                              device=dev)
+
+    def forward(self, stream):
+        rc = load().ref_fwd(self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(),
+                            self.o.data_ptr(), self.lse.data_ptr(), self.b, self.h, self.s,
+                            self.scale, self.causal, self.qs, self.ks, self.vs, stream)
+        if rc != 0:
+            raise RuntimeError(f"ref_fwd failed ({rc})")
+
+    def backward(self, d_o, stream):
+        rc = load().ref_bwd(self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(),
+                            self.o.data_ptr(), self.lse.data_ptr(), d_o.data_ptr(),
+                            self.dqkv.data_ptr(), self.ws.data_ptr(), self.b, self.h, self.s,
+                            self.scale, self.causal, self.qs, self.ks, self.vs,
+                            _s3(d_o.stride()[:3]), stream)
+        if rc != 0:
+            raise RuntimeError(f"ref_bwd failed ({rc})")

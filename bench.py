@@ -13,9 +13,10 @@ One JSON line on rank 0:
   value      whole-job TFLOP/s (algorithmic 14 b h s^2 d per step) with inputs resident in HBM,
              over K steps timed with CUDA events between barriers; inputs rotate over 3 sets
              (> L2) so no step starts from a warm L2;
-  e2e        the same metric through the public API (fused_attention_qkv + autograd backward)
-             with host buffers: pinned qkv, dO copied in and O, dqkv copied out inside the timed
-             region;
+  e2e        the same metric through the public host-buffer API (HostPipeline: pinned qkv, dO
+             copied in and O, dqkv copied out inside the timed region, batch chunks overlapping
+             both copy directions with the kernels); the plain fused_attention_qkv + autograd
+             path with unoverlapped copies is reported beside it;
   roofline   the backward kernel (the dominant one): achieved = 10 b h s^2 d / its event-timed
              duration, against the FFMA peak (148 SMs x 128 FMA/clk x 2 x the measured max SM
              clock of MEASURED_PEAKS.json);
@@ -166,6 +167,114 @@ class OursStep:
             raise RuntimeError(self.abi.strerror(rc))
 
 
+class OursViews:
+    """Forward + backward through the C ABI on [b, h, s, 64] views q, k, v and dO."""
+
+    def __init__(self, q, k, v, d_o, causal):
+        from candle_fused_attn import _abi
+        self.abi = _abi
+        b, h, s, _ = q.shape
+        self.dims = (b, h, s, 64)
+        self.q, self.k, self.v, self.d_o, self.causal = q, k, v, d_o, causal
+        dev = q.device
+        self.o = torch.empty(b, s, h, 64, device=dev)
+        self.lse = torch.empty(b, h, s, device=dev)
+        self.dqkv = torch.empty(b, s, 3, h, 64, device=dev)
+        self.ws_bytes = _abi.bwd_workspace_bytes_fast(b, h, s)
+        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
+
+    def forward(self, stream):
+        st = [t.stride()[:3] for t in (self.q, self.k, self.v)]
+        rc = self.abi.fwd(self.q.data_ptr(), st[0], self.k.data_ptr(), st[1], self.v.data_ptr(),
+                          st[2], self.o.data_ptr(), self.lse.data_ptr(), *self.dims, SCALE,
+                          self.causal, stream)
+        if rc:
+            raise RuntimeError(self.abi.strerror(rc))
+
+    def backward(self, d_o, stream):
+        st = [t.stride()[:3] for t in (self.q, self.k, self.v)]
+        rc = self.abi.bwd(self.q.data_ptr(), st[0], self.k.data_ptr(), st[1], self.v.data_ptr(),
+                          st[2], self.o.data_ptr(), self.lse.data_ptr(), d_o.data_ptr(),
+                          d_o.stride()[:3], self.dqkv.data_ptr(), self.ws.data_ptr(),
+                          self.ws_bytes, *self.dims, SCALE, self.causal, stream)
+        if rc:
+            raise RuntimeError(self.abi.strerror(rc))
+
+
+def suite(args):
+    """Every BASELINE.json config on one GPU: ours and the reference's own kernels, forward and
+    forward + backward, alternating rounds; one JSON line per config."""
+    from baseline import ref_kernel
+    from oracle import oracle
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+    pk = peaks()
+
+    def views_qkv(b, h, s, causal, seed, qscale):
+        qkv, dout = oracle.seeded_inputs(b, h, s, seed, qscale)
+        x, g = qkv.to(dev), dout.to(dev)
+        q, k, v = oracle.qkv_views(x, h)
+        return q, k, v, oracle.heads_view(g, h)
+
+    def views_general(b, h, s, causal, seed, _):
+        gen = torch.Generator().manual_seed(seed)
+        q, k, v, d_o = (torch.randn(b, h, s, 64, generator=gen).to(dev) for _ in range(4))
+        return q, k, v, d_o
+
+    def views_strided(b, h, s, causal, seed, _):
+        gen = torch.Generator().manual_seed(seed)
+        x = torch.randn(b, s, 3, h, 64, generator=gen).to(dev)
+        d_o = torch.randn(b, h, s, 64, generator=gen).to(dev)
+        q, k, v = (x[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+        return q, k, v, d_o
+
+    configs = [
+        ("general [2,4,128,64] contiguous", 2, 4, 128, False, views_general, 1.0),
+        ("canvas qkv [64,240,1152]", 64, 6, 240, False, views_qkv, 0.5),
+        ("strided views of [16,1024,3,12,64], causal", 16, 12, 1024, True, views_strided, 1.0),
+        ("long qkv [4,8192,3072], causal", 4, 16, 8192, True, views_qkv, 0.5),
+    ]
+    for name, b, h, s, causal, make, qscale in configs:
+        q, k, v, d_o = make(b, h, s, causal, 0, qscale)
+        impls = {"ours": OursViews(q, k, v, d_o, causal),
+                 "reference_kernel": ref_kernel.RefAttention(q, k, v, SCALE, causal)
+                 if ref_kernel.available() else None}
+        f_fwd, f_all = flops(b, h, s, 64, causal, "fwd"), flops(b, h, s, 64, causal)
+        steps = max(3, min(args.steps, int(2e11 // f_all) + 1))
+        res = {}
+        for _ in range(args.warmup):
+            for im in impls.values():
+                if im is not None:
+                    im.forward(sh)
+                    im.backward(d_o, sh)
+        rounds = {n: {"fwd": [], "fwdbwd": []} for n in impls}
+        for _ in range(3):
+            for n, im in impls.items():
+                if im is None:
+                    continue
+                rounds[n]["fwd"].append(timed(lambda i: im.forward(sh), steps, stream))
+                rounds[n]["fwdbwd"].append(
+                    timed(lambda i: (im.forward(sh), im.backward(d_o, sh)), steps, stream))
+        for n, r in rounds.items():
+            if not r["fwd"]:
+                res[n] = None
+                continue
+            fm, am = statistics.median(r["fwd"]), statistics.median(r["fwdbwd"])
+            res[n] = {"fwd_ms": fm, "fwdbwd_ms": am,
+                      "fwd_tflops": f_fwd / fm / 1e9, "fwdbwd_tflops": f_all / am / 1e9,
+                      "fwdbwd_frac_ffma": f_all / am / 1e9 / pk["ffma_tflops"]}
+        line = {"suite": name, "b": b, "h": h, "s": s, "causal": causal, "steps": steps,
+                "gflop_fwd": f_fwd / 1e9, "gflop_fwdbwd": f_all / 1e9, **res}
+        if res.get("reference_kernel"):
+            line["speedup_fwdbwd"] = res["reference_kernel"]["fwdbwd_ms"] / res["ours"]["fwdbwd_ms"]
+            line["speedup_fwd"] = res["reference_kernel"]["fwd_ms"] / res["ours"]["fwd_ms"]
+        print(json.dumps(line), flush=True)
+        del impls, q, k, v, d_o
+        torch.cuda.empty_cache()
+
+
 def timed(fn, steps, stream, sync=None):
     """ms per call of fn(i) over `steps` calls, CUDA events on `stream`."""
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -229,8 +338,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-ref-kernel", action="store_true")
-    ap.add_argument("--mode", choices=["full", "kernels"], default="full",
-                    help="kernels: warm-up + `steps` plain steps, no timing (for ncu)")
+    ap.add_argument("--mode", choices=["full", "kernels", "suite"], default="full",
+                    help="kernels: warm-up + `steps` plain steps, no timing (for ncu); "
+                         "suite: every BASELINE config, ours vs the reference kernel")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -239,6 +349,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference_arm(args, rank, world)
+    if args.mode == "suite":
+        return suite(args)
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -301,14 +413,39 @@ def main():
     fwd_ms = timed(lambda i: sets[i % N_SETS].fwd(sh), args.steps, stream)
     bwd_ms = timed(lambda i: sets[i % N_SETS].bwd(sh), args.steps, stream)
 
-    # e2e through the public API with pinned host buffers
+    # e2e through the public API with pinned host buffers: HostPipeline streams batch chunks
+    # through H2D / kernels / D2H on three streams (the timed region spans every copy).
     import candle_fused_attn as cfa
+    from candle_fused_attn.host_pipeline import HostPipeline
     hq = [s.qkv.cpu().pin_memory() for s in sets]
     hg = [s.dout.cpu().pin_memory() for s in sets]
     ho = torch.empty(b, S, H * D).pin_memory()
     hd = torch.empty(b, S, 3 * H * D).pin_memory()
+    pipe = HostPipeline(b, H, S, SCALE, CAUSAL, dev, chunks=4, slots=2)
 
-    def e2e_step(i):
+    def e2e_timed(steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        e0.record(pipe.h2d)
+        for i in range(steps):
+            pipe.step(hq[i % N_SETS], hg[i % N_SETS], ho, hd)
+        pipe.record_done(e1)
+        e1.synchronize()
+        barrier()
+        return e0.elapsed_time(e1) / steps
+
+    for i in range(args.warmup):
+        pipe.step(hq[i % N_SETS], hg[i % N_SETS], ho, hd)
+    pipe.synchronize()
+    e2e_ms = e2e_timed(args.steps)
+    e2e_t = torch.tensor([e2e_ms], device=dev)
+    if dist is not None:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_t.item())
+
+    # the same through fused_attention_qkv + autograd, one whole-batch call, copies not overlapped
+    def autograd_step(i):
         x = hq[i % N_SETS].to(dev, non_blocking=True).requires_grad_(True)
         g = hg[i % N_SETS].to(dev, non_blocking=True)
         o = cfa.fused_attention_qkv(x, H, SCALE, CAUSAL)
@@ -317,12 +454,8 @@ def main():
         hd.copy_(x.grad, non_blocking=True)
 
     for i in range(args.warmup):
-        e2e_step(i)
-    e2e_ms = timed(e2e_step, args.steps, stream, sync=barrier)
-    e2e_t = torch.tensor([e2e_ms], device=dev)
-    if dist is not None:
-        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
-    e2e_ms = float(e2e_t.item())
+        autograd_step(i)
+    autograd_ms = timed(autograd_step, args.steps, stream, sync=barrier)
 
     # the reference's own kernels on the same GPU, alternating rounds with ours
     ref = None
@@ -375,7 +508,11 @@ def main():
                 "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": (sets[0].qkv.numel() + sets[0].dout.numel()) * 4,
                 "d2h_bytes_per_step": (ho.numel() + hd.numel()) * 4,
-                "path": "fused_attention_qkv + autograd backward, pinned host buffers"},
+                "path": "candle_fused_attn.HostPipeline (pinned host qkv, dO in; O, dqkv out; "
+                        "4 batch chunks, 2 buffer slots over H2D / kernel / D2H streams)",
+                "autograd_ms_per_step": autograd_ms,
+                "autograd_path": "fused_attention_qkv + autograd backward, whole batch, copies "
+                                 "not overlapped"},
         "roofline": {"bound": "compute", "pipe": "fp32 FFMA (CUDA cores)",
                      "kernel": "backward (prep + main, one cfa_bwd_f32_d64 call)",
                      "achieved": achieved, "peak": pk["ffma_tflops"], "unit": "TFLOP/s",

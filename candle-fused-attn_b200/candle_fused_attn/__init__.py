@@ -38,6 +38,7 @@ __all__ = [
     "qkv_geometry",
     "attention_forward",
     "attention_backward",
+    "HostPipeline",
 ]
 
 CUDA_HEAD_DIM = 64  # src/lib.rs:91
@@ -251,3 +252,6 @@ def fused_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
     [batch, heads, seq, 64] (a transposed view of a dense [batch, seq, heads, 64] buffer)."""
     q, k, v = _float4_rows(q), _float4_rows(k), _float4_rows(v)
     return _FusedAttention.apply(q, k, v, float(scale), bool(causal)).transpose(1, 2)
+
+
+from .host_pipeline import HostPipeline  # noqa: E402  (uses _abi; public host-buffer API)
