@@ -35,6 +35,7 @@ EXPORTS = (
     "cfa_bwd_f32_d64",
     "cfa_bwd_f32_d64_noalloc",
     "cfa_bwd_status",
+    "cfa_selftest_bounded_wait",
     "cfa_strerror",
     "cfa_abi_version",
 )
@@ -79,6 +80,8 @@ def load() -> ctypes.CDLL:
         _i64, _i64, _i64, _i64, ctypes.c_float, ctypes.c_int, _p]
     lib.cfa_bwd_status.restype = ctypes.c_int
     lib.cfa_bwd_status.argtypes = [_p, _p]
+    lib.cfa_selftest_bounded_wait.restype = ctypes.c_int
+    lib.cfa_selftest_bounded_wait.argtypes = [_p, _i64, ctypes.c_int, _p]
     lib.cfa_strerror.restype = ctypes.c_char_p
     lib.cfa_strerror.argtypes = [ctypes.c_int]
     lib.cfa_abi_version.restype = ctypes.c_int
@@ -127,6 +130,10 @@ def bwd(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, do_ptr, dos, dqkv_ptr, 
 
 def bwd_status(ws_ptr, stream) -> int:
     return load().cfa_bwd_status(ws_ptr, stream)
+
+
+def selftest_bounded_wait(ws_ptr, timeout_ns, blocks, stream) -> int:
+    return load().cfa_selftest_bounded_wait(ws_ptr, int(timeout_ns), int(blocks), stream)
 
 
 NOALLOC_SCRATCH_BYTES = 4 << 20  # include/cfa.h CFA_NOALLOC_SCRATCH_BYTES

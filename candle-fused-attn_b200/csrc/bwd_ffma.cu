@@ -133,34 +133,41 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
     cp_async_wait_all();
     __syncthreads();
 
-    // Phase 1. grp 0: s = Q K^T; grp 1: s = dO V^T (dP). Rows in two halves of 4, so each
-    // accumulator's dependent FMAs are 16 apart; every element sums d = 0..63 in order.
+    // Phase 1. grp 0: s = Q K^T; grp 1: s = dO V^T (dP). Packed FMAs: every element is the sum
+    // of an even-d and an odd-d chain (each in increasing d), the same order as the forward's
+    // scores, so P = exp(S * scale - L) recomputed here matches the forward's normalisation.
+    // Rows in two halves of 4 (32 packed accumulators live at a time).
     {
       const float* As = grp ? dOs : Qs;
       const float* Bs = grp ? Vs : Ks;
       float s[8][4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int hh = 0; hh < 2; ++hh) {
+        uint64_t s2[4][4];
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) s[i][jj] = 0.0f;
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) s2[i][jj] = 0ull;
 #pragma unroll 2
-      for (int c = 0; c < 64; c += 4) {
-        float4 bv[4];
+        for (int c = 0; c < 64; c += 4) {
+          ulonglong2 bv[4], av[4];
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) bv[jj] = ld4(Bs + (tx + 16 * jj) * LD + c);
+          for (int jj = 0; jj < 4; ++jj) bv[jj] = ld2x2(Bs + (tx + 16 * jj) * LD + c);
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          float4 av[4];
+          for (int i = 0; i < 4; ++i) av[i] = ld2x2(As + (rb1 + 2 * (4 * hh + i)) * LD + c);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) av[i] = ld4(As + (rb1 + 2 * (4 * hh + i)) * LD + c);
+          for (int i = 0; i < 4; ++i)
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc)
+            for (int jj = 0; jj < 4; ++jj) s2[i][jj] = fma2(av[i].x, bv[jj].x, s2[i][jj]);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+          for (int i = 0; i < 4; ++i)
 #pragma unroll
-              for (int jj = 0; jj < 4; ++jj)
-                s[4 * hh + i][jj] = fmaf(f4c(av[i], cc), f4c(bv[jj], cc), s[4 * hh + i][jj]);
+            for (int jj = 0; jj < 4; ++jj) s2[i][jj] = fma2(av[i].y, bv[jj].y, s2[i][jj]);
         }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) s[4 * hh + i][jj] = sum2(s2[i][jj]);
       }
       if (grp == 0) {
         const bool edge = (q0 + BWD_BM > S) || (k0 + BWD_BN > S) ||
@@ -371,6 +378,31 @@ cudaError_t launch_bwd(const BwdArgs& a, int causal, cudaStream_t stream) {
     bwd_ffma_kernel<true><<<grid, BWD_THREADS, bwd_smem_bytes(), stream>>>(a);
   else
     bwd_ffma_kernel<false><<<grid, BWD_THREADS, bwd_smem_bytes(), stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace cfa
+
+namespace cfa {
+namespace {
+
+// Self-test of the backward's failure detection: every block's thread 0 waits, with the same
+// bounded routine the dQ turn chain uses, for a flag that nothing ever sets. Block 0 gives up after
+// `short_ns`; the others would wait 100x longer but bail out as soon as block 0 has flagged the
+// error. The kernel always ends: with CFA_ERR_TIMEOUT in ws[1] after about `short_ns`.
+__global__ void selftest_wait_kernel(int* ws, uint64_t short_ns) {
+  if (threadIdx.x != 0) return;
+  const int* never = ws + 2;  // cleared by the host-side memset; nothing writes it afterwards
+  const uint64_t limit = blockIdx.x == 0 ? short_ns : 100 * short_ns;
+  wait_turn_bounded(never, 1, ws + 1, limit);
+}
+
+}  // namespace
+
+cudaError_t launch_selftest_wait(int* ws, uint64_t short_ns, int blocks, cudaStream_t stream) {
+  cudaError_t e = cudaMemsetAsync(ws, 0, 16, stream);
+  if (e != cudaSuccess) return e;
+  selftest_wait_kernel<<<blocks, 32, 0, stream>>>(ws, short_ns);
   return cudaGetLastError();
 }
 

@@ -214,6 +214,17 @@ int cfa_bwd_f32_d64(const float* q, const int64_t q_strides[3], const float* k,
   return e == cudaSuccess ? CFA_OK : CFA_ERR_LAUNCH;
 }
 
+int cfa_selftest_bounded_wait(void* workspace, int64_t timeout_ns, int blocks, void* stream) {
+  if (!workspace) return CFA_ERR_NULL;
+  if (timeout_ns <= 0 || timeout_ns > 10000000000ll || blocks < 1 || blocks > 1024)
+    return CFA_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return CFA_ERR_WORKSPACE;
+  const cudaError_t e = cfa::launch_selftest_wait(static_cast<int*>(workspace),
+                                                  static_cast<uint64_t>(timeout_ns), blocks,
+                                                  static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CFA_OK : CFA_ERR_LAUNCH;
+}
+
 int cfa_bwd_status(const void* workspace, void* stream) {
   if (!workspace) return CFA_ERR_NULL;
   int flags[2] = {0, 0};

@@ -111,6 +111,25 @@ __device__ __forceinline__ float f4c(const float4& v, int c) {
   return c == 0 ? v.x : (c == 1 ? v.y : (c == 2 ? v.z : v.w));
 }
 
+// Packed fp32 pairs (sm_100 fma.rn.f32x2: two single-rounding FMAs per lane per instruction).
+// A float4 loaded from shared memory as ulonglong2 holds the pairs (x, y) and (z, w).
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__device__ __forceinline__ ulonglong2 ld2x2(const float* p) {
+  return *reinterpret_cast<const ulonglong2*>(p);
+}
+
+// The sum of a pair's two halves: lo + hi.
+__device__ __forceinline__ float sum2(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return lo + hi;
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

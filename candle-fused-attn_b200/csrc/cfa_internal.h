@@ -114,6 +114,9 @@ cudaError_t launch_fwd(const FwdArgs& a, int causal, cudaStream_t stream);
 cudaError_t launch_bwd_prep(const PrepArgs& a, cudaStream_t stream);
 cudaError_t launch_bwd(const BwdArgs& a, int causal, cudaStream_t stream);
 
+// The failure-detection self-test (cfa_selftest_bounded_wait).
+cudaError_t launch_selftest_wait(int* ws, uint64_t short_ns, int blocks, cudaStream_t stream);
+
 // One-time per-device attribute set-up (dynamic shared memory limits).
 cudaError_t setup_fwd_attributes();
 cudaError_t setup_bwd_attributes();

@@ -125,6 +125,13 @@ int cfa_bwd_f32_d64_noalloc(const float* q, const int64_t q_strides[3],
  * used `workspace` expired (its results are then invalid), else CFA_OK (or CFA_ERR_CUDA). */
 int cfa_bwd_status(const void* workspace, void* stream);
 
+/* Self-test of the failure detection (no counterpart in the reference, whose spin has no bound):
+ * launches `blocks` blocks whose waits -- the bounded routine of the backward's dQ chain -- can
+ * never be satisfied. Block 0 gives up after `timeout_ns`, the others bail out as soon as it has
+ * flagged the error, so the kernel ends after about `timeout_ns`, leaving CFA_ERR_TIMEOUT in the
+ * 256-byte, 256-aligned `workspace` for cfa_bwd_status to read. No GPU fault, no hang. */
+int cfa_selftest_bounded_wait(void* workspace, int64_t timeout_ns, int blocks, void* stream);
+
 /* A static description of a status code. */
 const char* cfa_strerror(int status);
 
