@@ -63,6 +63,44 @@ __global__ void __launch_bounds__(PREP_THREADS) bwd_prep_kernel(const PrepArgs a
   if (row < rows && c == 0) a.dsum[row] = static_cast<float>(x);
 }
 
+// Phase 1 products for this thread's 8 rows (rb1 + 2i) and the first JN of its 4 key groups
+// (keys tx + 16jj): s = A B^T over d as an even-d chain plus an odd-d chain (packed FMAs), the
+// same order as the forward's scores. Rows in two halves of 4 (32 packed accumulators live).
+// Key groups jj >= JN lie wholly past the sequence end: left at 0 (masked or multiplied by P = 0).
+template <int JN>
+__device__ __forceinline__ void phase1_tile(const float* As, const float* Bs, int rb1, int tx,
+                                            float (&s)[8][4]) {
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    uint64_t s2[4][JN];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int jj = 0; jj < JN; ++jj) s2[i][jj] = 0ull;
+#pragma unroll 2
+    for (int c = 0; c < 64; c += 4) {
+      ulonglong2 bv[JN], av[4];
+#pragma unroll
+      for (int jj = 0; jj < JN; ++jj) bv[jj] = ld2x2(Bs + (tx + 16 * jj) * LD + c);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) av[i] = ld2x2(As + (rb1 + 2 * (4 * hh + i)) * LD + c);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int jj = 0; jj < JN; ++jj) s2[i][jj] = fma2(av[i].x, bv[jj].x, s2[i][jj]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int jj = 0; jj < JN; ++jj) s2[i][jj] = fma2(av[i].y, bv[jj].y, s2[i][jj]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj)
+        s[4 * hh + i][jj] = jj < JN ? sum2(s2[i][jj < JN ? jj : 0]) : 0.0f;
+  }
+}
+
 template <bool CAUSAL>
 __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs a) {
   extern __shared__ float4 smem4[];
@@ -133,42 +171,26 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
     cp_async_wait_all();
     __syncthreads();
 
-    // Phase 1. grp 0: s = Q K^T; grp 1: s = dO V^T (dP). Packed FMAs: every element is the sum
-    // of an even-d and an odd-d chain (each in increasing d), the same order as the forward's
-    // scores, so P = exp(S * scale - L) recomputed here matches the forward's normalisation.
-    // Rows in two halves of 4 (32 packed accumulators live at a time).
+    // Dead work on edge tiles is skipped, uniformly per tile: key groups wholly past the sequence
+    // end (jn) and query rows past it in the phase-2 sums (iq). The skipped terms are masked
+    // scores and products with P = 0 or dS = 0: the live results are the same bits either way.
+    // (Skipping whole dead warps measured slower: the branches cost registers.)
+    const int jn = min(4, (S - k0 + 15) / 16);
+    const int iq = min(BWD_BM, (S - q0 + 15) / 16 * 16);
+
+    // Phase 1. grp 0: s = Q K^T; grp 1: s = dO V^T (dP), as even/odd packed chains.
     {
       const float* As = grp ? dOs : Qs;
       const float* Bs = grp ? Vs : Ks;
       float s[8][4];
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint64_t s2[4][4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) s2[i][jj] = 0ull;
-#pragma unroll 2
-        for (int c = 0; c < 64; c += 4) {
-          ulonglong2 bv[4], av[4];
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) bv[jj] = ld2x2(Bs + (tx + 16 * jj) * LD + c);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) av[i] = ld2x2(As + (rb1 + 2 * (4 * hh + i)) * LD + c);
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) s2[i][jj] = fma2(av[i].x, bv[jj].x, s2[i][jj]);
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) s2[i][jj] = fma2(av[i].y, bv[jj].y, s2[i][jj]);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) s[4 * hh + i][jj] = sum2(s2[i][jj]);
-      }
+      if (jn == 4)
+        phase1_tile<4>(As, Bs, rb1, tx, s);
+      else if (jn == 3)
+        phase1_tile<3>(As, Bs, rb1, tx, s);
+      else if (jn == 2)
+        phase1_tile<2>(As, Bs, rb1, tx, s);
+      else
+        phase1_tile<1>(As, Bs, rb1, tx, s);
       if (grp == 0) {
         const bool edge = (q0 + BWD_BM > S) || (k0 + BWD_BN > S) ||
                           (CAUSAL && k0 + BWD_BN - 1 > q0);
@@ -209,7 +231,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
       const float* Xs = grp ? dSs : Ps;
       const float* Ys = grp ? Qs : dOs;
 #pragma unroll 4
-      for (int i = 0; i < BWD_BM; ++i) {
+      for (int i = 0; i < iq; ++i) {
         const float4 xa = ld4(Xs + i * LDP + kb2), xb = ld4(Xs + i * LDP + kb2 + 4);
         const float4 y = ld4(Ys + i * LD + 4 * tx);
         const float xs[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
@@ -236,8 +258,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
     for (int r = 0; r < 4; ++r)
 #pragma unroll
       for (int e = 0; e < 4; ++e) pq[r][e] = 0.0f;
+    const int jlim = 16 * jn;
 #pragma unroll 2
-    for (int j = 0; j < BWD_BN; j += 4) {
+    for (int j = 0; j < jlim; j += 4) {
       float4 k4[4], d4[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) k4[u] = ld4(Ks + (j + u) * LD + 4 * tx);

@@ -27,6 +27,40 @@ namespace {
 
 constexpr int FWD_SMEM_FLOATS = 3 * FWD_BM * LD + FWD_BM * LDP;
 
+// S = Q K^T for this thread's 8 rows (rb + 2i) and the first JN of its 4 key groups (keys
+// tx + 16jj), with packed FMAs: each score is an even-d chain plus an odd-d chain (a float4 of Q
+// and one of K give the pairs (d, d + 1), (d + 2, d + 3) directly), each in increasing d, added at
+// the end. Key groups jj >= JN lie wholly past the sequence end: left at 0 (masked later).
+template <int JN>
+__device__ __forceinline__ void score_tile(const float* Qs, const float* Ks, int rb, int tx,
+                                           float (&s)[8][4]) {
+  uint64_t s2[8][JN];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int jj = 0; jj < JN; ++jj) s2[i][jj] = 0ull;
+#pragma unroll 2
+  for (int c = 0; c < 64; c += 4) {
+    ulonglong2 kv[JN], qv[8];
+#pragma unroll
+    for (int jj = 0; jj < JN; ++jj) kv[jj] = ld2x2(Ks + (tx + 16 * jj) * LD + c);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qv[i] = ld2x2(Qs + (rb + 2 * i) * LD + c);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int jj = 0; jj < JN; ++jj) s2[i][jj] = fma2(qv[i].x, kv[jj].x, s2[i][jj]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int jj = 0; jj < JN; ++jj) s2[i][jj] = fma2(qv[i].y, kv[jj].y, s2[i][jj]);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) s[i][jj] = jj < JN ? sum2(s2[i][jj < JN ? jj : 0]) : 0.0f;
+}
+
 template <bool CAUSAL>
 __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs a) {
   extern __shared__ float4 smem4[];
@@ -83,38 +117,17 @@ __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs 
     load_tile_async<FWD_BN, FWD_THREADS>(Vs, vp, a.v_ss, k0, S);
     cp_async_commit();
 
-    // S = Q K^T with packed FMAs: each score is two chains, the even and the odd d (a float4 of
-    // Q and one of K give the pairs (d, d + 1) and (d + 2, d + 3) directly), added at the end:
-    // s = sum_{d even} q k + sum_{d odd} q k, each chain in increasing d. Half the FMA
-    // instructions of scalar FFMA, same pipe throughput.
+    // Dead work is skipped, uniformly per tile: the key groups wholly past the sequence end of
+    // a 33..48-key last tile. The skipped terms are masked scores and products with P = 0: the
+    // live results are the same bits either way. (Two instantiations only, for code size and
+    // registers; shorter last tiles compute their dead groups and mask them. Skipping whole dead
+    // warps measured slower: the branch costs registers.)
+    const int jn = min(4, (S - k0 + 15) / 16);
     float s[8][4];
-    {
-      uint64_t s2[8][4];
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) s2[i][jj] = 0ull;
-#pragma unroll 2
-      for (int c = 0; c < 64; c += 4) {
-        ulonglong2 kv[4], qv[8];
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) kv[jj] = ld2x2(Ks + (tx + 16 * jj) * LD + c);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) qv[i] = ld2x2(Qs + (rb + 2 * i) * LD + c);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) s2[i][jj] = fma2(qv[i].x, kv[jj].x, s2[i][jj]);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) s2[i][jj] = fma2(qv[i].y, kv[jj].y, s2[i][jj]);
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) s[i][jj] = sum2(s2[i][jj]);
-    }
+    if (jn == 3)
+      score_tile<3>(Qs, Ks, rb, tx, s);
+    else
+      score_tile<4>(Qs, Ks, rb, tx, s);
 
     // Masks only where the tile crosses the sequence end or the causal diagonal (block-uniform).
     const bool edge = (k0 + FWD_BN > S) || (CAUSAL && k0 + FWD_BN - 1 > q0);
@@ -159,9 +172,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs 
       cp_async_commit();
     }
 
-    // O += P V, keys j = k0 .. k0 + 63 in order for every element.
+    // O += P V, keys j = k0 .. in order for every element (key groups past the end hold P = 0).
+    const int jlim = jn == 3 ? 48 : 64;
 #pragma unroll 2
-    for (int j = 0; j < FWD_BN; j += 4) {
+    for (int j = 0; j < jlim; j += 4) {
       float4 vv[4], pv[8];
 #pragma unroll
       for (int t = 0; t < 4; ++t) vv[t] = ld4(Vs + (j + t) * LD + 4 * tx);
