@@ -122,8 +122,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
   if (tid == 0) s_int[0] = atomicAdd(a.ticket, 1);
   __syncthreads();
   const int ticket = s_int[0];
-  const int kb = ticket % a.n_kblocks;
-  const int bh = ticket / a.n_kblocks;
+  // Turn chain: key blocks of one (b, h) on consecutive tickets (a block waits only on smaller
+  // tickets). No-wait path, causal: longest key blocks first (block kb walks n_qtiles - kb tiles),
+  // so the short ones fill the last wave.
+  const bool lpt = CAUSAL && a.dq_part != nullptr;
+  const int BH = a.B * a.H;
+  const int kb = lpt ? ticket / BH : ticket % a.n_kblocks;
+  const int bh = lpt ? ticket % BH : ticket / a.n_kblocks;
   const int b = bh / a.H, h = bh % a.H;
   const int k0 = kb * BWD_BN;
 

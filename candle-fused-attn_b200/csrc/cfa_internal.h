@@ -24,10 +24,11 @@ constexpr int BWD_BM = 64;
 constexpr int BWD_THREADS = 256;
 constexpr int PREP_THREADS = 256;
 
-// Sequences of at most PART_MAX_KBLOCKS key blocks can take the backward's no-wait dQ path: each
-// key block stores its dQ partials to scratch and the last block of a (batch, head) to finish
-// sums them in key-block order (the same sums, bit for bit, as the turn chain).
-constexpr int PART_MAX_KBLOCKS = 8;
+// Sequences of at most PART_MAX_KBLOCKS key blocks (s <= 1024) can take the backward's no-wait dQ
+// path: each key block stores its dQ partials to scratch and the last block of a (batch, head) to
+// finish sums them in key-block order (the same sums, bit for bit, as the turn chain). The
+// partials take n_kblocks times the size of dQ; longer sequences keep the turn chain.
+constexpr int PART_MAX_KBLOCKS = 16;
 
 // A bounded wait gives up after this much GPU time (ns) and flags CFA_ERR_TIMEOUT.
 constexpr uint64_t WAIT_TIMEOUT_NS = 2000000000ull;

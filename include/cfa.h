@@ -78,8 +78,9 @@ size_t cfa_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq);
 /* Bytes of device scratch that let the backward skip the waits of its dQ key-block chain: with
  * at least this much workspace, each key block stores its dQ partials to the scratch and the
  * last block of a (batch, head) to finish adds them in key-block order -- the same sums, bit for
- * bit, as with cfa_bwd_workspace_bytes, in less time. Applies to seq <= 512 (at most 8 key blocks
- * of 64); for longer sequences it equals cfa_bwd_workspace_bytes. Canvas b64 h6 s240: 94.7 MB. */
+ * bit, as with cfa_bwd_workspace_bytes, in less time. Applies to seq <= 1024 (at most 16 key
+ * blocks of 64; the partials take ceil(seq / 64) times the size of dQ); for longer sequences it
+ * equals cfa_bwd_workspace_bytes. Canvas b64 h6 s240: 94.7 MB. */
 size_t cfa_bwd_workspace_bytes_fast(int64_t batch, int64_t heads, int64_t seq);
 
 /* Backward from dO to one dqkv [batch, seq, 3, heads, 64] buffer (dQ, dK, dV interleaved).

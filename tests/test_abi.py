@@ -56,6 +56,8 @@ def test_workspace_formula():
     nkb = (s + 63) // 64
     assert _abi.bwd_workspace_bytes_fast(b, h, s) == 256 + turn + dsum + nkb * b * h * s * 64 * 4
     assert _abi.bwd_workspace_bytes_fast(4, 16, 8192) == _abi.bwd_workspace_bytes(4, 16, 8192)
+    assert _abi.bwd_workspace_bytes_fast(1, 1, 1024) > _abi.bwd_workspace_bytes(1, 1, 1024)
+    assert _abi.bwd_workspace_bytes_fast(1, 1, 1025) == _abi.bwd_workspace_bytes(1, 1, 1025)
 
 
 FAKE = 1 << 20  # a 16-byte aligned non-null "device pointer" never dereferenced by these checks

@@ -192,7 +192,8 @@ def test_c_abi_direct(cuda):
 
 
 @pytest.mark.parametrize("b,h,s,causal", [(64, 6, 240, False), (3, 2, 200, True),
-                                          (2, 2, 512, True), (2, 3, 65, False)])
+                                          (2, 2, 512, True), (2, 3, 65, False),
+                                          (3, 4, 1024, True), (2, 2, 1000, False)])
 def test_no_wait_dq_path_equals_turn_chain(cuda, b, h, s, causal):
     """The two dQ orderings (the key-block turn chain with the minimal workspace, the
     store-then-last-block-sums path with cfa_bwd_workspace_bytes_fast) give the same bits."""
