@@ -491,6 +491,11 @@ def main():
         return
 
     pk = peaks()
+    try:  # DRAM bytes of one backward call from the committed ncu capture (profiles/)
+        traffic = json.loads((ROOT / "profiles" / "roofline_traffic.json").read_text())
+        traffic = float(traffic["dram_bytes_per_call"])
+    except (OSError, ValueError, KeyError):
+        traffic = None
     bwd_flops = flops(b, H, S, D, CAUSAL, "bwd")
     achieved = bwd_flops / (bwd_ms * 1e-3) / 1e12
     line = {
@@ -516,7 +521,8 @@ def main():
         "roofline": {"bound": "compute", "pipe": "fp32 FFMA (CUDA cores)",
                      "kernel": "backward (prep + main, one cfa_bwd_f32_d64 call)",
                      "achieved": achieved, "peak": pk["ffma_tflops"], "unit": "TFLOP/s",
-                     "frac": achieved / pk["ffma_tflops"], "traffic": None,
+                     "frac": achieved / pk["ffma_tflops"], "traffic": traffic,
+                     "traffic_unit": "bytes per backward call (ncu, profiles/roofline_traffic.json)",
                      "peak_source": pk["source"],
                      "fwd_frac": flops(b, H, S, D, CAUSAL, "fwd") / (fwd_ms * 1e-3) / 1e12
                      / pk["ffma_tflops"]},
