@@ -24,8 +24,8 @@
 //   :178-205), no atomics on data: dQ = ((p0 + p1) + p2) + ... for every schedule.
 //
 // Forward progress without dispatch-order assumptions: a block takes its (batch, head, key block)
-// from a global ticket (atomicAdd), key blocks of one (batch, head) on consecutive tickets, so a
-// block only ever waits on blocks holding smaller tickets, which are already running or done.
+// from a global ticket (atomicAdd), key-block-major, so a block only ever waits on blocks holding
+// smaller tickets, which are already running or done.
 // Every wait is bounded (cfa::WAIT_TIMEOUT_NS); on expiry the error flag is set and the host
 // reads it with cfa_bwd_status. No GPU hangs on a broken invariant.
 #include "cfa_common.cuh"
@@ -122,13 +122,14 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
   if (tid == 0) s_int[0] = atomicAdd(a.ticket, 1);
   __syncthreads();
   const int ticket = s_int[0];
-  // Turn chain: key blocks of one (b, h) on consecutive tickets (a block waits only on smaller
-  // tickets). No-wait path, causal: longest key blocks first (block kb walks n_qtiles - kb tiles),
-  // so the short ones fill the last wave.
-  const bool lpt = CAUSAL && a.dq_part != nullptr;
+  // Tickets run key-block-major: every (b, h) of key block 0, then of key block 1, ... A block of
+  // the turn chain waits only on key block kb - 1 of its (b, h), which holds a smaller ticket, so
+  // it is running or done; and blocks of similar length (causal: block kb walks n_qtiles - kb
+  // tiles) share a wave, longest first, instead of a wave holding every key block of one (b, h)
+  // that all end with its key block 0.
   const int BH = a.B * a.H;
-  const int kb = lpt ? ticket / BH : ticket % a.n_kblocks;
-  const int bh = lpt ? ticket % BH : ticket / a.n_kblocks;
+  const int kb = ticket / BH;
+  const int bh = ticket % BH;
   const int b = bh / a.H, h = bh % a.H;
   const int k0 = kb * BWD_BN;
 
