@@ -144,11 +144,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
   load_tile_async<64, BWD_THREADS>(Ks, a.k + b * a.k_sb + h * a.k_sh, a.k_ss, k0, S);
   load_tile_async<64, BWD_THREADS>(Vs, a.v + b * a.v_sb + h * a.v_sh, a.v_ss, k0, S);
 
-  float acc[8][4];  // grp 0: dV, grp 1: dK (unscaled); [a][e]: key 16wg + 8ty + a, dim 4tx + e
+  // grp 0: dV, grp 1: dK (unscaled): acc2[rp][e] holds keys 16wg + 8ty + 2rp and + 2rp + 1 (the
+  // two halves of the pair), dim 4tx + e.
+  uint64_t acc2[4][4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
+    for (int e = 0; e < 4; ++e) acc2[i][e] = 0ull;
 
   const int rb1 = 16 * wg + ty;       // phase 1 rows: rb1 + 2i
   const int kb2 = 16 * wg + 8 * ty;   // phase 2 keys: kb2 .. kb2 + 7
@@ -231,6 +233,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
     }
 
     // Phase 2. grp 0: dV[j] += sum_i P[i][j] dO[i]; grp 1: dK[j] += sum_i dS[i][j] Q[i].
+    // Packed FMAs with the accumulators paired along keys: (x[j], x[j + 1]) is a register pair of
+    // the float4 read from P / dS, the dO / Q element is broadcast; each lane computes the same
+    // fmaf per element as scalar code would.
     // DETERMINISM: each dK, dV element is one thread's register, summed over query tiles and
     // then queries in index order.
     {
@@ -238,16 +243,14 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
       const float* Ys = grp ? Qs : dOs;
 #pragma unroll 4
       for (int i = 0; i < iq; ++i) {
-        const float4 xa = ld4(Xs + i * LDP + kb2), xb = ld4(Xs + i * LDP + kb2 + 4);
+        const ulonglong2 xa = ld2x2(Xs + i * LDP + kb2), xb = ld2x2(Xs + i * LDP + kb2 + 4);
         const float4 y = ld4(Ys + i * LD + 4 * tx);
-        const float xs[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+        const uint64_t xp[4] = {xa.x, xa.y, xb.x, xb.y};
+        const uint64_t yb[4] = {dup2(y.x), dup2(y.y), dup2(y.z), dup2(y.w)};
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          acc[r][0] = fmaf(xs[r], y.x, acc[r][0]);
-          acc[r][1] = fmaf(xs[r], y.y, acc[r][1]);
-          acc[r][2] = fmaf(xs[r], y.z, acc[r][2]);
-          acc[r][3] = fmaf(xs[r], y.w, acc[r][3]);
-        }
+        for (int rp = 0; rp < 4; ++rp)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc2[rp][e] = fma2(xp[rp], yb[e], acc2[rp][e]);
       }
     }
     // Every thread is done with Q, dO, L, D of this tile: the next tile's copies travel during
@@ -259,29 +262,37 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
     }
 
     // Phase 3: the dQ partial pq[r][e] = sum_j dS[rb3 + 2r][j] K[j][4tx + e], keys in order.
-    float pq[4][4];
+    // Packed FMAs, accumulators paired along dims ((e, e + 1) of the float4 read from K), the
+    // dS element broadcast: the same fmaf per element as scalar code.
+    uint64_t pq2[4][2];
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) pq[r][e] = 0.0f;
+    for (int r = 0; r < 4; ++r) pq2[r][0] = pq2[r][1] = 0ull;
     const int jlim = 16 * jn;
 #pragma unroll 2
     for (int j = 0; j < jlim; j += 4) {
-      float4 k4[4], d4[4];
+      ulonglong2 k4[4];
+      float4 d4[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) k4[u] = ld4(Ks + (j + u) * LD + 4 * tx);
+      for (int u = 0; u < 4; ++u) k4[u] = ld2x2(Ks + (j + u) * LD + 4 * tx);
 #pragma unroll
       for (int r = 0; r < 4; ++r) d4[r] = ld4(dSs + (rb3 + 2 * r) * LDP + j);
 #pragma unroll
       for (int u = 0; u < 4; ++u)
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-          const float ds = f4c(d4[r], u);
-          pq[r][0] = fmaf(ds, k4[u].x, pq[r][0]);
-          pq[r][1] = fmaf(ds, k4[u].y, pq[r][1]);
-          pq[r][2] = fmaf(ds, k4[u].z, pq[r][2]);
-          pq[r][3] = fmaf(ds, k4[u].w, pq[r][3]);
+          const uint64_t ds = dup2(f4c(d4[r], u));
+          pq2[r][0] = fma2(ds, k4[u].x, pq2[r][0]);
+          pq2[r][1] = fma2(ds, k4[u].y, pq2[r][1]);
         }
+    }
+    float pq[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float2 lo = split2(pq2[r][0]), hi = split2(pq2[r][1]);
+      pq[r][0] = lo.x;
+      pq[r][1] = lo.y;
+      pq[r][2] = hi.x;
+      pq[r][3] = hi.y;
     }
 
     if (a.dq_part != nullptr) {
@@ -371,11 +382,17 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
                 h * 64 + 4 * tx;
   const float f = grp ? a.scale : 1.0f;
 #pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const int j = k0 + kb2 + r;
-    if (j >= S) continue;
-    *reinterpret_cast<float4*>(dst0 + j * row_stride) =
-        make_float4(acc[r][0] * f, acc[r][1] * f, acc[r][2] * f, acc[r][3] * f);
+  for (int rp = 0; rp < 4; ++rp) {
+    float2 v[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = split2(acc2[rp][e]);
+    const int j = k0 + kb2 + 2 * rp;
+    if (j < S)
+      *reinterpret_cast<float4*>(dst0 + j * row_stride) =
+          make_float4(v[0].x * f, v[1].x * f, v[2].x * f, v[3].x * f);
+    if (j + 1 < S)
+      *reinterpret_cast<float4*>(dst0 + (j + 1) * row_stride) =
+          make_float4(v[0].y * f, v[1].y * f, v[2].y * f, v[3].y * f);
   }
 }
 

@@ -123,6 +123,26 @@ __device__ __forceinline__ ulonglong2 ld2x2(const float* p) {
   return *reinterpret_cast<const ulonglong2*>(p);
 }
 
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// (x, x): one value in both halves of a pair (the broadcast operand of an outer product).
+__device__ __forceinline__ uint64_t dup2(float x) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(x));
+  return r;
+}
+
+// The two halves of a pair.
+__device__ __forceinline__ float2 split2(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+
 // The sum of a pair's two halves: lo + hi.
 __device__ __forceinline__ float sum2(uint64_t v) {
   float lo, hi;

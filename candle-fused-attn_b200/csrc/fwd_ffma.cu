@@ -100,13 +100,14 @@ __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs 
   // with CUDA's expf. lpart is this thread's share
   // of the row sum (its 4 keys per tile, rescaled like O); the 16 shares of a row are added once,
   // after the last tile.
-  float m[8], lpart[8], acc[8][4];
+  // acc2[i][0] holds dims 4tx, 4tx + 1 of row rb + 2i, acc2[i][1] dims 4tx + 2, 4tx + 3.
+  float m[8], lpart[8];
+  uint64_t acc2[8][2];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     m[i] = -INFINITY;
     lpart[i] = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
+    acc2[i][0] = acc2[i][1] = 0ull;
   }
 
   for (int k0 = 0; k0 < k_end; k0 += FWD_BN) {
@@ -160,8 +161,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs 
       }
       lpart[i] = fmaf(lpart[i], alpha, psum);
       m[i] = m_new;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[i][e] *= alpha;
+      const uint64_t al = dup2(alpha);
+      acc2[i][0] = mul2(acc2[i][0], al);
+      acc2[i][1] = mul2(acc2[i][1], al);
     }
     // V(k0) has landed, every P is written, and every thread is done with Ks: K(k0 + 64) may
     // overwrite Ks while P V runs.
@@ -173,23 +175,24 @@ __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs 
     }
 
     // O += P V, keys j = k0 .. in order for every element (key groups past the end hold P = 0).
+    // Packed FMAs, accumulators paired along dims ((e, e + 1) of the float4 read from V), the P
+    // element broadcast: the same fmaf per element as scalar code.
     const int jlim = jn == 3 ? 48 : 64;
 #pragma unroll 2
     for (int j = 0; j < jlim; j += 4) {
-      float4 vv[4], pv[8];
+      ulonglong2 vv[4];
+      float4 pv[8];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) vv[t] = ld4(Vs + (j + t) * LD + 4 * tx);
+      for (int t = 0; t < 4; ++t) vv[t] = ld2x2(Vs + (j + t) * LD + 4 * tx);
 #pragma unroll
       for (int i = 0; i < 8; ++i) pv[i] = ld4(Ps + (rb + 2 * i) * LDP + j);
 #pragma unroll
       for (int t = 0; t < 4; ++t)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float pr = f4c(pv[i], t);
-          acc[i][0] = fmaf(pr, vv[t].x, acc[i][0]);
-          acc[i][1] = fmaf(pr, vv[t].y, acc[i][1]);
-          acc[i][2] = fmaf(pr, vv[t].z, acc[i][2]);
-          acc[i][3] = fmaf(pr, vv[t].w, acc[i][3]);
+          const uint64_t pr = dup2(f4c(pv[i], t));
+          acc2[i][0] = fma2(pr, vv[t].x, acc2[i][0]);
+          acc2[i][1] = fma2(pr, vv[t].y, acc2[i][1]);
         }
     }
   }
@@ -203,8 +206,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs 
     float4* dst = reinterpret_cast<float4*>(
         a.o + ((static_cast<int64_t>(b) * S + qi) * a.H + h) * 64 + 4 * tx);
     // O = acc / l with one rounding (IEEE division), once per output element.
-    *dst = make_float4(__fdiv_rn(acc[i][0], l), __fdiv_rn(acc[i][1], l), __fdiv_rn(acc[i][2], l),
-                       __fdiv_rn(acc[i][3], l));
+    const float2 lo = split2(acc2[i][0]), hi = split2(acc2[i][1]);
+    *dst = make_float4(__fdiv_rn(lo.x, l), __fdiv_rn(lo.y, l), __fdiv_rn(hi.x, l),
+                       __fdiv_rn(hi.y, l));
     if (tx == 0) a.lse[static_cast<int64_t>(bh) * S + qi] = m[i] + logf(l);
   }
 }
