@@ -128,8 +128,11 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
   // tiles) share a wave, longest first, instead of a wave holding every key block of one (b, h)
   // that all end with its key block 0.
   const int BH = a.B * a.H;
-  const int kb = ticket / BH;
-  const int bh = ticket % BH;
+  // (Non-causal, no-wait path: (b, h)-major instead, so each (b, h)'s last block -- the one that
+  // sums its dQ partials -- finishes throughout the run rather than all in the last wave.)
+  const bool bh_major = !CAUSAL && a.dq_part != nullptr;
+  const int kb = bh_major ? ticket % a.n_kblocks : ticket / BH;
+  const int bh = bh_major ? ticket / a.n_kblocks : ticket % BH;
   const int b = bh / a.H, h = bh % a.H;
   const int k0 = kb * BWD_BN;
 
@@ -358,21 +361,45 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
       __threadfence();
       const float* part = a.dq_part + static_cast<int64_t>(bh) * a.n_kblocks * S * 64;
       // DETERMINISM: dQ = (((p0 + p1) + p2) + ...) * scale over the contributing key blocks in
-      // index order: the turn chain's sums, bit for bit, whichever block does them.
-      for (int idx = tid; idx < S * 16; idx += BWD_THREADS) {
-        const int i = idx >> 4, c4 = idx & 15;
-        const int t = i / BWD_BM;
-        const int last = CAUSAL ? min(a.n_kblocks - 1, min(S - 1, t * BWD_BM + BWD_BM - 1) / BWD_BN)
-                                : a.n_kblocks - 1;
-        const float* src = part + static_cast<int64_t>(i) * 64 + 4 * c4;
-        float4 v = __ldcg(reinterpret_cast<const float4*>(src));
-        for (int j = 1; j <= last; ++j) {
-          const float4 p =
-              __ldcg(reinterpret_cast<const float4*>(src + static_cast<int64_t>(j) * S * 64));
-          v = make_float4(v.x + p.x, v.y + p.y, v.z + p.z, v.w + p.w);
+      // index order: the turn chain's sums, bit for bit, whichever block does them. Eight rows
+      // per thread in flight at once (their partial loads are independent).
+      constexpr int R = 8;
+      for (int base = 0; base < S * 16; base += BWD_THREADS * R) {
+        float4 v[R];
+        int last[R];
+#pragma unroll
+        for (int u = 0; u < R; ++u) {
+          const int idx = base + u * BWD_THREADS + tid;
+          const int i = min(idx, S * 16 - 1) >> 4, c4 = idx & 15;
+          const int t = i / BWD_BM;
+          last[u] = CAUSAL
+                        ? min(a.n_kblocks - 1, min(S - 1, t * BWD_BM + BWD_BM - 1) / BWD_BN)
+                        : a.n_kblocks - 1;
+          v[u] = __ldcg(reinterpret_cast<const float4*>(part + static_cast<int64_t>(i) * 64 +
+                                                        4 * c4));
         }
-        v = make_float4(v.x * a.scale, v.y * a.scale, v.z * a.scale, v.w * a.scale);
-        *reinterpret_cast<float4*>(dq_base + i * row_stride + 4 * c4) = v;
+        for (int j = 1; j < a.n_kblocks; ++j) {
+#pragma unroll
+          for (int u = 0; u < R; ++u) {
+            const int idx = base + u * BWD_THREADS + tid;
+            const int i = min(idx, S * 16 - 1) >> 4, c4 = idx & 15;
+            if (j <= last[u]) {
+              const float4 p = __ldcg(reinterpret_cast<const float4*>(
+                  part + (static_cast<int64_t>(j) * S + i) * 64 + 4 * c4));
+              v[u] = make_float4(v[u].x + p.x, v[u].y + p.y, v[u].z + p.z, v[u].w + p.w);
+            }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < R; ++u) {
+          const int idx = base + u * BWD_THREADS + tid;
+          if (idx < S * 16) {
+            const int i = idx >> 4, c4 = idx & 15;
+            *reinterpret_cast<float4*>(dq_base + i * row_stride + 4 * c4) =
+                make_float4(v[u].x * a.scale, v[u].y * a.scale, v[u].z * a.scale,
+                            v[u].w * a.scale);
+          }
+        }
       }
     }
   }
