@@ -444,6 +444,32 @@ def main():
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     e2e_ms = float(e2e_t.item())
 
+    # the floor e2e is measured against: the same bytes, both directions at once, no kernels (all
+    # ranks copy concurrently, as in the e2e; the host side of a box is shared between them)
+    fq, fg = torch.empty_like(sets[0].qkv), torch.empty_like(sets[0].dout)
+
+    def copy_step(i):
+        cur = torch.cuda.current_stream()
+        pipe.h2d.wait_stream(cur)
+        pipe.d2h.wait_stream(cur)
+        with torch.cuda.stream(pipe.h2d):
+            fq.copy_(hq[i % N_SETS], non_blocking=True)
+            fg.copy_(hg[i % N_SETS], non_blocking=True)
+        with torch.cuda.stream(pipe.d2h):
+            ho.copy_(sets[i % N_SETS].dout.view(b, S, H * D), non_blocking=True)
+            hd.copy_(sets[i % N_SETS].qkv.view(b, S, 3 * H * D), non_blocking=True)
+        cur.wait_stream(pipe.h2d)
+        cur.wait_stream(pipe.d2h)
+
+    for i in range(3):
+        copy_step(i)
+    floor_ms = timed(copy_step, args.steps, torch.cuda.current_stream(), sync=barrier)
+    floor_t = torch.tensor([floor_ms], device=dev)
+    if dist is not None:
+        dist.all_reduce(floor_t, op=dist.ReduceOp.MAX)
+    floor_ms = float(floor_t.item())
+    del fq, fg
+
     # the same through fused_attention_qkv + autograd, one whole-batch call, copies not overlapped
     def autograd_step(i):
         x = hq[i % N_SETS].to(dev, non_blocking=True).requires_grad_(True)
@@ -515,6 +541,9 @@ def main():
                 "d2h_bytes_per_step": (ho.numel() + hd.numel()) * 4,
                 "path": "candle_fused_attn.HostPipeline (pinned host qkv, dO in; O, dqkv out; "
                         "4 batch chunks, 2 buffer slots over H2D / kernel / D2H streams)",
+                "copy_floor_ms": floor_ms,
+                "copy_floor": "the same bytes copied both ways at once with no kernel, every "
+                              "rank concurrently, max over ranks",
                 "autograd_ms_per_step": autograd_ms,
                 "autograd_path": "fused_attention_qkv + autograd backward, whole batch, copies "
                                  "not overlapped"},
