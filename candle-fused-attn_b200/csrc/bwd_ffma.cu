@@ -183,9 +183,11 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
     __syncthreads();
 
     // Dead work on edge tiles is skipped, uniformly per tile: key groups wholly past the sequence
-    // end (jn) and query rows past it in the phase-2 sums (iq). The skipped terms are masked
-    // scores and products with P = 0 or dS = 0: the live results are the same bits either way.
-    // (Skipping whole dead warps measured slower: the branches cost registers.)
+    // end (jn) and query rows past it in the phase-2 sums (iq); and, uniformly per warp, a warp
+    // whose rows (phases 1 and 3) or keys (phase 2) all lie past the end does no products. The
+    // skipped terms are masked scores and products with P = 0 or dS = 0: the live results are
+    // the same bits either way. (Canvas s = 240: -2.7% time; the forward's counterpart measured
+    // slower and is not done.)
     const int jn = min(4, (S - k0 + 15) / 16);
     const int iq = min(BWD_BM, (S - q0 + 15) / 16 * 16);
 
@@ -194,7 +196,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
       const float* As = grp ? dOs : Qs;
       const float* Bs = grp ? Vs : Ks;
       float s[8][4];
-      if (jn == 4)
+      if (q0 + 16 * wg >= S) {
+        // rows 16 wg .. 16 wg + 15 all past the end: s = 0 gives P = 0 (masked) and dS = 0
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) s[i][jj] = 0.0f;
+      } else if (jn == 4)
         phase1_tile<4>(As, Bs, rb1, tx, s);
       else if (jn == 3)
         phase1_tile<3>(As, Bs, rb1, tx, s);
@@ -244,8 +252,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
     {
       const float* Xs = grp ? dSs : Ps;
       const float* Ys = grp ? Qs : dOs;
+      const int iw = k0 + 16 * wg >= S ? 0 : iq;  // keys kb2 .. kb2 + 7 all past the end: none
 #pragma unroll 4
-      for (int i = 0; i < iq; ++i) {
+      for (int i = 0; i < iw; ++i) {
         const ulonglong2 xa = ld2x2(Xs + i * LDP + kb2), xb = ld2x2(Xs + i * LDP + kb2 + 4);
         const float4 y = ld4(Ys + i * LD + 4 * tx);
         const uint64_t xp[4] = {xa.x, xa.y, xb.x, xb.y};
@@ -270,7 +279,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
     uint64_t pq2[4][2];
 #pragma unroll
     for (int r = 0; r < 4; ++r) pq2[r][0] = pq2[r][1] = 0ull;
-    const int jlim = 16 * jn;
+    const int jlim = q0 + 8 * w >= S ? 0 : 16 * jn;  // rows rb3 + 2r all past the end: none
 #pragma unroll 2
     for (int j = 0; j < jlim; j += 4) {
       ulonglong2 k4[4];
