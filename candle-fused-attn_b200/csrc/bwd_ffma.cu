@@ -36,6 +36,8 @@ namespace {
 constexpr int BWD_SMEM_FLOATS = 4 * 64 * LD + 2 * 64 * LDP + 2 * 64 + 4;
 
 __global__ void __launch_bounds__(PREP_THREADS) bwd_prep_kernel(const PrepArgs a) {
+  griddep_wait();  // O (the forward's) and dO may come from the previous kernel
+  griddep_launch_dependents();
   const int64_t gtid = static_cast<int64_t>(blockIdx.x) * PREP_THREADS + threadIdx.x;
   const int64_t gstride = static_cast<int64_t>(gridDim.x) * PREP_THREADS;
   for (int64_t z = gtid; z < a.n_zero; z += gstride) a.zero[z] = 0;
@@ -114,6 +116,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
   float* Dt = Lt + 64;                          // [64] D of this tile (0 past S)
   int* s_int = reinterpret_cast<int*>(Dt + 64); // [0]: ticket, [1]: turn came
 
+  griddep_wait();  // D, the cleared ticket and counters: the prep kernel's writes
+  griddep_launch_dependents();
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
   const int ty = lane >> 4, tx = lane & 15;
   const int grp = w >> 2, wg = w & 3;  // grp 0: S, P, dV; grp 1: dP, dS, dK (warp-uniform)
@@ -449,18 +453,16 @@ cudaError_t launch_bwd_prep(const PrepArgs& a, cudaStream_t stream) {
   const int64_t rows = static_cast<int64_t>(a.B) * a.H * a.S;
   int64_t blocks = (rows * 16 + PREP_THREADS - 1) / PREP_THREADS;
   if (blocks < 1) blocks = 1;
-  bwd_prep_kernel<<<static_cast<unsigned>(blocks), PREP_THREADS, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(bwd_prep_kernel, dim3(static_cast<unsigned>(blocks)), dim3(PREP_THREADS), 0,
+                    stream, a);
 }
 
 cudaError_t launch_bwd(const BwdArgs& a, int causal, cudaStream_t stream) {
   const int64_t blocks = static_cast<int64_t>(a.n_kblocks) * a.B * a.H;
   const dim3 grid(static_cast<unsigned>(blocks));
   if (causal)
-    bwd_ffma_kernel<true><<<grid, BWD_THREADS, bwd_smem_bytes(), stream>>>(a);
-  else
-    bwd_ffma_kernel<false><<<grid, BWD_THREADS, bwd_smem_bytes(), stream>>>(a);
-  return cudaGetLastError();
+    return launch_pdl(bwd_ffma_kernel<true>, grid, dim3(BWD_THREADS), bwd_smem_bytes(), stream, a);
+  return launch_pdl(bwd_ffma_kernel<false>, grid, dim3(BWD_THREADS), bwd_smem_bytes(), stream, a);
 }
 
 }  // namespace cfa

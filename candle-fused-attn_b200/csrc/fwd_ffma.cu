@@ -69,6 +69,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs 
   float* Vs = Ks + FWD_BN * LD;                 // [64][LD]
   float* Ps = Vs + FWD_BN * LD;                 // [64][LDP], query-major; warp w uses rows 16w..
 
+  griddep_wait();  // q, k, v may come from the previous kernel on the stream
+  griddep_launch_dependents();
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
   const int ty = lane >> 4, tx = lane & 15;
   const int BH = a.B * a.H;
@@ -230,10 +232,8 @@ cudaError_t launch_fwd(const FwdArgs& a, int causal, cudaStream_t stream) {
   const int64_t blocks = static_cast<int64_t>(a.n_qtiles) * a.B * a.H;
   const dim3 grid(static_cast<unsigned>(blocks));
   if (causal)
-    fwd_ffma_kernel<true><<<grid, FWD_THREADS, fwd_smem_bytes(), stream>>>(a);
-  else
-    fwd_ffma_kernel<false><<<grid, FWD_THREADS, fwd_smem_bytes(), stream>>>(a);
-  return cudaGetLastError();
+    return launch_pdl(fwd_ffma_kernel<true>, grid, dim3(FWD_THREADS), fwd_smem_bytes(), stream, a);
+  return launch_pdl(fwd_ffma_kernel<false>, grid, dim3(FWD_THREADS), fwd_smem_bytes(), stream, a);
 }
 
 }  // namespace cfa
