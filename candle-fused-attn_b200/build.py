@@ -20,7 +20,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 OUT = PKG / "candle_fused_attn" / "libcfa.so"
-SOURCES = ["fwd_ffma.cu", "bwd_ffma.cu", "cfa_abi.cu", "cfa_noalloc.cu"]
+SOURCES = ["fwd_ffma.cu", "bwd_ffma.cu", "hd_ffma.cu", "cfa_abi.cu", "cfa_noalloc.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

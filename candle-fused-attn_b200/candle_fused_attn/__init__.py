@@ -1,5 +1,5 @@
 # SPDX-License-Identifier: MIT OR Apache-2.0
-"""candle_fused_attn -- fused fp32 scaled-dot-product attention for B200 (sm_100a), head_dim 64.
+"""candle_fused_attn -- fused fp32 scaled-dot-product attention for B200 (sm_100a).
 
 The public API of the candle-fused-attn crate (src/lib.rs), over torch tensors, on the C ABI of
 include/cfa.h:
@@ -10,7 +10,9 @@ include/cfa.h:
 - `fused_attention(q, k, v, scale, causal)` (src/lib.rs:143-161): `[batch, heads, seq, 64]` with
   any strides -> `[batch, heads, seq, 64]`, a transposed view of a dense `[batch, seq, heads, 64]`
   buffer (merge-heads ready).
-- `CUDA_HEAD_DIM` (src/lib.rs:91).
+- `CUDA_HEAD_DIM` (src/lib.rs:91): 64, the head dim of the reference's CUDA path; `HEAD_DIMS`:
+  the head dims these kernels take, (32, 64, 128) -- 32 and 128 extend the reference's CUDA path
+  (its ROADMAP.md "head_dim 32 and 128"; its CPU path takes any head dim).
 
 Both read their operands in place when `head_dim` is contiguous and the offset and every other
 stride are multiples of 4 floats, and copy them to a contiguous tensor first otherwise (the
@@ -19,8 +21,8 @@ backward is the row log-sum-exp L `[batch, heads, seq]` (src/lib.rs:301-315); th
 recomputes P from it.
 
 Device only: the CUDA kernels are the product; the reference's CPU composed path lives in the
-test oracle (oracle/), never here. A CPU tensor, a dtype other than float32, a head_dim other
-than 64, or a missing libcfa.so raise `FusedAttentionError` / `ImportError`.
+test oracle (oracle/), never here. A CPU tensor, a dtype other than float32, a head_dim not in
+`HEAD_DIMS`, or a missing libcfa.so raise `FusedAttentionError` / `ImportError`.
 """
 
 from __future__ import annotations
@@ -31,6 +33,7 @@ from . import _abi
 
 __all__ = [
     "CUDA_HEAD_DIM",
+    "HEAD_DIMS",
     "FusedAttentionError",
     "fused_attention",
     "fused_attention_qkv",
@@ -42,6 +45,14 @@ __all__ = [
 ]
 
 CUDA_HEAD_DIM = 64  # src/lib.rs:91
+HEAD_DIMS = _abi.HEAD_DIMS  # (32, 64, 128)
+
+
+def _check_head_dim(d: int) -> None:
+    if d not in HEAD_DIMS:
+        raise FusedAttentionError(
+            f"fused_attention: the CUDA kernels take head_dim {CUDA_HEAD_DIM} "
+            f"(and 32 or 128), got {d}")
 
 
 class FusedAttentionError(RuntimeError):
@@ -131,14 +142,13 @@ def attention_forward(q_ptr, qs, k_ptr, ks, v_ptr, vs, dims, scale, causal, devi
     """One forward over device operands given as (pointer, (sb, sh, ss)): returns (O [b, s, h, d],
     L [b, h, s]) as fresh tensors (the role of src/cuda.rs:140-185)."""
     b, h, s, d = dims
-    if d != CUDA_HEAD_DIM:
-        raise FusedAttentionError(
-            f"fused_attention: the CUDA kernels take head_dim {CUDA_HEAD_DIM}, got {d}")
+    _check_head_dim(d)
     o = torch.empty((b, s, h, d), dtype=torch.float32, device=device)
     lse = torch.empty((b, h, s), dtype=torch.float32, device=device)
+    fwd = _abi.fwd if d == CUDA_HEAD_DIM else _abi.fwd_hd
     with torch.cuda.device(device):
-        st = _abi.fwd(q_ptr, qs, k_ptr, ks, v_ptr, vs, o.data_ptr(), lse.data_ptr(),
-                      b, h, s, d, float(scale), causal, _stream(device))
+        st = fwd(q_ptr, qs, k_ptr, ks, v_ptr, vs, o.data_ptr(), lse.data_ptr(),
+                 b, h, s, d, float(scale), causal, _stream(device))
     if st != _abi.CFA_OK:
         raise FusedAttentionError(_abi.strerror(st))
     return o, lse
@@ -149,21 +159,20 @@ def attention_backward(q_ptr, qs, k_ptr, ks, v_ptr, vs, o, lse, do_ptr, dos, dim
     """One backward: dqkv [b, s, 3, h, d] (the role of src/cuda.rs:190-260). The scratch comes
     from torch's caching allocator; `check_status` synchronises and reads the device error flag."""
     b, h, s, d = dims
-    if d != CUDA_HEAD_DIM:
-        raise FusedAttentionError(
-            f"fused_attention: the CUDA kernels take head_dim {CUDA_HEAD_DIM}, got {d}")
+    _check_head_dim(d)
     if not (o.is_contiguous() and lse.is_contiguous()):
         raise FusedAttentionError("fused_attention: O and L must be contiguous")
     dqkv = torch.empty((b, s, 3, h, d), dtype=torch.float32, device=device)
     # The larger workspace enables the no-wait dQ path (same bits); torch's caching allocator
     # recycles it across steps.
-    ws_bytes = _abi.bwd_workspace_bytes_fast(b, h, s)
+    ws_bytes = _abi.bwd_workspace_bytes_fast_hd(b, h, s, d)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+    bwd = _abi.bwd if d == CUDA_HEAD_DIM else _abi.bwd_hd
     with torch.cuda.device(device):
         stream = _stream(device)
-        st = _abi.bwd(q_ptr, qs, k_ptr, ks, v_ptr, vs, o.data_ptr(), lse.data_ptr(), do_ptr, dos,
-                      dqkv.data_ptr(), ws.data_ptr(), ws_bytes, b, h, s, d, float(scale), causal,
-                      stream)
+        st = bwd(q_ptr, qs, k_ptr, ks, v_ptr, vs, o.data_ptr(), lse.data_ptr(), do_ptr, dos,
+                 dqkv.data_ptr(), ws.data_ptr(), ws_bytes, b, h, s, d, float(scale), causal,
+                 stream)
         if st == _abi.CFA_OK and check_status:
             st = _abi.bwd_status(ws.data_ptr(), stream)
     if st != _abi.CFA_OK:
@@ -237,7 +246,8 @@ class _FusedAttentionQkv(torch.autograd.Function):
 
 
 def fused_attention_qkv(qkv: torch.Tensor, heads: int, scale: float, causal: bool) -> torch.Tensor:
-    """src/lib.rs:110-125. `qkv` [batch, seq, 3*heads*64] f32 on CUDA -> [batch, seq, heads*64]."""
+    """src/lib.rs:110-125. `qkv` [batch, seq, 3*heads*d] f32 on CUDA -> [batch, seq, heads*d], d in
+    HEAD_DIMS."""
     st = qkv.stride()
     aligned = (qkv.dim() == 3 and qkv.storage_offset() % 4 == 0 and st[2] == 1
                and st[0] % 4 == 0 and st[1] % 4 == 0)
@@ -248,8 +258,8 @@ def fused_attention_qkv(qkv: torch.Tensor, heads: int, scale: float, causal: boo
 
 def fused_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
                     causal: bool) -> torch.Tensor:
-    """src/lib.rs:143-161. q, k, v [batch, heads, seq, 64] f32 on CUDA, any strides ->
-    [batch, heads, seq, 64] (a transposed view of a dense [batch, seq, heads, 64] buffer)."""
+    """src/lib.rs:143-161. q, k, v [batch, heads, seq, d] f32 on CUDA (d in HEAD_DIMS), any
+    strides -> [batch, heads, seq, d] (a transposed view of a dense [batch, seq, heads, d] buffer)."""
     q, k, v = _float4_rows(q), _float4_rows(k), _float4_rows(v)
     return _FusedAttention.apply(q, k, v, float(scale), bool(causal)).transpose(1, 2)
 

@@ -38,7 +38,15 @@ EXPORTS = (
     "cfa_selftest_bounded_wait",
     "cfa_strerror",
     "cfa_abi_version",
+    "cfa_fwd_f32",
+    "cfa_bwd_workspace_bytes_hd",
+    "cfa_bwd_workspace_bytes_fast_hd",
+    "cfa_bwd_f32",
 )
+
+# Head dims the generic entry points (cfa_fwd_f32, cfa_bwd_f32) take; the _d64 ones take 64 only,
+# as the reference's CUDA path does (src/lib.rs:91).
+HEAD_DIMS = (32, 64, 128)
 
 _i64 = ctypes.c_int64
 _p = ctypes.c_void_p
@@ -86,6 +94,14 @@ def load() -> ctypes.CDLL:
     lib.cfa_strerror.argtypes = [ctypes.c_int]
     lib.cfa_abi_version.restype = ctypes.c_int
     lib.cfa_abi_version.argtypes = []
+    lib.cfa_fwd_f32.restype = ctypes.c_int
+    lib.cfa_fwd_f32.argtypes = lib.cfa_fwd_f32_d64.argtypes
+    lib.cfa_bwd_f32.restype = ctypes.c_int
+    lib.cfa_bwd_f32.argtypes = lib.cfa_bwd_f32_d64.argtypes
+    for name in ("cfa_bwd_workspace_bytes_hd", "cfa_bwd_workspace_bytes_fast_hd"):
+        fn = getattr(lib, name)
+        fn.restype = ctypes.c_size_t
+        fn.argtypes = [_i64, _i64, _i64, _i64]
     _lib = lib
     return lib
 
@@ -123,6 +139,31 @@ def bwd(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, do_ptr, dos, dqkv_ptr, 
         b, h, s, d, scale, causal, stream) -> int:
     """cfa_bwd_f32_d64; returns the status."""
     return load().cfa_bwd_f32_d64(
+        q_ptr, strides3(qs), k_ptr, strides3(ks), v_ptr, strides3(vs), o_ptr, lse_ptr,
+        do_ptr, strides3(dos), dqkv_ptr, ws_ptr, ws_bytes, b, h, s, d,
+        ctypes.c_float(scale), int(bool(causal)), stream)
+
+
+def fwd_hd(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, b, h, s, d, scale, causal,
+           stream) -> int:
+    """cfa_fwd_f32 (head dim d in HEAD_DIMS); returns the status."""
+    return load().cfa_fwd_f32(
+        q_ptr, strides3(qs), k_ptr, strides3(ks), v_ptr, strides3(vs), o_ptr, lse_ptr,
+        b, h, s, d, ctypes.c_float(scale), int(bool(causal)), stream)
+
+
+def bwd_workspace_bytes_hd(b, h, s, d) -> int:
+    return int(load().cfa_bwd_workspace_bytes_hd(b, h, s, d))
+
+
+def bwd_workspace_bytes_fast_hd(b, h, s, d) -> int:
+    return int(load().cfa_bwd_workspace_bytes_fast_hd(b, h, s, d))
+
+
+def bwd_hd(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, do_ptr, dos, dqkv_ptr, ws_ptr,
+           ws_bytes, b, h, s, d, scale, causal, stream) -> int:
+    """cfa_bwd_f32 (head dim d in HEAD_DIMS); returns the status."""
+    return load().cfa_bwd_f32(
         q_ptr, strides3(qs), k_ptr, strides3(ks), v_ptr, strides3(vs), o_ptr, lse_ptr,
         do_ptr, strides3(dos), dqkv_ptr, ws_ptr, ws_bytes, b, h, s, d,
         ctypes.c_float(scale), int(bool(causal)), stream)

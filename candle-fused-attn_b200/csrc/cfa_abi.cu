@@ -24,6 +24,7 @@ struct DeviceOnce {
 };
 DeviceOnce g_fwd_once[kMaxDevices];
 DeviceOnce g_bwd_once[kMaxDevices];
+DeviceOnce g_hd_once[kMaxDevices];  // head dims 32 and 128
 
 int setup(DeviceOnce* table, cudaError_t (*fn)()) {
   int dev = 0;
@@ -40,11 +41,16 @@ bool strides_ok(const int64_t* s) {
   return s[0] % 4 == 0 && s[1] % 4 == 0 && s[2] % 4 == 0;
 }
 
-// Common shape checks. Returns CFA_OK with *empty set when there is nothing to do.
-int check_dims(int64_t B, int64_t H, int64_t S, int64_t D, bool* empty) {
+bool head_dim_ok(int64_t D, bool any_dim) {
+  return any_dim ? (D == 32 || D == 64 || D == 128) : D == CFA_HEAD_DIM;
+}
+
+// Common shape checks. Returns CFA_OK with *empty set when there is nothing to do. any_dim: the
+// head-dim-generic entry points (32, 64, 128); otherwise the reference's gate (64 only).
+int check_dims(int64_t B, int64_t H, int64_t S, int64_t D, bool any_dim, bool* empty) {
   *empty = false;
   if (B < 0 || H < 0 || S < 0 || D < 0) return CFA_ERR_SHAPE;
-  if (D != CFA_HEAD_DIM) return CFA_ERR_HEAD_DIM;
+  if (!head_dim_ok(D, any_dim)) return CFA_ERR_HEAD_DIM;
   if (B == 0 || H == 0 || S == 0) {
     *empty = true;
     return CFA_OK;
@@ -52,45 +58,24 @@ int check_dims(int64_t B, int64_t H, int64_t S, int64_t D, bool* empty) {
   // Kernel indices: (b * H + h) and its tiles fit int32; element offsets are int64.
   const int64_t lim = (int64_t(1) << 31) - 1;
   if (B > lim || H > lim || S > lim) return CFA_ERR_OVERFLOW;
-  if (B * H > lim / ((S + 63) / 64)) return CFA_ERR_OVERFLOW;  // grid size
+  if (B * H > lim / ((S + 31) / 32)) return CFA_ERR_OVERFLOW;  // grid size (smallest tile: 32)
   if (B * H * S > lim) return CFA_ERR_OVERFLOW;                 // row index of L, D
   return CFA_OK;
 }
 
-}  // namespace
-
-extern "C" {
-
-int cfa_abi_version(void) { return (1 << 16) | 0; }
-
-const char* cfa_strerror(int status) {
-  switch (status) {
-    case CFA_OK: return "fused_attention: ok";
-    case CFA_ERR_HEAD_DIM: return "fused_attention: the CUDA kernels take head_dim 64";
-    case CFA_ERR_ALIGNMENT: return "fused_attention: rows must be 16-byte aligned";
-    case CFA_ERR_SHAPE: return "fused_attention: negative dimension";
-    case CFA_ERR_OVERFLOW: return "fused_attention: problem size exceeds the kernels' index range";
-    case CFA_ERR_NULL: return "fused_attention: null pointer";
-    case CFA_ERR_WORKSPACE: return "fused_attention: workspace too small or misaligned";
-    case CFA_ERR_LAUNCH: return "fused_attention: kernel launch failed";
-    case CFA_ERR_TIMEOUT: return "fused_attention: a bounded device wait expired (results invalid)";
-    case CFA_ERR_CUDA: return "fused_attention: CUDA runtime error";
-    default: return "fused_attention: unknown status";
-  }
-}
-
-int cfa_fwd_f32_d64(const float* q, const int64_t q_strides[3], const float* k,
-                    const int64_t k_strides[3], const float* v, const int64_t v_strides[3],
-                    float* o, float* lse, int64_t batch, int64_t heads, int64_t seq,
-                    int64_t head_dim, float scale, int causal, void* stream) {
+int fwd_impl(const float* q, const int64_t q_strides[3], const float* k,
+             const int64_t k_strides[3], const float* v, const int64_t v_strides[3], float* o,
+             float* lse, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, float scale,
+             int causal, void* stream, bool any_dim) {
   bool empty = false;
-  int st = check_dims(batch, heads, seq, head_dim, &empty);
+  int st = check_dims(batch, heads, seq, head_dim, any_dim, &empty);
   if (st != CFA_OK || empty) return st;
   if (!q || !k || !v || !o || !lse || !q_strides || !k_strides || !v_strides) return CFA_ERR_NULL;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return CFA_ERR_ALIGNMENT;
   if (!strides_ok(q_strides) || !strides_ok(k_strides) || !strides_ok(v_strides))
     return CFA_ERR_ALIGNMENT;
-  st = setup(g_fwd_once, cfa::setup_fwd_attributes);
+  const bool d64 = head_dim == 64;
+  st = d64 ? setup(g_fwd_once, cfa::setup_fwd_attributes) : setup(g_hd_once, cfa::setup_hd_attributes);
   if (st != CFA_OK) return st;
 
   FwdArgs a;
@@ -112,29 +97,21 @@ int cfa_fwd_f32_d64(const float* q, const int64_t q_strides[3], const float* k,
   a.H = static_cast<int>(heads);
   a.S = static_cast<int>(seq);
   a.scale = scale;
-  a.n_qtiles = static_cast<int>((seq + cfa::FWD_BM - 1) / cfa::FWD_BM);
-  const cudaError_t e = cfa::launch_fwd(a, causal != 0, static_cast<cudaStream_t>(stream));
+  const int bm = d64 ? cfa::FWD_BM : cfa::hd_fwd_bm(static_cast<int>(head_dim));
+  a.n_qtiles = static_cast<int>((seq + bm - 1) / bm);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const cudaError_t e = d64 ? cfa::launch_fwd(a, causal != 0, s)
+                            : cfa::launch_hd_fwd(a, static_cast<int>(head_dim), causal != 0, s);
   return e == cudaSuccess ? CFA_OK : CFA_ERR_LAUNCH;
 }
 
-size_t cfa_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq) {
-  if (batch <= 0 || heads <= 0 || seq <= 0) return 256;
-  return cfa::bwd_workspace_layout(batch, heads, seq).total;
-}
-
-size_t cfa_bwd_workspace_bytes_fast(int64_t batch, int64_t heads, int64_t seq) {
-  if (batch <= 0 || heads <= 0 || seq <= 0) return 256;
-  return cfa::bwd_workspace_layout(batch, heads, seq).total_fast;
-}
-
-int cfa_bwd_f32_d64(const float* q, const int64_t q_strides[3], const float* k,
-                    const int64_t k_strides[3], const float* v, const int64_t v_strides[3],
-                    const float* o, const float* lse, const float* d_o,
-                    const int64_t do_strides[3], float* dqkv, void* workspace,
-                    size_t workspace_bytes, int64_t batch, int64_t heads, int64_t seq,
-                    int64_t head_dim, float scale, int causal, void* stream) {
+int bwd_impl(const float* q, const int64_t q_strides[3], const float* k,
+             const int64_t k_strides[3], const float* v, const int64_t v_strides[3],
+             const float* o, const float* lse, const float* d_o, const int64_t do_strides[3],
+             float* dqkv, void* workspace, size_t workspace_bytes, int64_t batch, int64_t heads,
+             int64_t seq, int64_t head_dim, float scale, int causal, void* stream, bool any_dim) {
   bool empty = false;
-  int st = check_dims(batch, heads, seq, head_dim, &empty);
+  int st = check_dims(batch, heads, seq, head_dim, any_dim, &empty);
   if (st != CFA_OK || empty) return st;
   if (!q || !k || !v || !o || !lse || !d_o || !dqkv || !workspace || !q_strides || !k_strides ||
       !v_strides || !do_strides)
@@ -145,10 +122,11 @@ int cfa_bwd_f32_d64(const float* q, const int64_t q_strides[3], const float* k,
   if (!strides_ok(q_strides) || !strides_ok(k_strides) || !strides_ok(v_strides) ||
       !strides_ok(do_strides))
     return CFA_ERR_ALIGNMENT;
-  const cfa::BwdWorkspace lay = cfa::bwd_workspace_layout(batch, heads, seq);
+  const cfa::BwdWorkspace lay = cfa::bwd_workspace_layout(batch, heads, seq, head_dim);
   if (workspace_bytes < lay.total || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return CFA_ERR_WORKSPACE;
-  st = setup(g_bwd_once, cfa::setup_bwd_attributes);
+  const bool d64 = head_dim == 64;
+  st = d64 ? setup(g_bwd_once, cfa::setup_bwd_attributes) : setup(g_hd_once, cfa::setup_hd_attributes);
   if (st != CFA_OK) return st;
 
   char* ws = static_cast<char*>(workspace);
@@ -173,7 +151,8 @@ int cfa_bwd_f32_d64(const float* q, const int64_t q_strides[3], const float* k,
   p.B = static_cast<int>(batch);
   p.H = static_cast<int>(heads);
   p.S = static_cast<int>(seq);
-  cudaError_t e = cfa::launch_bwd_prep(p, s);
+  cudaError_t e = d64 ? cfa::launch_bwd_prep(p, s)
+                      : cfa::launch_hd_bwd_prep(p, static_cast<int>(head_dim), s);
   if (e != cudaSuccess) return CFA_ERR_LAUNCH;
 
   BwdArgs a;
@@ -210,8 +189,91 @@ int cfa_bwd_f32_d64(const float* q, const int64_t q_strides[3], const float* k,
   a.dq_part = (lay.total_fast > lay.total && workspace_bytes >= lay.total_fast)
                   ? reinterpret_cast<float*>(ws + lay.part_off)
                   : nullptr;
-  e = cfa::launch_bwd(a, causal != 0, s);
+  e = d64 ? cfa::launch_bwd(a, causal != 0, s)
+          : cfa::launch_hd_bwd(a, static_cast<int>(head_dim), causal != 0, s);
   return e == cudaSuccess ? CFA_OK : CFA_ERR_LAUNCH;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cfa_abi_version(void) { return (1 << 16) | 1; }
+
+const char* cfa_strerror(int status) {
+  switch (status) {
+    case CFA_OK: return "fused_attention: ok";
+    case CFA_ERR_HEAD_DIM:
+      return "fused_attention: the CUDA kernels take head_dim 64 (cfa_*_f32: 32, 64 or 128)";
+    case CFA_ERR_ALIGNMENT: return "fused_attention: rows must be 16-byte aligned";
+    case CFA_ERR_SHAPE: return "fused_attention: negative dimension";
+    case CFA_ERR_OVERFLOW: return "fused_attention: problem size exceeds the kernels' index range";
+    case CFA_ERR_NULL: return "fused_attention: null pointer";
+    case CFA_ERR_WORKSPACE: return "fused_attention: workspace too small or misaligned";
+    case CFA_ERR_LAUNCH: return "fused_attention: kernel launch failed";
+    case CFA_ERR_TIMEOUT: return "fused_attention: a bounded device wait expired (results invalid)";
+    case CFA_ERR_CUDA: return "fused_attention: CUDA runtime error";
+    default: return "fused_attention: unknown status";
+  }
+}
+
+int cfa_fwd_f32_d64(const float* q, const int64_t q_strides[3], const float* k,
+                    const int64_t k_strides[3], const float* v, const int64_t v_strides[3],
+                    float* o, float* lse, int64_t batch, int64_t heads, int64_t seq,
+                    int64_t head_dim, float scale, int causal, void* stream) {
+  return fwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, batch, heads, seq, head_dim,
+                  scale, causal, stream, false);
+}
+
+int cfa_fwd_f32(const float* q, const int64_t q_strides[3], const float* k,
+                const int64_t k_strides[3], const float* v, const int64_t v_strides[3], float* o,
+                float* lse, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                float scale, int causal, void* stream) {
+  return fwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, batch, heads, seq, head_dim,
+                  scale, causal, stream, true);
+}
+
+size_t cfa_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq) {
+  if (batch <= 0 || heads <= 0 || seq <= 0) return 256;
+  return cfa::bwd_workspace_layout(batch, heads, seq).total;
+}
+
+size_t cfa_bwd_workspace_bytes_fast(int64_t batch, int64_t heads, int64_t seq) {
+  if (batch <= 0 || heads <= 0 || seq <= 0) return 256;
+  return cfa::bwd_workspace_layout(batch, heads, seq).total_fast;
+}
+
+size_t cfa_bwd_workspace_bytes_hd(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim) {
+  if (batch <= 0 || heads <= 0 || seq <= 0 || !head_dim_ok(head_dim, true)) return 256;
+  return cfa::bwd_workspace_layout(batch, heads, seq, head_dim).total;
+}
+
+size_t cfa_bwd_workspace_bytes_fast_hd(int64_t batch, int64_t heads, int64_t seq,
+                                       int64_t head_dim) {
+  if (batch <= 0 || heads <= 0 || seq <= 0 || !head_dim_ok(head_dim, true)) return 256;
+  return cfa::bwd_workspace_layout(batch, heads, seq, head_dim).total_fast;
+}
+
+int cfa_bwd_f32_d64(const float* q, const int64_t q_strides[3], const float* k,
+                    const int64_t k_strides[3], const float* v, const int64_t v_strides[3],
+                    const float* o, const float* lse, const float* d_o,
+                    const int64_t do_strides[3], float* dqkv, void* workspace,
+                    size_t workspace_bytes, int64_t batch, int64_t heads, int64_t seq,
+                    int64_t head_dim, float scale, int causal, void* stream) {
+  return bwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, d_o, do_strides, dqkv,
+                  workspace, workspace_bytes, batch, heads, seq, head_dim, scale, causal, stream,
+                  false);
+}
+
+int cfa_bwd_f32(const float* q, const int64_t q_strides[3], const float* k,
+                const int64_t k_strides[3], const float* v, const int64_t v_strides[3],
+                const float* o, const float* lse, const float* d_o, const int64_t do_strides[3],
+                float* dqkv, void* workspace, size_t workspace_bytes, int64_t batch,
+                int64_t heads, int64_t seq, int64_t head_dim, float scale, int causal,
+                void* stream) {
+  return bwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, d_o, do_strides, dqkv,
+                  workspace, workspace_bytes, batch, heads, seq, head_dim, scale, causal, stream,
+                  true);
 }
 
 int cfa_selftest_bounded_wait(void* workspace, int64_t timeout_ns, int blocks, void* stream) {

@@ -58,7 +58,7 @@ struct BwdArgs {
   int* turn;      // turn chain: [B * H * n_qtiles]; no-wait path: arrival counter per (b, h)
   int* ticket;
   int* err;
-  float* dq_part; // no-wait path: [B * H][n_kblocks][S][64] dQ partials; nullptr: turn chain
+  float* dq_part; // no-wait path: [B * H][n_kblocks][S][D] dQ partials; nullptr: turn chain
   int64_t q_sb, q_sh, q_ss;
   int64_t k_sb, k_sh, k_ss;
   int64_t v_sb, v_sh, v_ss;
@@ -86,13 +86,14 @@ struct BwdWorkspace {
   size_t turn_off;    // int turn[B * H * n_qtiles]
   size_t dsum_off;    // float D[B * H * S]
   size_t total;       // bytes of the turn-chain layout
-  size_t part_off;    // float partials[B * H * n_kblocks * S * 64] (no-wait dQ path)
+  size_t part_off;    // float partials[B * H * n_kblocks * S * D] (no-wait dQ path)
   size_t total_fast;  // bytes with the partials (== total when the path does not apply)
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-inline BwdWorkspace bwd_workspace_layout(int64_t B, int64_t H, int64_t S) {
+// D: the head dim (the partials hold D floats per row); the layout is otherwise independent of it.
+inline BwdWorkspace bwd_workspace_layout(int64_t B, int64_t H, int64_t S, int64_t D = 64) {
   BwdWorkspace w;
   const int64_t nqt = (S + BWD_BM - 1) / BWD_BM;
   w.ticket_off = 0;
@@ -102,7 +103,7 @@ inline BwdWorkspace bwd_workspace_layout(int64_t B, int64_t H, int64_t S) {
   const int64_t nkb = (S + BWD_BN - 1) / BWD_BN;
   w.part_off = w.total;
   w.total_fast = nkb <= PART_MAX_KBLOCKS
-                     ? w.total + static_cast<size_t>(nkb * B * H * S) * 64 * sizeof(float)
+                     ? w.total + static_cast<size_t>(nkb * B * H * S) * D * sizeof(float)
                      : w.total;
   return w;
 }
@@ -114,6 +115,15 @@ size_t bwd_smem_bytes();
 cudaError_t launch_fwd(const FwdArgs& a, int causal, cudaStream_t stream);
 cudaError_t launch_bwd_prep(const PrepArgs& a, cudaStream_t stream);
 cudaError_t launch_bwd(const BwdArgs& a, int causal, cudaStream_t stream);
+
+// Head dims 32 and 128 (csrc/hd_ffma.cu): the forward's query tile (64 or 32), the attribute
+// set-up and the launchers; the backward uses the same 64-key blocks and 64-query tiles as head
+// dim 64, so BwdArgs, PrepArgs and the workspace layout carry over.
+int hd_fwd_bm(int head_dim);
+cudaError_t setup_hd_attributes();
+cudaError_t launch_hd_fwd(const FwdArgs& a, int head_dim, int causal, cudaStream_t stream);
+cudaError_t launch_hd_bwd_prep(const PrepArgs& a, int head_dim, cudaStream_t stream);
+cudaError_t launch_hd_bwd(const BwdArgs& a, int head_dim, int causal, cudaStream_t stream);
 
 // The failure-detection self-test (cfa_selftest_bounded_wait).
 cudaError_t launch_selftest_wait(int* ws, uint64_t short_ns, int blocks, cudaStream_t stream);

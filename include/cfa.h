@@ -18,6 +18,10 @@
  *                                        bounded waits of the backward set (the reference spins
  *                                        without a bound, kernels/fused_attn.cu:161-170)
  *   cfa_strerror               replaces  the `Error::Msg` strings of src/cuda.rs:69-93
+ *   cfa_fwd_f32, cfa_bwd_f32,  extend     the above to head dims 32 and 128, which the
+ *   cfa_bwd_workspace_bytes*_hd            reference's CUDA path rejects (src/cuda.rs:85-93) and
+ *                                          lists as later work (ROADMAP.md "head_dim 32 and 128");
+ *                                          its CPU path (src/lib.rs:241-299) takes any head dim
  *
  * Conventions (the reference's, src/cuda.rs:60-67 and src/lib.rs:165-188):
  *  - Every pointer is a device pointer at the operand's first element, on the current device.
@@ -97,6 +101,32 @@ int cfa_bwd_f32_d64(const float* q, const int64_t q_strides[3],
                     int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                     float scale, int causal, void* stream);
 
+/* Head dims 32, 64 and 128 (no counterpart in the reference's CUDA path, which takes 64 only).
+ * The same arguments, layouts (with 64 replaced by head_dim), orders of summation and results as
+ * the _d64 entry points; for head_dim 64 they ARE those entry points. Any other head_dim returns
+ * CFA_ERR_HEAD_DIM. Workspace sizes take the head dim because the dQ partials hold head_dim floats
+ * per row (the rest of the workspace does not depend on it). */
+int cfa_fwd_f32(const float* q, const int64_t q_strides[3],
+                const float* k, const int64_t k_strides[3],
+                const float* v, const int64_t v_strides[3],
+                float* o, float* lse,
+                int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                float scale, int causal, void* stream);
+
+size_t cfa_bwd_workspace_bytes_hd(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim);
+
+size_t cfa_bwd_workspace_bytes_fast_hd(int64_t batch, int64_t heads, int64_t seq,
+                                       int64_t head_dim);
+
+int cfa_bwd_f32(const float* q, const int64_t q_strides[3],
+                const float* k, const int64_t k_strides[3],
+                const float* v, const int64_t v_strides[3],
+                const float* o, const float* lse,
+                const float* d_o, const int64_t do_strides[3],
+                float* dqkv, void* workspace, size_t workspace_bytes,
+                int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                float scale, int causal, void* stream);
+
 /* Size of the static scratch of cfa_bwd_f32_d64_noalloc (4 MiB per GPU that loads the library). */
 #define CFA_NOALLOC_SCRATCH_BYTES (4u << 20)
 
@@ -136,7 +166,7 @@ int cfa_selftest_bounded_wait(void* workspace, int64_t timeout_ns, int blocks, v
 /* A static description of a status code. */
 const char* cfa_strerror(int status);
 
-/* ABI version: (major << 16) | minor. */
+/* ABI version: (major << 16) | minor (1.1: the head-dim-generic entry points). */
 int cfa_abi_version(void);
 
 #ifdef __cplusplus

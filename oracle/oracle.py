@@ -156,11 +156,12 @@ def closed_form_inputs(b, s, h, d):
     return x.reshape(b, s, 3 * h * d), w.reshape(b, s, h * d)
 
 
-def seeded_inputs(b, h, s, seed, qkv_scale=1.0):
-    """bench/compare.py:496-503: torch.Generator seeded, qkv [b, s, 3*h*64] then dout [b, s, h*64],
-    N(0, 1), drawn on the CPU; qkv optionally scaled (the canvas config uses 0.5)."""
+def seeded_inputs(b, h, s, seed, qkv_scale=1.0, d=64):
+    """bench/compare.py:496-503: torch.Generator seeded, qkv [b, s, 3*h*d] then dout [b, s, h*d],
+    N(0, 1), drawn on the CPU; qkv optionally scaled (the canvas config uses 0.5). The reference
+    draws head dim 64; d is this build's extension to the head dims 32 and 128."""
     g = torch.Generator().manual_seed(seed)
-    hd = h * 64
+    hd = h * d
     qkv = torch.randn(b, s, 3 * hd, generator=g)
     dout = torch.randn(b, s, hd, generator=g)
     if qkv_scale != 1.0:

@@ -60,6 +60,22 @@ def test_workspace_formula():
     assert _abi.bwd_workspace_bytes_fast(1, 1, 1025) == _abi.bwd_workspace_bytes(1, 1, 1025)
 
 
+def test_workspace_formula_head_dims():
+    """The head-dim-generic sizes: the same layout, the dQ partials holding head_dim floats a row;
+    unsupported head dims get the minimal size (their calls return CFA_ERR_HEAD_DIM)."""
+    b, h, s = 64, 6, 240
+    assert _abi.bwd_workspace_bytes_hd(b, h, s, 64) == _abi.bwd_workspace_bytes(b, h, s)
+    assert _abi.bwd_workspace_bytes_fast_hd(b, h, s, 64) == _abi.bwd_workspace_bytes_fast(b, h, s)
+    base = _abi.bwd_workspace_bytes(b, h, s)
+    part64 = _abi.bwd_workspace_bytes_fast(b, h, s) - base
+    for d in (32, 128):
+        assert _abi.bwd_workspace_bytes_hd(b, h, s, d) == base
+        assert _abi.bwd_workspace_bytes_fast_hd(b, h, s, d) - base == part64 * d // 64
+    for d in (0, 16, 48, 256):
+        assert _abi.bwd_workspace_bytes_hd(b, h, s, d) == 256
+        assert _abi.bwd_workspace_bytes_fast_hd(b, h, s, d) == 256
+
+
 FAKE = 1 << 20  # a 16-byte aligned non-null "device pointer" never dereferenced by these checks
 
 
@@ -69,8 +85,23 @@ def fwd(ptrs=(FAKE,) * 5, strides=((64 * 240, 64, 64),) * 3, dims=(2, 3, 240, 64
 
 
 def test_rejects_head_dim():
+    # the _d64 entry points keep the reference's gate (src/cuda.rs:85-93)
     assert fwd(dims=(2, 3, 240, 32)) == _abi.CFA_ERR_HEAD_DIM
     assert fwd(dims=(2, 3, 240, 128)) == _abi.CFA_ERR_HEAD_DIM
+
+
+def test_generic_entry_points_reject_other_head_dims():
+    """cfa_fwd_f32 / cfa_bwd_f32 take 32, 64 and 128; anything else fails before any device work
+    (empty problems included, as the _d64 ones do for head dims other than 64)."""
+    for d in (0, 16, 48, 96, 256):
+        st = (64 * 240, d, d)
+        assert _abi.fwd_hd(FAKE, st, FAKE, st, FAKE, st, FAKE, FAKE, 2, 3, 240, d, 0.1, 0,
+                           None) == _abi.CFA_ERR_HEAD_DIM
+        assert _abi.bwd_hd(FAKE, st, FAKE, st, FAKE, st, FAKE, FAKE, FAKE, st, FAKE, FAKE, 1 << 30,
+                           2, 3, 240, d, 0.1, 0, None) == _abi.CFA_ERR_HEAD_DIM
+    for d in (32, 128):  # empty problems are fine for the supported head dims, no launch
+        st = (0, 0, 0)
+        assert _abi.fwd_hd(0, st, 0, st, 0, st, 0, 0, 0, 3, 240, d, 0.1, 0, None) == _abi.CFA_OK
 
 
 def test_empty_problem_is_ok_and_launches_nothing():
