@@ -168,35 +168,39 @@ class OursStep:
 
 
 class OursViews:
-    """Forward + backward through the C ABI on [b, h, s, 64] views q, k, v and dO."""
+    """Forward + backward through the C ABI on [b, h, s, d] views q, k, v and dO (head dim 64 via
+    the _d64 entry points, 32 and 128 via the generic ones; scale 1/sqrt(d))."""
 
     def __init__(self, q, k, v, d_o, causal):
         from candle_fused_attn import _abi
         self.abi = _abi
-        b, h, s, _ = q.shape
-        self.dims = (b, h, s, 64)
+        b, h, s, d = q.shape
+        self.dims = (b, h, s, d)
+        self.scale = SCALE if d == 64 else d ** -0.5
+        self.fwd_fn = _abi.fwd if d == 64 else _abi.fwd_hd
+        self.bwd_fn = _abi.bwd if d == 64 else _abi.bwd_hd
         self.q, self.k, self.v, self.d_o, self.causal = q, k, v, d_o, causal
         dev = q.device
-        self.o = torch.empty(b, s, h, 64, device=dev)
+        self.o = torch.empty(b, s, h, d, device=dev)
         self.lse = torch.empty(b, h, s, device=dev)
-        self.dqkv = torch.empty(b, s, 3, h, 64, device=dev)
-        self.ws_bytes = _abi.bwd_workspace_bytes_fast(b, h, s)
+        self.dqkv = torch.empty(b, s, 3, h, d, device=dev)
+        self.ws_bytes = _abi.bwd_workspace_bytes_fast_hd(b, h, s, d)
         self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
 
     def forward(self, stream):
         st = [t.stride()[:3] for t in (self.q, self.k, self.v)]
-        rc = self.abi.fwd(self.q.data_ptr(), st[0], self.k.data_ptr(), st[1], self.v.data_ptr(),
-                          st[2], self.o.data_ptr(), self.lse.data_ptr(), *self.dims, SCALE,
-                          self.causal, stream)
+        rc = self.fwd_fn(self.q.data_ptr(), st[0], self.k.data_ptr(), st[1], self.v.data_ptr(),
+                         st[2], self.o.data_ptr(), self.lse.data_ptr(), *self.dims, self.scale,
+                         self.causal, stream)
         if rc:
             raise RuntimeError(self.abi.strerror(rc))
 
     def backward(self, d_o, stream):
         st = [t.stride()[:3] for t in (self.q, self.k, self.v)]
-        rc = self.abi.bwd(self.q.data_ptr(), st[0], self.k.data_ptr(), st[1], self.v.data_ptr(),
-                          st[2], self.o.data_ptr(), self.lse.data_ptr(), d_o.data_ptr(),
-                          d_o.stride()[:3], self.dqkv.data_ptr(), self.ws.data_ptr(),
-                          self.ws_bytes, *self.dims, SCALE, self.causal, stream)
+        rc = self.bwd_fn(self.q.data_ptr(), st[0], self.k.data_ptr(), st[1], self.v.data_ptr(),
+                         st[2], self.o.data_ptr(), self.lse.data_ptr(), d_o.data_ptr(),
+                         d_o.stride()[:3], self.dqkv.data_ptr(), self.ws.data_ptr(),
+                         self.ws_bytes, *self.dims, self.scale, self.causal, stream)
         if rc:
             raise RuntimeError(self.abi.strerror(rc))
 
@@ -212,18 +216,18 @@ def suite(args):
     sh = stream.cuda_stream
     pk = peaks()
 
-    def views_qkv(b, h, s, causal, seed, qscale):
-        qkv, dout = oracle.seeded_inputs(b, h, s, seed, qscale)
+    def views_qkv(b, h, s, d, causal, seed, qscale):
+        qkv, dout = oracle.seeded_inputs(b, h, s, seed, qscale, d=d)
         x, g = qkv.to(dev), dout.to(dev)
         q, k, v = oracle.qkv_views(x, h)
         return q, k, v, oracle.heads_view(g, h)
 
-    def views_general(b, h, s, causal, seed, _):
+    def views_general(b, h, s, d, causal, seed, _):
         gen = torch.Generator().manual_seed(seed)
         q, k, v, d_o = (torch.randn(b, h, s, 64, generator=gen).to(dev) for _ in range(4))
         return q, k, v, d_o
 
-    def views_strided(b, h, s, causal, seed, _):
+    def views_strided(b, h, s, d, causal, seed, _):
         gen = torch.Generator().manual_seed(seed)
         x = torch.randn(b, s, 3, h, 64, generator=gen).to(dev)
         d_o = torch.randn(b, h, s, 64, generator=gen).to(dev)
@@ -231,17 +235,23 @@ def suite(args):
         return q, k, v, d_o
 
     configs = [
-        ("general [2,4,128,64] contiguous", 2, 4, 128, False, views_general, 1.0),
-        ("canvas qkv [64,240,1152]", 64, 6, 240, False, views_qkv, 0.5),
-        ("strided views of [16,1024,3,12,64], causal", 16, 12, 1024, True, views_strided, 1.0),
-        ("long qkv [4,8192,3072], causal", 4, 16, 8192, True, views_qkv, 0.5),
+        ("general [2,4,128,64] contiguous", 2, 4, 128, 64, False, views_general, 1.0),
+        ("canvas qkv [64,240,1152]", 64, 6, 240, 64, False, views_qkv, 0.5),
+        ("strided views of [16,1024,3,12,64], causal", 16, 12, 1024, 64, True, views_strided, 1.0),
+        ("long qkv [4,8192,3072], causal", 4, 16, 8192, 64, True, views_qkv, 0.5),
+        # head dims 32 and 128: this build's extension (the reference kernel takes 64 only)
+        ("canvas-shaped qkv [64,240,1152], 12 heads of 32", 64, 12, 240, 32, False, views_qkv, 0.5),
+        ("canvas-shaped qkv [64,240,1152], 3 heads of 128", 64, 3, 240, 128, False, views_qkv, 0.5),
+        ("long qkv [4,8192,3072], 8 heads of 128, causal", 4, 8, 8192, 128, True, views_qkv, 0.5),
     ]
-    for name, b, h, s, causal, make, qscale in configs:
-        q, k, v, d_o = make(b, h, s, causal, 0, qscale)
+    if args.only:
+        configs = [c for c in configs if args.only in c[0]]
+    for name, b, h, s, d, causal, make, qscale in configs:
+        q, k, v, d_o = make(b, h, s, d, causal, 0, qscale)
         impls = {"ours": OursViews(q, k, v, d_o, causal),
                  "reference_kernel": ref_kernel.RefAttention(q, k, v, SCALE, causal)
-                 if ref_kernel.available() else None}
-        f_fwd, f_all = flops(b, h, s, 64, causal, "fwd"), flops(b, h, s, 64, causal)
+                 if ref_kernel.available() and d == 64 else None}
+        f_fwd, f_all = flops(b, h, s, d, causal, "fwd"), flops(b, h, s, d, causal)
         steps = max(3, min(args.steps, int(2e11 // f_all) + 1))
         res = {}
         for _ in range(args.warmup):
@@ -265,7 +275,7 @@ def suite(args):
             res[n] = {"fwd_ms": fm, "fwdbwd_ms": am,
                       "fwd_tflops": f_fwd / fm / 1e9, "fwdbwd_tflops": f_all / am / 1e9,
                       "fwdbwd_frac_ffma": f_all / am / 1e9 / pk["ffma_tflops"]}
-        line = {"suite": name, "b": b, "h": h, "s": s, "causal": causal, "steps": steps,
+        line = {"suite": name, "b": b, "h": h, "s": s, "d": d, "causal": causal, "steps": steps,
                 "gflop_fwd": f_fwd / 1e9, "gflop_fwdbwd": f_all / 1e9, **res}
         if res.get("reference_kernel"):
             line["speedup_fwdbwd"] = res["reference_kernel"]["fwdbwd_ms"] / res["ours"]["fwdbwd_ms"]
@@ -338,6 +348,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-ref-kernel", action="store_true")
+    ap.add_argument("--only", default="", help="suite: run the configs whose name contains this")
     ap.add_argument("--mode", choices=["full", "kernels", "suite"], default="full",
                     help="kernels: warm-up + `steps` plain steps, no timing (for ncu); "
                          "suite: every BASELINE config, ours vs the reference kernel")
