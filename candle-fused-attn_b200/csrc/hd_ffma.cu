@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(FWD_THREADS, Hd<D>::FWD_MINB) hd_fwd_kernel(co
 
     // O += P V over the live key groups, keys in order (groups past the end hold P = 0).
     const int jlim = 16 * jn;
-#pragma unroll 2
+#pragma unroll 8
     for (int j = 0; j < jlim; j += 4) {
       uint64_t vv[4][NP];
       float4 pv[RPT];
@@ -479,7 +479,7 @@ __global__ void __launch_bounds__(Bwd<D>::NT, 256 / (Bwd<D>::NT / 2)) hd_bwd_ker
       const float* Xs = grp ? dSs : Ps;
       const float* Ys = grp ? Qs : dOs;
       const int iw = k0 + kb2 - K2 * ty >= S ? 0 : iq;  // all this warp's keys past the end
-#pragma unroll 4
+#pragma unroll 8
       for (int i = 0; i < iw; ++i) {
         uint64_t xp[K2 / 2];
         if constexpr (K2 == 8) {
