@@ -1,0 +1,321 @@
+// SPDX-License-Identifier: MIT OR Apache-2.0
+//
+// The C++ host layer (candle-fused-attn_b200/host, libcfa_host.so) against the CPU oracle: the
+// reference's tests/parity.rs, test for test, in C++ -- `cuda_matches_cpu` (:210-221, band 5e-6
+// max-abs, both public functions, causal and not), `cuda_backward_is_deterministic` (:226-242, 8
+// reruns compared bit for bit), `outputs_are_merge_heads_ready` (:169-183),
+// `backward_twice_over_one_graph` (:185-204) -- plus the layout checks and error messages of
+// src/lib.rs. The oracle (oracle/liboracle.so, the crate's composed CPU path restated) is the
+// checker only.
+//
+//   parity_host               every test (needs a GPU)
+//   parity_host --host-only   the layout / geometry / error tests that touch no device
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <string>
+#include <vector>
+
+#include "candle_fused_attn.hpp"
+
+extern "C" {
+void oracle_fwd_f32(const float* q, const int64_t* qs, const float* k, const int64_t* ks,
+                    const float* v, const int64_t* vs, int64_t B, int64_t H, int64_t S, int64_t D,
+                    double scale, int causal, float* o, float* lse, int threads, int64_t bh_begin,
+                    int64_t bh_end);
+void oracle_bwd_f32(const float* q, const int64_t* qs, const float* k, const int64_t* ks,
+                    const float* v, const int64_t* vs, const float* o, const float* lse,
+                    const float* dout, const int64_t* dos, int64_t B, int64_t H, int64_t S,
+                    int64_t D, double scale, int causal, float* dqkv, int threads,
+                    int64_t bh_begin, int64_t bh_end);
+}
+
+namespace cfa = candle_fused_attn;
+using cfa::Layout;
+using cfa::Tensor;
+
+namespace {
+
+int g_failures = 0;
+
+#define EXPECT(cond, ...)                                      \
+  do {                                                         \
+    if (!(cond)) {                                             \
+      std::fprintf(stderr, "  FAILED %s:%d: ", __FILE__, __LINE__); \
+      std::fprintf(stderr, __VA_ARGS__);                       \
+      std::fprintf(stderr, "\n");                              \
+      ++g_failures;                                            \
+    }                                                          \
+  } while (0)
+
+template <typename Fn>
+void expect_error(Fn fn, const char* needle, const char* what) {
+  try {
+    fn();
+    EXPECT(false, "%s: no error", what);
+  } catch (const cfa::Error& e) {
+    EXPECT(std::strstr(e.what(), needle) != nullptr, "%s: message '%s' lacks '%s'", what,
+           e.what(), needle);
+  }
+}
+
+// tests/parity.rs:126-138: the projection x_i = sin(i * 0.618034) * 1.5 and the loss weights
+// (= dO) w_i = cos(i * 0.414213), in f32.
+void inputs(size_t b, size_t s, size_t h, size_t d, std::vector<float>& x, std::vector<float>& w) {
+  x.resize(b * s * 3 * h * d);
+  w.resize(b * s * h * d);
+  for (size_t i = 0; i < x.size(); ++i) x[i] = std::sin(static_cast<float>(i) * 0.618034f) * 1.5f;
+  for (size_t i = 0; i < w.size(); ++i) w[i] = std::cos(static_cast<float>(i) * 0.414213f);
+}
+
+// The oracle on the same projection: O [b, s, h*d] and dqkv [b, s, 3*h*d].
+void oracle(size_t b, size_t s, size_t h, size_t d, bool causal, const std::vector<float>& x,
+            const std::vector<float>& w, std::vector<float>& o, std::vector<float>& g) {
+  const int64_t hd = static_cast<int64_t>(h * d);
+  const int64_t st[3] = {static_cast<int64_t>(s) * 3 * hd, static_cast<int64_t>(d), 3 * hd};
+  const int64_t dst[3] = {static_cast<int64_t>(s) * hd, static_cast<int64_t>(d), hd};
+  std::vector<float> lse(b * h * s);
+  o.resize(b * s * h * d);
+  g.resize(b * s * 3 * h * d);
+  const double scale = 1.0 / std::sqrt(static_cast<double>(d));
+  const int64_t B = b, H = h, S = s, D = d;
+  oracle_fwd_f32(x.data(), st, x.data() + hd, st, x.data() + 2 * hd, st, B, H, S, D,
+                 static_cast<float>(scale), causal, o.data(), lse.data(), 0, 0, B * H);
+  oracle_bwd_f32(x.data(), st, x.data() + hd, st, x.data() + 2 * hd, st, o.data(), lse.data(),
+                 w.data(), dst, B, H, S, D, static_cast<float>(scale), causal, g.data(), 0, 0,
+                 B * H);
+}
+
+float max_abs(const std::vector<float>& a, const std::vector<float>& b) {
+  float m = 0.0f;
+  for (size_t i = 0; i < a.size(); ++i) m = std::fmax(m, std::fabs(a[i] - b[i]));
+  return m;
+}
+
+enum class Path { Fused, FusedQkv };
+
+// tests/parity.rs:78-123: out [b, s, h*d] and d(sum(out * w))/d(qkv) through one public function.
+void attend(Path path, const std::vector<float>& x, const std::vector<float>& w, size_t b,
+            size_t s, size_t h, size_t d, bool causal, std::vector<float>& o,
+            std::vector<float>& g) {
+  const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(d)));
+  const Tensor qkv = Tensor::from_host(x, {b, s, 3 * h * d});
+  const Tensor dout = Tensor::from_host(w, {b, s, h * d});
+  if (path == Path::FusedQkv) {
+    const cfa::QkvAttention r = cfa::fused_attention_qkv(qkv, h, scale, causal);
+    o = r.out.to_host();
+    g = r.backward(dout).to_host();
+    return;
+  }
+  // The head-split views of tests/parity.rs:40-51: strided [b, h, s, d] views of the projection,
+  // read in place.
+  auto view = [&](size_t i) {
+    Layout l;
+    l.shape = {b, h, s, d};
+    l.stride = {s * 3 * h * d, d, 3 * h * d, 1};
+    l.start_offset = qkv.layout().start_offset + i * h * d;
+    return Tensor::view(qkv, l);
+  };
+  const cfa::Attention r = cfa::fused_attention(view(0), view(1), view(2), scale, causal);
+  o = r.out.transpose(1, 2).reshape({b, s, h * d}).to_host();
+  const auto grads = r.backward(dout.reshape({b, s, h, d}).transpose(1, 2));
+  // dq, dk, dv [b, h, s, d] -> the projection's layout [b, s, 3*h*d]
+  g.assign(b * s * 3 * h * d, 0.0f);
+  for (size_t i = 0; i < 3; ++i) {
+    const std::vector<float> gi = grads[i].transpose(1, 2).reshape({b, s, h * d}).to_host();
+    for (size_t bs = 0; bs < b * s; ++bs)
+      std::memcpy(&g[bs * 3 * h * d + i * h * d], &gi[bs * h * d], h * d * sizeof(float));
+  }
+}
+
+// tests/parity.rs:141-159 / :210-221.
+void check(Path path, size_t b, size_t s, size_t h, size_t d, bool causal, float band) {
+  std::vector<float> x, w, o_ref, g_ref, o, g;
+  inputs(b, s, h, d, x, w);
+  oracle(b, s, h, d, causal, x, w, o_ref, g_ref);
+  attend(path, x, w, b, s, h, d, causal, o, g);
+  const float eo = max_abs(o, o_ref), eg = max_abs(g, g_ref);
+  EXPECT(eo < band && eg < band, "%s (%zu,%zu,%zu,%zu) causal=%d: max-abs O %.2e dqkv %.2e",
+         path == Path::Fused ? "fused" : "fused_qkv", b, s, h, d, causal ? 1 : 0, eo, eg);
+}
+
+// ---- tests ------------------------------------------------------------------------------------
+
+void layout_checks() {
+  Layout l = Layout::contiguous({2, 3, 8, 64});
+  EXPECT(cfa::float4_aligned(l), "contiguous [2,3,8,64] is float4-aligned");
+  l.start_offset = 2;
+  EXPECT(!cfa::float4_aligned(l), "offset 2 is not float4-aligned");
+  Layout t = Layout::contiguous({2, 8, 3, 64});  // [b, s, h, d] seen as [b, h, s, d]
+  std::swap(t.shape[1], t.shape[2]);
+  std::swap(t.stride[1], t.stride[2]);
+  EXPECT(cfa::float4_aligned(t), "a merge-heads transpose view is float4-aligned");
+  const auto st = cfa::bhs_strides(t);
+  EXPECT(st[0] == 8 * 3 * 64 && st[1] == 64 && st[2] == 3 * 64, "bhs_strides of the view");
+  Layout bad = Layout::contiguous({2, 3, 64, 8});
+  std::swap(bad.shape[2], bad.shape[3]);
+  std::swap(bad.stride[2], bad.stride[3]);
+  expect_error([&] { cfa::bhs_strides(bad); }, "d contiguous expected", "bhs_strides");
+}
+
+void geometry_checks() {
+  const cfa::QkvGeometry g = cfa::qkv_geometry(Layout::contiguous({64, 240, 1152}), 6);
+  const auto [b, h, s, d] = g.dims;
+  EXPECT(b == 64 && h == 6 && s == 240 && d == 64, "qkv_geometry dims");
+  EXPECT(g.strides[0] == 240 * 1152 && g.strides[1] == 64 && g.strides[2] == 1152,
+         "qkv_geometry strides");
+  EXPECT(g.offsets[0] == 0 && g.offsets[1] == 384 && g.offsets[2] == 768, "qkv_geometry offsets");
+  expect_error([] { cfa::qkv_geometry(Layout::contiguous({2, 7, 1152}), 0); },
+               "is not 3 x 0 heads", "zero heads");
+  expect_error([] { cfa::qkv_geometry(Layout::contiguous({2, 7, 1000}), 6); },
+               "last dimension 1000 is not 3 x 6 heads", "indivisible last dim");
+  expect_error([] { cfa::qkv_geometry(Layout::contiguous({2, 1152}), 6); }, "rank-3", "rank");
+  Layout tr = Layout::contiguous({2, 1152, 7});
+  std::swap(tr.shape[1], tr.shape[2]);
+  std::swap(tr.stride[1], tr.stride[2]);
+  expect_error([&] { cfa::qkv_geometry(tr, 6); }, "last dimension must be contiguous",
+               "non-contiguous last dim");
+  expect_error(
+      [] {
+        cfa::check_shapes(Layout::contiguous({2, 3, 8, 64}), Layout::contiguous({2, 3, 9, 64}),
+                          Layout::contiguous({2, 3, 8, 64}));
+      },
+      "must share one [b, h, s, d] shape", "check_shapes");
+}
+
+void cuda_matches_cpu() {
+  for (Path p : {Path::Fused, Path::FusedQkv})
+    for (bool causal : {false, true}) {
+      check(p, 2, 7, 3, 64, causal, 5e-6f);
+      check(p, 1, 33, 2, 64, causal, 5e-6f);
+      check(p, 2, 240, 6, 64, causal, 5e-6f);
+    }
+}
+
+void head_dims_match_cpu() {
+  for (size_t d : {32, 128})
+    for (bool causal : {false, true}) {
+      check(Path::FusedQkv, 2, 97, 2, d, causal, 5e-6f);
+      check(Path::Fused, 1, 65, 3, d, causal, 5e-6f);
+    }
+}
+
+// tests/parity.rs:226-242: the backward reruns bit for bit.
+void cuda_backward_is_deterministic() {
+  const size_t b = 2, s = 240, h = 6, d = 64;
+  std::vector<float> x, w, o0, g0, o, g;
+  inputs(b, s, h, d, x, w);
+  attend(Path::FusedQkv, x, w, b, s, h, d, true, o0, g0);
+  for (int r = 0; r < 8; ++r) {
+    attend(Path::FusedQkv, x, w, b, s, h, d, true, o, g);
+    EXPECT(std::memcmp(o.data(), o0.data(), o.size() * 4) == 0 &&
+               std::memcmp(g.data(), g0.data(), g.size() * 4) == 0,
+           "rerun %d differs", r);
+  }
+}
+
+// tests/parity.rs:169-183: fused_attention's output transposed and reshaped is the merged output
+// of fused_attention_qkv on the same projection, bit for bit.
+void outputs_are_merge_heads_ready() {
+  const size_t b = 2, s = 33, h = 3, d = 64;
+  std::vector<float> x, w, o1, g1, o2, g2;
+  inputs(b, s, h, d, x, w);
+  attend(Path::Fused, x, w, b, s, h, d, false, o1, g1);
+  attend(Path::FusedQkv, x, w, b, s, h, d, false, o2, g2);
+  EXPECT(std::memcmp(o1.data(), o2.data(), o1.size() * 4) == 0, "outputs differ");
+  EXPECT(std::memcmp(g1.data(), g2.data(), g1.size() * 4) == 0, "gradients differ");
+}
+
+// tests/parity.rs:185-204: two backward passes over one forward give the same gradients.
+void backward_twice_over_one_graph() {
+  const size_t b = 1, s = 50, h = 2, d = 64;
+  std::vector<float> x, w;
+  inputs(b, s, h, d, x, w);
+  const Tensor qkv = Tensor::from_host(x, {b, s, 3 * h * d});
+  const Tensor dout = Tensor::from_host(w, {b, s, h * d});
+  const cfa::QkvAttention r = cfa::fused_attention_qkv(qkv, h, 0.125f, true);
+  const std::vector<float> g1 = r.backward(dout).to_host(), g2 = r.backward(dout).to_host();
+  EXPECT(std::memcmp(g1.data(), g2.data(), g1.size() * 4) == 0, "second backward differs");
+}
+
+void errors_on_device() {
+  // a head dim the kernels do not take
+  expect_error(
+      [] { cfa::fused_attention_qkv(Tensor::zeros({1, 8, 3 * 2 * 48}), 2, 0.1f, false); },
+      "head_dim", "head_dim 48");
+  // backward before forward (src/lib.rs:310-315)
+  expect_error(
+      [] {
+        cfa::FusedAttentionQkv op(2, 0.1f, false);
+        const Tensor qkv = Tensor::zeros({1, 8, 3 * 2 * 64});
+        op.bwd(qkv, Tensor::zeros({1, 8, 128}), Tensor::zeros({1, 8, 128}));
+      },
+      "backward before forward", "backward before forward");
+  // A contiguous projection at an offset of 2 floats: contiguous() leaves it as it is (candle's
+  // too), so the op refuses it exactly as src/lib.rs:533-538 does.
+  {
+    std::vector<float> x(2 + 1 * 8 * 3 * 2 * 64, 0.5f);
+    const Tensor base = Tensor::from_host(x, {x.size()});
+    const Tensor off2 = Tensor::view(base, Layout::contiguous({1, 8, 3 * 2 * 64}, 2));
+    expect_error([&] { cfa::fused_attention_qkv(off2, 2, 0.125f, false); },
+                 "rows must be 16-byte aligned", "contiguous offset-2 projection");
+  }
+  // Rows the kernels cannot read in place (a row pitch of 3hd + 2 floats) are copied first
+  // (src/lib.rs:111-118): the results match the oracle on the same values.
+  const size_t b = 1, s = 40, h = 2, d = 64, row = 3 * h * d;
+  std::vector<float> x, w, o_ref, g_ref;
+  inputs(b, s, h, d, x, w);
+  oracle(b, s, h, d, false, x, w, o_ref, g_ref);
+  std::vector<float> padded(b * s * (row + 2), 0.0f);
+  for (size_t r = 0; r < b * s; ++r)
+    std::memcpy(&padded[r * (row + 2)], &x[r * row], row * sizeof(float));
+  const Tensor base = Tensor::from_host(padded, {padded.size()});
+  Layout l;
+  l.shape = {b, s, row};
+  l.stride = {s * (row + 2), row + 2, 1};
+  const Tensor qkv = Tensor::view(base, l);
+  const cfa::QkvAttention r = cfa::fused_attention_qkv(qkv, h, 0.125f, false);
+  EXPECT(r.qkv.layout().is_contiguous() && r.qkv.storage() != base.storage(),
+         "the op saw a contiguous copy");
+  const std::vector<float> o = r.out.to_host();
+  const std::vector<float> g = r.backward(Tensor::from_host(w, {b, s, h * d})).to_host();
+  EXPECT(max_abs(o, o_ref) < 5e-6f && max_abs(g, g_ref) < 5e-6f, "padded-row projection");
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  const bool host_only = argc > 1 && std::strcmp(argv[1], "--host-only") == 0;
+  struct Case {
+    const char* name;
+    std::function<void()> fn;
+    bool device;
+  };
+  const Case cases[] = {
+      {"layout_checks", layout_checks, false},
+      {"geometry_checks", geometry_checks, false},
+      {"cuda_matches_cpu", cuda_matches_cpu, true},
+      {"head_dims_match_cpu", head_dims_match_cpu, true},
+      {"cuda_backward_is_deterministic", cuda_backward_is_deterministic, true},
+      {"outputs_are_merge_heads_ready", outputs_are_merge_heads_ready, true},
+      {"backward_twice_over_one_graph", backward_twice_over_one_graph, true},
+      {"errors_on_device", errors_on_device, true},
+  };
+  int ran = 0;
+  for (const Case& c : cases) {
+    if (host_only && c.device) continue;
+    const int before = g_failures;
+    try {
+      c.fn();
+    } catch (const std::exception& e) {
+      std::fprintf(stderr, "  FAILED %s: exception %s\n", c.name, e.what());
+      ++g_failures;
+    }
+    std::printf("%s %s\n", g_failures == before ? "ok  " : "FAIL", c.name);
+    ++ran;
+  }
+  std::printf("%d tests, %d failures\n", ran, g_failures);
+  return g_failures == 0 ? 0 : 1;
+}
