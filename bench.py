@@ -349,6 +349,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-ref-kernel", action="store_true")
     ap.add_argument("--only", default="", help="suite: run the configs whose name contains this")
+    ap.add_argument("--head-dim", type=int, default=D,
+                    help="kernels mode: the canvas-shaped projection as heads of this dim (32, 128)")
     ap.add_argument("--mode", choices=["full", "kernels", "suite"], default="full",
                     help="kernels: warm-up + `steps` plain steps, no timing (for ncu); "
                          "suite: every BASELINE config, ours vs the reference kernel")
@@ -379,6 +381,23 @@ def main():
     b = B_PER_GPU
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
+    if args.mode == "kernels" and args.head_dim != D:
+        # the canvas-shaped projection [64, 240, 1152] as 384 / d heads of d (csrc/hd_ffma.cu)
+        from oracle import oracle
+        d = args.head_dim
+        h = H * D // d
+        views = []
+        for i in range(N_SETS):
+            qkv, dout = oracle.seeded_inputs(b, h, S, 1000 + i, 0.5, d=d)
+            x, g = qkv.to(dev), dout.to(dev)
+            q, k, v = oracle.qkv_views(x, h)
+            views.append(OursViews(q, k, v, oracle.heads_view(g, h), CAUSAL))
+        for i in range(args.warmup + args.steps):
+            vw = views[i % N_SETS]
+            vw.forward(sh)
+            vw.backward(vw.d_o, sh)
+        torch.cuda.synchronize()
+        return
     sets = []
     for i in range(N_SETS):
         qkv, dout = make_inputs(rank * N_SETS + i, b)
