@@ -451,7 +451,7 @@ def main():
     hg = [s.dout.cpu().pin_memory() for s in sets]
     ho = torch.empty(b, S, H * D).pin_memory()
     hd = torch.empty(b, S, 3 * H * D).pin_memory()
-    pipe = HostPipeline(b, H, S, SCALE, CAUSAL, dev, chunks=4, slots=2)
+    pipe = HostPipeline(b, H, S, SCALE, CAUSAL, dev, chunks=1, slots=2)
 
     def e2e_timed(steps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -570,7 +570,8 @@ def main():
                 "h2d_bytes_per_step": (sets[0].qkv.numel() + sets[0].dout.numel()) * 4,
                 "d2h_bytes_per_step": (ho.numel() + hd.numel()) * 4,
                 "path": "candle_fused_attn.HostPipeline (pinned host qkv, dO in; O, dqkv out; "
-                        "4 batch chunks, 2 buffer slots over H2D / kernel / D2H streams)",
+                        "1 chunk per step, 2 buffer slots over H2D / kernel / D2H streams: "
+                        "consecutive steps overlap their copies)",
                 "copy_floor_ms": floor_ms,
                 "copy_floor": "the same bytes copied both ways at once with no kernel, every "
                               "rank concurrently, max over ranks",

@@ -27,14 +27,16 @@ class HostPipeline:
     """fused_attention_qkv forward + backward from host buffers to host buffers.
 
     batch, heads, seq: the problem (qkv [batch, seq, 3*heads*64], dO [batch, seq, heads*64]).
-    chunks: batch chunks per step; slots: device buffer sets in rotation (>= 2 to overlap).
-    Measured on a B200 at the canvas shape (b64 h6 s240): 4 chunks x 2 slots reach 2.18 ms per
-    step against a 2.0 ms floor for moving 94 MB each way over PCIe at once; many more chunks lose
-    to per-chunk host overhead.
+    chunks: batch chunks per step; slots: device buffer sets, rotating over chunks and steps
+    (>= 2 to overlap: the H2D copy of one chunk or step runs during the kernels and the D2H copy of
+    the previous one). Measured on a B200 at the canvas shape (b64 h6 s240), steps back to back:
+    1 chunk x 2 slots 2.11-2.15 ms per step, 2 chunks 2.16 ms, 4 chunks 2.27-2.46 ms, against a
+    1.92-1.95 ms floor for moving 94 MB each way over PCIe at once: once consecutive steps overlap,
+    splitting a step only adds per-chunk overhead and smaller, less efficient kernel launches.
     """
 
     def __init__(self, batch: int, heads: int, seq: int, scale: float, causal: bool,
-                 device: torch.device, chunks: int = 4, slots: int = 2):
+                 device: torch.device, chunks: int = 1, slots: int = 2):
         self.b, self.h, self.s = batch, heads, seq
         self.scale, self.causal = float(scale), bool(causal)
         self.dev = torch.device(device)
@@ -42,7 +44,7 @@ class HostPipeline:
         self.ranges = [shard_range(batch, self.chunks, c) for c in range(self.chunks)]
         cb = max(hi - lo for lo, hi in self.ranges)
         hd = heads * 64
-        n = min(slots, self.chunks)
+        n = max(1, slots)
         f32 = dict(dtype=torch.float32, device=self.dev)
         self.qkv = [torch.empty(cb, seq, 3 * hd, **f32) for _ in range(n)]
         self.dout = [torch.empty(cb, seq, hd, **f32) for _ in range(n)]
@@ -59,6 +61,7 @@ class HostPipeline:
         self.computed = [torch.cuda.Event() for _ in range(n)]
         self.unloaded = [torch.cuda.Event() for _ in range(n)]
         self.used = [False] * n
+        self.next_slot = 0  # slots rotate across chunks and across steps
 
     def _kernels(self, slot: int, b: int) -> None:
         h, s = self.h, self.s
@@ -85,8 +88,9 @@ class HostPipeline:
         waits for the outputs."""
         n = len(self.qkv)
         hd = self.h * 64
-        for c, (lo, hi) in enumerate(self.ranges):
-            slot, b = c % n, hi - lo
+        for lo, hi in self.ranges:
+            slot, b = self.next_slot, hi - lo
+            self.next_slot = (slot + 1) % n
             with torch.cuda.stream(self.h2d):
                 if self.used[slot]:
                     self.h2d.wait_event(self.computed[slot])  # inputs of the slot consumed
