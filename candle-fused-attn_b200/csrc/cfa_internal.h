@@ -12,9 +12,10 @@
 
 namespace cfa {
 
-// The forward's tile: FWD_BM queries per block, FWD_BN keys per step.
-constexpr int FWD_BM = 64;
+// The forward's tile: fwd_tile_rows(seq) queries per block (64 or 48, whichever pads fewer rows;
+// the results do not depend on it), FWD_BN keys per step.
 constexpr int FWD_BN = 64;
+int fwd_tile_rows(int64_t seq);
 constexpr int FWD_THREADS = 128;
 
 // The backward's tile: BWD_BN keys per block (one key block; fixes dQ's summation order, so it
@@ -108,10 +109,9 @@ inline BwdWorkspace bwd_workspace_layout(int64_t B, int64_t H, int64_t S, int64_
   return w;
 }
 
-size_t fwd_smem_bytes();
 size_t bwd_smem_bytes();
 
-// Launchers (return a cudaError_t from the launch).
+// Launchers (return a cudaError_t from the launch). launch_fwd sets the query-tile count itself.
 cudaError_t launch_fwd(const FwdArgs& a, int causal, cudaStream_t stream);
 cudaError_t launch_bwd_prep(const PrepArgs& a, cudaStream_t stream);
 cudaError_t launch_bwd(const BwdArgs& a, int causal, cudaStream_t stream);

@@ -4,16 +4,20 @@
 // online softmax of FlashAttention-2 (Dao 2023), saving only O and the row log-sum-exp L.
 // Replaces fattn_fwd_f32_d64 (kernels/fused_attn.cu:469-598); same inputs, outputs, layouts.
 //
-// Block: FWD_THREADS = 128 threads (4 warps) own FWD_BM = 64 queries of one (batch, head) and walk
-// key tiles of FWD_BN = 64. Warp w owns query rows 16w .. 16w + 15; within it, lane (ty, tx) =
-// (lane / 16, lane % 16) owns rows 16w + ty + 2i (i = 0..7) and
-//   - scores for keys tx + 16jj (jj = 0..3): an 8 x 4 register tile, so the row max / sum of the
+// Block: FWD_THREADS = 128 threads (4 warps) own BM = 8 * RPT queries of one (batch, head) and walk
+// key tiles of FWD_BN = 64; RPT (rows per thread) is 8 (BM = 64) or 6 (BM = 48), whichever leaves
+// fewer padded query rows at the sequence length (fwd_tile_rows). Warp w owns query rows
+// 2 RPT w .. 2 RPT w + 2 RPT - 1; within it, lane (ty, tx) = (lane / 16, lane % 16) owns rows
+// 2 RPT w + ty + 2i (i < RPT) and
+//   - scores for keys tx + 16jj (jj = 0..3): an RPT x 4 register tile, so the row max / sum of the
 //     online softmax is a 16-lane butterfly inside one half-warp;
 //   - output dims 4tx .. 4tx + 3 of the same 8 rows: the rescale by exp(m_old - m_new) and the
 //     final 1 / l never leave the thread.
-// Each k-step of 4 reads 8 float4 of Q and 4 of K from shared memory for 128 FFMA (and the same
-// for P V), against the reference's 8 loads per 16 FFMA: the FFMA pipe, not the shared-memory
-// pipe, is the bound. Three blocks per SM (72.7 KB shared memory each, <= 168 registers).
+// Each k-step of 4 reads RPT float4 of Q and 4 of K from shared memory for 16 RPT FFMA (and the
+// same for P V), against the reference's 8 loads per 16 FFMA: the FFMA pipe, not the shared-memory
+// pipe, is the bound. Three blocks per SM (72.7 / 63.2 KB shared memory, <= 168 registers).
+// Rows are independent, so the tile height changes no result bit; it only removes padded rows and
+// evens the waves (canvas s = 240: BM = 48, no padded rows, 162.5 -> 148.6 us).
 //
 // Loads: cp.async (16 B, L2-only) into padded tiles. V(n) travels while S(n) is computed, K(n+1)
 // while P V(n) is; Q once. Tiles past `seq` are zero-filled.
@@ -25,49 +29,53 @@
 namespace cfa {
 namespace {
 
-constexpr int FWD_SMEM_FLOATS = 3 * FWD_BM * LD + FWD_BM * LDP;
+template <int RPT>
+constexpr int fwd_smem_floats() {
+  return (8 * RPT + 2 * FWD_BN) * LD + 8 * RPT * LDP;
+}
 
-// S = Q K^T for this thread's 8 rows (rb + 2i) and the first JN of its 4 key groups (keys
+// S = Q K^T for this thread's NR rows (rb + 2i) and the first JN of its 4 key groups (keys
 // tx + 16jj), with packed FMAs: each score is an even-d chain plus an odd-d chain (a float4 of Q
 // and one of K give the pairs (d, d + 1), (d + 2, d + 3) directly), each in increasing d, added at
 // the end. Key groups jj >= JN lie wholly past the sequence end: left at 0 (masked later).
-template <int JN>
+template <int JN, int NR>
 __device__ __forceinline__ void score_tile(const float* Qs, const float* Ks, int rb, int tx,
-                                           float (&s)[8][4]) {
-  uint64_t s2[8][JN];
+                                           float (&s)[NR][4]) {
+  uint64_t s2[NR][JN];
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < NR; ++i)
 #pragma unroll
     for (int jj = 0; jj < JN; ++jj) s2[i][jj] = 0ull;
 #pragma unroll 2
   for (int c = 0; c < 64; c += 4) {
-    ulonglong2 kv[JN], qv[8];
+    ulonglong2 kv[JN], qv[NR];
 #pragma unroll
     for (int jj = 0; jj < JN; ++jj) kv[jj] = ld2x2(Ks + (tx + 16 * jj) * LD + c);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) qv[i] = ld2x2(Qs + (rb + 2 * i) * LD + c);
+    for (int i = 0; i < NR; ++i) qv[i] = ld2x2(Qs + (rb + 2 * i) * LD + c);
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < NR; ++i)
 #pragma unroll
       for (int jj = 0; jj < JN; ++jj) s2[i][jj] = fma2(qv[i].x, kv[jj].x, s2[i][jj]);
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < NR; ++i)
 #pragma unroll
       for (int jj = 0; jj < JN; ++jj) s2[i][jj] = fma2(qv[i].y, kv[jj].y, s2[i][jj]);
   }
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < NR; ++i)
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) s[i][jj] = jj < JN ? sum2(s2[i][jj < JN ? jj : 0]) : 0.0f;
 }
 
-template <bool CAUSAL>
+template <int RPT, bool CAUSAL>
 __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs a) {
+  constexpr int BM = 8 * RPT;
   extern __shared__ float4 smem4[];
-  float* Qs = reinterpret_cast<float*>(smem4);  // [64][LD]
-  float* Ks = Qs + FWD_BM * LD;                 // [64][LD]
+  float* Qs = reinterpret_cast<float*>(smem4);  // [BM][LD]
+  float* Ks = Qs + BM * LD;                     // [64][LD]
   float* Vs = Ks + FWD_BN * LD;                 // [64][LD]
-  float* Ps = Vs + FWD_BN * LD;                 // [64][LDP], query-major; warp w uses rows 16w..
+  float* Ps = Vs + FWD_BN * LD;                 // [BM][LDP], query-major; warp w its own rows
 
   griddep_wait();  // q, k, v may come from the previous kernel on the stream
   griddep_launch_dependents();
@@ -85,28 +93,28 @@ __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs 
     bh = static_cast<int>(blockIdx.x / a.n_qtiles);
   }
   const int b = bh / a.H, h = bh % a.H;
-  const int q0 = qt * FWD_BM;
+  const int q0 = qt * BM;
   const int S = a.S;
   const float* qp = a.q + b * a.q_sb + h * a.q_sh;
   const float* kp = a.k + b * a.k_sb + h * a.k_sh;
   const float* vp = a.v + b * a.v_sb + h * a.v_sh;
 
-  const int k_end = CAUSAL ? min(S, q0 + FWD_BM) : S;
+  const int k_end = CAUSAL ? min(S, q0 + BM) : S;
 
-  load_tile_async<FWD_BM, FWD_THREADS>(Qs, qp, a.q_ss, q0, S);
+  load_tile_async<BM, FWD_THREADS>(Qs, qp, a.q_ss, q0, S);
   load_tile_async<FWD_BN, FWD_THREADS>(Ks, kp, a.k_ss, 0, S);
   cp_async_commit();
 
-  const int rb = 16 * w + ty;  // this thread's rows: rb + 2i
+  const int rb = 2 * RPT * w + ty;  // this thread's rows: rb + 2i, i < RPT
   // x = (q.k) * scale (exact for a power-of-two scale, as in the composed path), p = e^(x - m)
   // with CUDA's expf. lpart is this thread's share
   // of the row sum (its 4 keys per tile, rescaled like O); the 16 shares of a row are added once,
   // after the last tile.
   // acc2[i][0] holds dims 4tx, 4tx + 1 of row rb + 2i, acc2[i][1] dims 4tx + 2, 4tx + 3.
-  float m[8], lpart[8];
-  uint64_t acc2[8][2];
+  float m[RPT], lpart[RPT];
+  uint64_t acc2[RPT][2];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < RPT; ++i) {
     m[i] = -INFINITY;
     lpart[i] = 0.0f;
     acc2[i][0] = acc2[i][1] = 0ull;
@@ -126,16 +134,16 @@ __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs 
     // registers; shorter last tiles compute their dead groups and mask them. Skipping whole dead
     // warps measured slower: the branch costs registers.)
     const int jn = min(4, (S - k0 + 15) / 16);
-    float s[8][4];
+    float s[RPT][4];
     if (jn == 3)
-      score_tile<3>(Qs, Ks, rb, tx, s);
+      score_tile<3, RPT>(Qs, Ks, rb, tx, s);
     else
-      score_tile<4>(Qs, Ks, rb, tx, s);
+      score_tile<4, RPT>(Qs, Ks, rb, tx, s);
 
     // Masks only where the tile crosses the sequence end or the causal diagonal (block-uniform).
     const bool edge = (k0 + FWD_BN > S) || (CAUSAL && k0 + FWD_BN - 1 > q0);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < RPT; ++i) {
       float x[4];
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) x[jj] = s[i][jj] * a.scale;
@@ -183,15 +191,15 @@ __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs 
 #pragma unroll 8  // (unroll 2 / 4 / 8: 167.6 / 164.4 / 162.6 us at the canvas shape)
     for (int j = 0; j < jlim; j += 4) {
       ulonglong2 vv[4];
-      float4 pv[8];
+      float4 pv[RPT];
 #pragma unroll
       for (int t = 0; t < 4; ++t) vv[t] = ld2x2(Vs + (j + t) * LD + 4 * tx);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) pv[i] = ld4(Ps + (rb + 2 * i) * LDP + j);
+      for (int i = 0; i < RPT; ++i) pv[i] = ld4(Ps + (rb + 2 * i) * LDP + j);
 #pragma unroll
       for (int t = 0; t < 4; ++t)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < RPT; ++i) {
           const uint64_t pr = dup2(f4c(pv[i], t));
           acc2[i][0] = fma2(pr, vv[t].x, acc2[i][0]);
           acc2[i][1] = fma2(pr, vv[t].y, acc2[i][1]);
@@ -200,7 +208,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs 
   }
 
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < RPT; ++i) {
     // DETERMINISM: the row sum is the butterfly of the 16 per-thread shares, in a fixed order.
     const float l = half_warp_sum(lpart[i]);
     const int qi = q0 + rb + 2 * i;
@@ -217,23 +225,39 @@ __global__ void __launch_bounds__(FWD_THREADS, 3) fwd_ffma_kernel(const FwdArgs 
 
 }  // namespace
 
-size_t fwd_smem_bytes() { return FWD_SMEM_FLOATS * sizeof(float); }
-
-cudaError_t setup_fwd_attributes() {
-  const int bytes = static_cast<int>(fwd_smem_bytes());
-  cudaError_t e = cudaFuncSetAttribute(fwd_ffma_kernel<false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(fwd_ffma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              bytes);
+int fwd_tile_rows(int64_t seq) {
+  const int64_t pad64 = (64 - seq % 64) % 64, pad48 = (48 - seq % 48) % 48;
+  return pad48 < pad64 ? 48 : 64;
 }
 
-cudaError_t launch_fwd(const FwdArgs& a, int causal, cudaStream_t stream) {
-  const int64_t blocks = static_cast<int64_t>(a.n_qtiles) * a.B * a.H;
-  const dim3 grid(static_cast<unsigned>(blocks));
-  if (causal)
-    return launch_pdl(fwd_ffma_kernel<true>, grid, dim3(FWD_THREADS), fwd_smem_bytes(), stream, a);
-  return launch_pdl(fwd_ffma_kernel<false>, grid, dim3(FWD_THREADS), fwd_smem_bytes(), stream, a);
+cudaError_t setup_fwd_attributes() {
+  cudaError_t e = cudaSuccess;
+  auto set = [&](const void* fn, int floats) {
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(floats * sizeof(float)));
+  };
+  set(reinterpret_cast<const void*>(fwd_ffma_kernel<8, false>), fwd_smem_floats<8>());
+  set(reinterpret_cast<const void*>(fwd_ffma_kernel<8, true>), fwd_smem_floats<8>());
+  set(reinterpret_cast<const void*>(fwd_ffma_kernel<6, false>), fwd_smem_floats<6>());
+  set(reinterpret_cast<const void*>(fwd_ffma_kernel<6, true>), fwd_smem_floats<6>());
+  return e;
+}
+
+cudaError_t launch_fwd(const FwdArgs& args, int causal, cudaStream_t stream) {
+  FwdArgs a = args;
+  const int bm = fwd_tile_rows(a.S);
+  a.n_qtiles = (a.S + bm - 1) / bm;
+  const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(a.n_qtiles) * a.B * a.H));
+  const dim3 block(FWD_THREADS);
+  if (bm == 48) {
+    const size_t smem = fwd_smem_floats<6>() * sizeof(float);
+    return causal ? launch_pdl(fwd_ffma_kernel<6, true>, grid, block, smem, stream, a)
+                  : launch_pdl(fwd_ffma_kernel<6, false>, grid, block, smem, stream, a);
+  }
+  const size_t smem = fwd_smem_floats<8>() * sizeof(float);
+  return causal ? launch_pdl(fwd_ffma_kernel<8, true>, grid, block, smem, stream, a)
+                : launch_pdl(fwd_ffma_kernel<8, false>, grid, block, smem, stream, a);
 }
 
 }  // namespace cfa
