@@ -97,7 +97,7 @@ int fwd_impl(const float* q, const int64_t q_strides[3], const float* k,
   a.H = static_cast<int>(heads);
   a.S = static_cast<int>(seq);
   a.scale = scale;
-  const int bm = d64 ? cfa::fwd_tile_rows(seq) : cfa::hd_fwd_bm(static_cast<int>(head_dim));
+  const int bm = d64 ? cfa::fwd_tile_rows(seq) : cfa::hd_fwd_rows(static_cast<int>(head_dim), seq);
   a.n_qtiles = static_cast<int>((seq + bm - 1) / bm);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const cudaError_t e = d64 ? cfa::launch_fwd(a, causal != 0, s)

@@ -116,10 +116,10 @@ cudaError_t launch_fwd(const FwdArgs& a, int causal, cudaStream_t stream);
 cudaError_t launch_bwd_prep(const PrepArgs& a, cudaStream_t stream);
 cudaError_t launch_bwd(const BwdArgs& a, int causal, cudaStream_t stream);
 
-// Head dims 32 and 128 (csrc/hd_ffma.cu): the forward's query tile (64 or 32), the attribute
+// Head dims 32 and 128 (csrc/hd_ffma.cu): the forward's query tile (per sequence length), the attribute
 // set-up and the launchers; the backward uses the same 64-key blocks and 64-query tiles as head
 // dim 64, so BwdArgs, PrepArgs and the workspace layout carry over.
-int hd_fwd_bm(int head_dim);
+int hd_fwd_rows(int head_dim, int64_t seq);
 cudaError_t setup_hd_attributes();
 cudaError_t launch_hd_fwd(const FwdArgs& a, int head_dim, int causal, cudaStream_t stream);
 cudaError_t launch_hd_bwd_prep(const PrepArgs& a, int head_dim, cudaStream_t stream);

@@ -8,9 +8,11 @@
 //
 // The head-dim-64 kernels stay as they are; these follow the same design, with the tiles resized
 // so that registers and shared memory fit:
-//   forward   D = 32:  64 queries per block, each thread 8 rows x 4 keys (S) and 8 rows x 2 dims (O)
-//             D = 128: 32 queries per block, each thread 4 rows x 4 keys (S) and 4 rows x 8 dims (O),
-//                      the 8 dims as two float4 64 apart (conflict-free loads); 2 blocks per SM
+//   forward   D = 32:  64 or 48 queries per block, each thread 8 or 6 rows x 4 keys (S) and x 2
+//                      dims (O)
+//             D = 128: 48 queries per block, each thread 6 rows x 4 keys (S) and x 8 dims (O),
+//                      the 8 dims as two float4 64 apart (conflict-free loads); 2 blocks per SM.
+//             (D = 32: the tile height that pads the fewer query rows at the sequence length.)
 //   backward  D = 32:  256 threads per 64-key block, as head dim 64 with 2 dims per thread
 //             D = 128: 512 threads per 64-key block (one block per SM, 176 KB of shared memory):
 //                      phase 1 4 rows x 4 keys per thread, phase 2 4 keys x 8 dims (dV, dK),
@@ -26,20 +28,25 @@ namespace {
 
 template <int D>
 struct Hd;
+// The forward's rows per thread: two candidates per head dim (query tiles of 8 RPT rows), the one
+// that pads fewer rows at the sequence length taken (hd_fwd_rows; rows are independent, so the
+// choice changes no bit), and blocks per SM.
 template <>
 struct Hd<32> {
-  static constexpr int RPT = 8;       // forward query rows per thread
-  static constexpr int FWD_MINB = 3;  // forward blocks per SM (registers)
+  static constexpr int RPT_A = 8, RPT_B = 6;  // 64- or 48-query tiles
+  static constexpr int FWD_MINB = 3;          // forward blocks per SM (registers)
 };
 template <>
 struct Hd<128> {
-  static constexpr int RPT = 4;
-  static constexpr int FWD_MINB = 2;  // (shared memory: 94.7 KB per block)
+  // 48-query tiles at every length: against 32-query tiles (4 rows per thread) they measured
+  // faster at every shape tried (canvas-shaped 185 -> 158 us, s = 4096 causal 917 -> 820 us).
+  static constexpr int RPT_A = 6, RPT_B = 6;
+  static constexpr int FWD_MINB = 2;          // (shared memory: 107.3 KB per block)
 };
 
-template <int D>
+template <int RPT>
 __host__ __device__ constexpr int fwd_bm() {
-  return 8 * Hd<D>::RPT;  // 4 warps x 2 half-warps x RPT rows
+  return 8 * RPT;  // 4 warps x 2 half-warps x RPT rows
 }
 
 // Row stride of the [rows][D] tiles: D + 4 floats, rows 16-byte aligned and 4 banks apart.
@@ -48,9 +55,9 @@ __host__ __device__ constexpr int ldh() {
   return D + 4;
 }
 
-template <int D>
+template <int D, int RPT>
 __host__ __device__ constexpr int hd_fwd_smem_floats() {
-  return (fwd_bm<D>() + 2 * 64) * ldh<D>() + fwd_bm<D>() * LDP;
+  return (fwd_bm<RPT>() + 2 * 64) * ldh<D>() + fwd_bm<RPT>() * LDP;
 }
 
 template <int D>
@@ -158,9 +165,9 @@ __device__ __forceinline__ void store_dims(float* dst, int tx, const float (&v)[
 
 // ---------------------------------------------------------------------------------------------
 // Forward: csrc/fwd_ffma.cu's kernel with D-sized tiles (see the header comment).
-template <int D, bool CAUSAL>
+template <int D, int RPT, bool CAUSAL>
 __global__ void __launch_bounds__(FWD_THREADS, Hd<D>::FWD_MINB) hd_fwd_kernel(const FwdArgs a) {
-  constexpr int RPT = Hd<D>::RPT, BM = fwd_bm<D>(), L = ldh<D>(), NP = Dims<D>::NP;
+  constexpr int BM = fwd_bm<RPT>(), L = ldh<D>(), NP = Dims<D>::NP;
   extern __shared__ float4 smem4[];
   float* Qs = reinterpret_cast<float*>(smem4);  // [BM][L]
   float* Ks = Qs + BM * L;                      // [64][L]
@@ -647,12 +654,18 @@ __global__ void __launch_bounds__(Bwd<D>::NT, 256 / (Bwd<D>::NT / 2)) hd_bwd_ker
 
 template <int D>
 cudaError_t set_attrs() {
-  cudaError_t e = cudaFuncSetAttribute(hd_fwd_kernel<D, false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       hd_fwd_smem_floats<D>() * 4);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(hd_fwd_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             hd_fwd_smem_floats<D>() * 4);
+  constexpr int A = Hd<D>::RPT_A, Bq = Hd<D>::RPT_B;
+  cudaError_t e = cudaSuccess;
+  auto set = [&](const void* fn, int floats) {
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, floats * 4);
+  };
+  set(reinterpret_cast<const void*>(hd_fwd_kernel<D, A, false>), hd_fwd_smem_floats<D, A>());
+  set(reinterpret_cast<const void*>(hd_fwd_kernel<D, A, true>), hd_fwd_smem_floats<D, A>());
+  if constexpr (Bq != A) {
+    set(reinterpret_cast<const void*>(hd_fwd_kernel<D, Bq, false>), hd_fwd_smem_floats<D, Bq>());
+    set(reinterpret_cast<const void*>(hd_fwd_kernel<D, Bq, true>), hd_fwd_smem_floats<D, Bq>());
+  }
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(hd_bwd_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              hd_bwd_smem_floats<D>() * 4);
@@ -664,7 +677,34 @@ cudaError_t set_attrs() {
 
 }  // namespace
 
-int hd_fwd_bm(int head_dim) { return head_dim == 128 ? fwd_bm<128>() : fwd_bm<32>(); }
+template <int D>
+int rows_for(int64_t seq) {
+  const int a = fwd_bm<Hd<D>::RPT_A>(), b = fwd_bm<Hd<D>::RPT_B>();
+  const int64_t pa = (a - seq % a) % a, pb = (b - seq % b) % b;
+  return pb < pa ? b : a;
+}
+
+template <int D>
+cudaError_t launch_fwd_d(const FwdArgs& args, int causal, cudaStream_t stream) {
+  constexpr int A = Hd<D>::RPT_A, Bq = Hd<D>::RPT_B;
+  FwdArgs a = args;
+  const int bm = rows_for<D>(a.S);
+  a.n_qtiles = (a.S + bm - 1) / bm;
+  const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(a.n_qtiles) * a.B * a.H));
+  const dim3 block(FWD_THREADS);
+  if (bm == fwd_bm<Bq>()) {
+    const size_t smem = hd_fwd_smem_floats<D, Bq>() * 4;
+    return causal ? launch_pdl(hd_fwd_kernel<D, Bq, true>, grid, block, smem, stream, a)
+                  : launch_pdl(hd_fwd_kernel<D, Bq, false>, grid, block, smem, stream, a);
+  }
+  const size_t smem = hd_fwd_smem_floats<D, A>() * 4;
+  return causal ? launch_pdl(hd_fwd_kernel<D, A, true>, grid, block, smem, stream, a)
+                : launch_pdl(hd_fwd_kernel<D, A, false>, grid, block, smem, stream, a);
+}
+
+int hd_fwd_rows(int head_dim, int64_t seq) {
+  return head_dim == 128 ? rows_for<128>(seq) : rows_for<32>(seq);
+}
 
 cudaError_t setup_hd_attributes() {
   cudaError_t e = set_attrs<32>();
@@ -672,16 +712,7 @@ cudaError_t setup_hd_attributes() {
 }
 
 cudaError_t launch_hd_fwd(const FwdArgs& a, int head_dim, int causal, cudaStream_t stream) {
-  const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(a.n_qtiles) * a.B * a.H));
-  const dim3 block(FWD_THREADS);
-  if (head_dim == 32) {
-    const size_t smem = hd_fwd_smem_floats<32>() * 4;
-    return causal ? launch_pdl(hd_fwd_kernel<32, true>, grid, block, smem, stream, a)
-                  : launch_pdl(hd_fwd_kernel<32, false>, grid, block, smem, stream, a);
-  }
-  const size_t smem = hd_fwd_smem_floats<128>() * 4;
-  return causal ? launch_pdl(hd_fwd_kernel<128, true>, grid, block, smem, stream, a)
-                : launch_pdl(hd_fwd_kernel<128, false>, grid, block, smem, stream, a);
+  return head_dim == 32 ? launch_fwd_d<32>(a, causal, stream) : launch_fwd_d<128>(a, causal, stream);
 }
 
 cudaError_t launch_hd_bwd_prep(const PrepArgs& a, int head_dim, cudaStream_t stream) {
