@@ -116,16 +116,27 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
   float* Dt = Lt + 64;                          // [64] D of this tile (0 past S)
   int* s_int = reinterpret_cast<int*>(Dt + 64); // [0]: ticket, [1]: turn came
 
-  griddep_wait();  // D, the cleared ticket and counters: the prep kernel's writes
   griddep_launch_dependents();
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
   const int ty = lane >> 4, tx = lane & 15;
   const int grp = w >> 2, wg = w & 3;  // grp 0: S, P, dV; grp 1: dP, dS, dK (warp-uniform)
   const int S = a.S;
 
-  if (tid == 0) s_int[0] = atomicAdd(a.ticket, 1);
-  __syncthreads();
-  const int ticket = s_int[0];
+  // The prep kernel's writes (D, the cleared ticket and counters) are awaited before their first
+  // use. The no-wait path (dQ partials) never waits on another block: its block index is its
+  // ticket, and the block's first tiles of q, k, v, dO -- inputs no kernel of this chain writes,
+  // read through L2 only -- load while the prep kernel finishes. The turn chain draws tickets
+  // (forward progress, below).
+  const bool no_wait = a.dq_part != nullptr;
+  int ticket;
+  if (no_wait) {
+    ticket = static_cast<int>(blockIdx.x);
+  } else {
+    griddep_wait();
+    if (tid == 0) s_int[0] = atomicAdd(a.ticket, 1);
+    __syncthreads();
+    ticket = s_int[0];
+  }
   // Tickets run key-block-major: every (b, h) of key block 0, then of key block 1, ... A block of
   // the turn chain waits only on key block kb - 1 of its (b, h), which holds a smaller ticket, so
   // it is running or done; and blocks of similar length (causal: block kb walks n_qtiles - kb
@@ -134,7 +145,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
   const int BH = a.B * a.H;
   // (Non-causal, no-wait path: (b, h)-major instead, so each (b, h)'s last block -- the one that
   // sums its dQ partials -- finishes throughout the run rather than all in the last wave.)
-  const bool bh_major = !CAUSAL && a.dq_part != nullptr;
+  const bool bh_major = !CAUSAL && no_wait;
   const int kb = bh_major ? ticket % a.n_kblocks : ticket / BH;
   const int bh = bh_major ? ticket / a.n_kblocks : ticket % BH;
   const int b = bh / a.H, h = bh % a.H;
@@ -163,10 +174,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
   const int kb2 = 16 * wg + 8 * ty;   // phase 2 keys: kb2 .. kb2 + 7
   const int rb3 = 8 * w + ty;         // phase 3 rows: rb3 + 2i
 
-  // Q, dO, L, D of query tile q0 into the (single) tile buffers, one cp.async group.
-  auto load_query_tile = [&](int q0) {
+  // Q, dO, then L, D of query tile q0 into the (single) tile buffers; one cp.async group.
+  auto load_q_do = [&](int q0) {
     load_tile_async<64, BWD_THREADS>(Qs, qp, a.q_ss, q0, S);
     load_tile_async<64, BWD_THREADS>(dOs, gp, a.do_ss, q0, S);
+  };
+  auto load_l_d = [&](int q0) {
     if (tid < 128) {
       const int r = tid & 63, i = q0 + r;
       const bool ok = i < S;
@@ -174,10 +187,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
       cp_async4((tid < 64 ? Lt : Dt) + r, src, ok ? 4 : 0);
     }
   };
+  auto load_query_tile = [&](int q0) {
+    load_q_do(q0);
+    load_l_d(q0);
+  };
 
   // Causal: queries before the block's first key never see it.
   const int t_begin = CAUSAL ? k0 / BWD_BM : 0;
-  load_query_tile(t_begin * BWD_BM);
+  load_q_do(t_begin * BWD_BM);
+  if (no_wait) griddep_wait();
+  load_l_d(t_begin * BWD_BM);
   cp_async_commit();
   for (int t = t_begin; t < a.n_qtiles; ++t) {
     const int q0 = t * BWD_BM;

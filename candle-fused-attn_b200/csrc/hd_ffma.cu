@@ -366,18 +366,27 @@ __global__ void __launch_bounds__(Bwd<D>::NT, 256 / (Bwd<D>::NT / 2)) hd_bwd_ker
   float* Dt = Lt + 64;
   int* s_int = reinterpret_cast<int*>(Dt + 64);
 
-  griddep_wait();  // D, the cleared ticket and counters: the prep kernel's writes
   griddep_launch_dependents();
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
   const int ty = lane >> 4, tx = lane & 15;
   const int grp = w / WG, wg = w % WG;  // grp 0: S, P, dV; grp 1: dP, dS, dK
   const int S = a.S;
 
-  if (tid == 0) s_int[0] = atomicAdd(a.ticket, 1);
-  __syncthreads();
-  const int ticket = s_int[0];
+  // The prep kernel's writes (D, the cleared ticket and counters) are awaited before their first
+  // use; the no-wait path takes its block index as ticket and loads its first q, k, v, dO tiles
+  // meanwhile (as the head-dim-64 kernel does).
+  const bool no_wait = a.dq_part != nullptr;
+  int ticket;
+  if (no_wait) {
+    ticket = static_cast<int>(blockIdx.x);
+  } else {
+    griddep_wait();
+    if (tid == 0) s_int[0] = atomicAdd(a.ticket, 1);
+    __syncthreads();
+    ticket = s_int[0];
+  }
   const int BH = a.B * a.H;
-  const bool bh_major = !CAUSAL && a.dq_part != nullptr;
+  const bool bh_major = !CAUSAL && no_wait;
   const int kb = bh_major ? ticket % a.n_kblocks : ticket / BH;
   const int bh = bh_major ? ticket / a.n_kblocks : ticket % BH;
   const int b = bh / a.H, h = bh % a.H;
@@ -408,9 +417,11 @@ __global__ void __launch_bounds__(Bwd<D>::NT, 256 / (Bwd<D>::NT / 2)) hd_bwd_ker
   const int rb3 = D == 32 ? 8 * w + ty : 8 * wg + ty;
   const int d3 = D == 32 ? 2 * tx : 64 * grp + 4 * tx;
 
-  auto load_query_tile = [&](int q0) {
+  auto load_q_do = [&](int q0) {
     load_rows_async<64, NT, D>(Qs, qp, a.q_ss, q0, S);
     load_rows_async<64, NT, D>(dOs, gp, a.do_ss, q0, S);
+  };
+  auto load_l_d = [&](int q0) {
     if (tid < 128) {
       const int r = tid & 63, i = q0 + r;
       const bool ok = i < S;
@@ -418,9 +429,15 @@ __global__ void __launch_bounds__(Bwd<D>::NT, 256 / (Bwd<D>::NT / 2)) hd_bwd_ker
       cp_async4((tid < 64 ? Lt : Dt) + r, src, ok ? 4 : 0);
     }
   };
+  auto load_query_tile = [&](int q0) {
+    load_q_do(q0);
+    load_l_d(q0);
+  };
 
   const int t_begin = CAUSAL ? k0 / 64 : 0;
-  load_query_tile(t_begin * 64);
+  load_q_do(t_begin * 64);
+  if (no_wait) griddep_wait();
+  load_l_d(t_begin * 64);
   cp_async_commit();
   for (int t = t_begin; t < a.n_qtiles; ++t) {
     const int q0 = t * 64;
