@@ -42,7 +42,13 @@ EXPORTS = (
     "cfa_bwd_workspace_bytes_hd",
     "cfa_bwd_workspace_bytes_fast_hd",
     "cfa_bwd_f32",
+    "cfa_fwd_select",
+    "cfa_fwd_status",
 )
+
+# Head-dim-64 forward implementations (cfa_fwd_select).
+FWD_FFMA = 0
+FWD_TC = 1
 
 # Head dims the generic entry points (cfa_fwd_f32, cfa_bwd_f32) take; the _d64 ones take 64 only,
 # as the reference's CUDA path does (src/lib.rs:91).
@@ -98,6 +104,10 @@ def load() -> ctypes.CDLL:
     lib.cfa_fwd_f32.argtypes = lib.cfa_fwd_f32_d64.argtypes
     lib.cfa_bwd_f32.restype = ctypes.c_int
     lib.cfa_bwd_f32.argtypes = lib.cfa_bwd_f32_d64.argtypes
+    lib.cfa_fwd_select.restype = ctypes.c_int
+    lib.cfa_fwd_select.argtypes = [ctypes.c_int]
+    lib.cfa_fwd_status.restype = ctypes.c_int
+    lib.cfa_fwd_status.argtypes = [_p]
     for name in ("cfa_bwd_workspace_bytes_hd", "cfa_bwd_workspace_bytes_fast_hd"):
         fn = getattr(lib, name)
         fn.restype = ctypes.c_size_t
@@ -171,6 +181,19 @@ def bwd_hd(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, do_ptr, dos, dqkv_pt
 
 def bwd_status(ws_ptr, stream) -> int:
     return load().cfa_bwd_status(ws_ptr, stream)
+
+
+def fwd_select(impl: int) -> int:
+    """Head-dim-64 forward for this process (FWD_FFMA or FWD_TC); returns the previous choice."""
+    prev = load().cfa_fwd_select(int(impl))
+    if prev < 0:
+        raise ValueError(f"candle_fused_attn: unknown forward implementation {impl}")
+    return prev
+
+
+def fwd_status(stream) -> int:
+    """Synchronises `stream`; CFA_ERR_TIMEOUT if a tensor-core forward's bounded wait expired."""
+    return load().cfa_fwd_status(stream)
 
 
 def selftest_bounded_wait(ws_ptr, timeout_ns, blocks, stream) -> int:

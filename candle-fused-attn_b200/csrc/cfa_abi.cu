@@ -5,6 +5,7 @@
 // same inputs, the same outputs and layouts, the same stream discipline (everything on the
 // caller's stream, no synchronisation), with the checks the reference makes in Rust
 // (src/cuda.rs:69-93, src/lib.rs:431-435, :533-538) repeated here so a C caller gets them too.
+#include <atomic>
 #include <mutex>
 
 #include "cfa_internal.h"
@@ -25,6 +26,9 @@ struct DeviceOnce {
 DeviceOnce g_fwd_once[kMaxDevices];
 DeviceOnce g_bwd_once[kMaxDevices];
 DeviceOnce g_hd_once[kMaxDevices];  // head dims 32 and 128
+DeviceOnce g_fwd_tc_once[kMaxDevices];
+// Head-dim-64 forward: 0 = CUDA-core FFMA kernel, 1 = tensor-core kernel (cfa_fwd_select).
+std::atomic<int> g_fwd_impl{0};
 
 int setup(DeviceOnce* table, cudaError_t (*fn)()) {
   int dev = 0;
@@ -75,7 +79,10 @@ int fwd_impl(const float* q, const int64_t q_strides[3], const float* k,
   if (!strides_ok(q_strides) || !strides_ok(k_strides) || !strides_ok(v_strides))
     return CFA_ERR_ALIGNMENT;
   const bool d64 = head_dim == 64;
-  st = d64 ? setup(g_fwd_once, cfa::setup_fwd_attributes) : setup(g_hd_once, cfa::setup_hd_attributes);
+  const bool tc = d64 && g_fwd_impl.load(std::memory_order_relaxed) == 1;
+  st = tc    ? setup(g_fwd_tc_once, cfa::setup_fwd_tc_attributes)
+       : d64 ? setup(g_fwd_once, cfa::setup_fwd_attributes)
+             : setup(g_hd_once, cfa::setup_hd_attributes);
   if (st != CFA_OK) return st;
 
   FwdArgs a;
@@ -100,8 +107,9 @@ int fwd_impl(const float* q, const int64_t q_strides[3], const float* k,
   const int bm = d64 ? cfa::fwd_tile_rows(seq) : cfa::hd_fwd_rows(static_cast<int>(head_dim), seq);
   a.n_qtiles = static_cast<int>((seq + bm - 1) / bm);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const cudaError_t e = d64 ? cfa::launch_fwd(a, causal != 0, s)
-                            : cfa::launch_hd_fwd(a, static_cast<int>(head_dim), causal != 0, s);
+  const cudaError_t e = tc    ? cfa::launch_fwd_tc(a, causal != 0, s)
+                        : d64 ? cfa::launch_fwd(a, causal != 0, s)
+                              : cfa::launch_hd_fwd(a, static_cast<int>(head_dim), causal != 0, s);
   return e == cudaSuccess ? CFA_OK : CFA_ERR_LAUNCH;
 }
 
@@ -285,6 +293,18 @@ int cfa_selftest_bounded_wait(void* workspace, int64_t timeout_ns, int blocks, v
                                                   static_cast<uint64_t>(timeout_ns), blocks,
                                                   static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? CFA_OK : CFA_ERR_LAUNCH;
+}
+
+int cfa_fwd_select(int impl) {
+  if (impl != 0 && impl != 1) return -1;
+  return g_fwd_impl.exchange(impl);
+}
+
+int cfa_fwd_status(void* stream) {
+  if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return CFA_ERR_CUDA;
+  int flag = 0;
+  if (cfa::fwd_tc_status(&flag) != cudaSuccess) return CFA_ERR_CUDA;
+  return flag != 0 ? CFA_ERR_TIMEOUT : CFA_OK;
 }
 
 int cfa_bwd_status(const void* workspace, void* stream) {

@@ -113,6 +113,10 @@ size_t bwd_smem_bytes();
 
 // Launchers (return a cudaError_t from the launch). launch_fwd sets the query-tile count itself.
 cudaError_t launch_fwd(const FwdArgs& a, int causal, cudaStream_t stream);
+// The tensor-core forward (fwd_tc.cu): 128-query tiles, sets the query-tile count itself.
+cudaError_t launch_fwd_tc(const FwdArgs& a, int causal, cudaStream_t stream);
+// Reads and clears the tensor-core forward's device error flag (1: an MMA wait expired).
+cudaError_t fwd_tc_status(int* flag);
 cudaError_t launch_bwd_prep(const PrepArgs& a, cudaStream_t stream);
 cudaError_t launch_bwd(const BwdArgs& a, int causal, cudaStream_t stream);
 
@@ -130,6 +134,7 @@ cudaError_t launch_selftest_wait(int* ws, uint64_t short_ns, int blocks, cudaStr
 
 // One-time per-device attribute set-up (dynamic shared memory limits).
 cudaError_t setup_fwd_attributes();
+cudaError_t setup_fwd_tc_attributes();
 cudaError_t setup_bwd_attributes();
 
 }  // namespace cfa

@@ -1,0 +1,461 @@
+// SPDX-License-Identifier: MIT OR Apache-2.0
+//
+// The forward on the tensor cores: O = softmax(Q K^T * scale [+ causal mask]) V and the row
+// log-sum-exp L over fp32, head_dim 64 -- the same inputs, outputs and layouts as fwd_ffma.cu and
+// the reference's fattn_fwd_f32_d64 (kernels/fused_attn.cu:469-598), computed with tcgen05.mma.
+//
+// fp32 products from bf16 parts. Every fp32 operand x is split into x0 + x1 + x2, three bf16
+// (each part the round-to-nearest bf16 of what the previous ones leave; the two subtractions are
+// exact), and A B is formed from the six products A0B0 + (A0B1 + A1B0 + A0B2 + A1B1 + A2B0): the
+// dropped terms are below 2^-24 relative. The tensor core accumulates in fp32 by truncation, so
+// A0B0 and the five small products go to two separate TMEM accumulators, each fresh for every
+// window of 64 reduction elements (S: all of d; O: one key tile), and the two are added in
+// registers with round-to-nearest: S = big + small; O = O * alpha + (big + small) per key tile.
+// Modelled against fp64 at the canvas shape (baseline/split_precision_model.py) this lands below
+// plain sequential-FFMA fp32 on every output of the forward and backward.
+//
+// Block: 16 softmax warps and one MMA warp own TC_BM = 128 queries of one (batch, head). Softmax
+// thread (warp w < 16, lane l) owns query row 32 (w % 4) + l -- its TMEM lane -- and the 16
+// columns (keys of S, dims of O) of group w / 4; warp 16 issues every MMA. Per key tile of 64 the
+// softmax threads read S from TMEM, run the online softmax (row max of the four column groups
+// through shared memory), split P into shared memory and split their items of V (transposed: the
+// P V product reads V^T K-major) and K; the MMA warp then issues P V(n) and S(n + 2). S is issued
+// two tiles ahead (two S buffers in TMEM, two K part buffers) and P V(n - 1) is folded into the
+// fp32 O registers one tile late, so the tensor core works while the softmax runs. Every thread
+// copies (cp.async) the fp32 chunks it splits itself, a tile ahead of use.
+//
+// Every mbarrier wait is bounded (WAIT_TIMEOUT_NS); on expiry the block sets the device error flag
+// (cfa_fwd_status reads it), waits once more, frees its TMEM and returns without writing.
+//
+// DETERMINISM: the MMA order is fixed by the code; every register sum has one order: S = big +
+// small; the row max over each group's 16 keys in order, then the groups 0..3; p summed over the
+// group's keys in order, per tile; l = ((l0 + l1) + l2) + l3; O over key tiles in index order.
+#include <cuda_bf16.h>
+
+#include "cfa_common.cuh"
+#include "cfa_tc.cuh"
+
+namespace cfa {
+
+__device__ int g_fwd_tc_err = 0;
+
+namespace {
+
+constexpr int TC_BM = 128;      // query rows per block = MMA M = TMEM lanes
+constexpr int TC_BN = 64;       // keys per tile = MMA N of S = MMA K of P V
+constexpr int TC_THREADS = 512;  // the softmax / split threads; one more warp issues the MMAs
+constexpr int TC_BLOCK = TC_THREADS + 32;
+constexpr int NQ = TC_THREADS / 128;  // threads per query row
+constexpr int CW = 64 / NQ;           // columns (keys of S, dims of O) per thread
+constexpr int PART_Q = TC_BM * 64 * 2;  // bytes of one bf16 part of a [128][64] operand
+constexpr int PART_K = TC_BN * 64 * 2;  // bytes of one bf16 part of a [64][64] operand
+constexpr int TILE_F32 = TC_BN * 64 * 4;  // bytes of one fp32 [64][64] tile
+constexpr int OFF_Q = 0;                       // Q parts, [128 rows][64 d], K-major
+constexpr int OFF_K = OFF_Q + 3 * PART_Q;      // two buffers of K parts, [64 keys][64 d]
+constexpr int OFF_V = OFF_K + 6 * PART_K;      // V^T parts, [64 d][64 keys], K-major
+constexpr int OFF_P = OFF_V + 3 * PART_K;      // P parts, [128 rows][64 keys] (first: Q in fp32)
+constexpr int OFF_KST = OFF_P + 3 * PART_Q;    // fp32 K tile in flight, [64][64]
+constexpr int OFF_VST = OFF_KST + TILE_F32;    // fp32 V tile in flight, [64][64]
+constexpr int OFF_RED = OFF_VST + TILE_F32;    // float [128][NQ]: the row max per column group, then l
+constexpr int OFF_BAR = OFF_RED + TC_BM * NQ * 4;  // mbarriers S0, S1, O and the TMEM base
+constexpr int TC_SMEM = OFF_BAR + 32;
+constexpr int TC_SMEM_ALLOC = TC_SMEM + 1024;  // room to align the base to 1024 bytes
+// TMEM columns: S big / small for two key tiles (0-63 / 64-127, 128-191 / 192-255), O big / small
+// (256-319 / 320-383); one block per SM, so it may take all 512.
+constexpr uint32_t TMEM_COLS = 512;
+
+// Byte offset of the 16-byte core-matrix row holding elements (row, 8 kc .. 8 kc + 7) of a
+// K-major bf16 operand with 64 elements per row: core matrices of 8 rows x 16 bytes, K-adjacent
+// core matrices 128 bytes apart, row groups of 8 rows 1024 bytes apart (the layout of
+// tc::desc_kmajor with LBO 128, SBO 1024).
+__device__ __forceinline__ uint32_t kmaj_off(int row, int kc) {
+  return static_cast<uint32_t>((((row >> 3) * 8 + kc) << 7) + ((row & 7) << 4));
+}
+
+__device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) {
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// x[0..7] -> three 16-byte rows of bf16 parts: x = p0 + p1 + p2 (+ below 2^-24 relative).
+__device__ __forceinline__ void split8(const float (&x)[8], uint4& p0, uint4& p1, uint4& p2) {
+  uint32_t a[4], b[4], c[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float x0 = x[2 * i], x1 = x[2 * i + 1];
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+    const float2 hf = __bfloat1622float2(h);
+    const float r0 = x0 - hf.x, r1 = x1 - hf.y;  // exact
+    const __nv_bfloat162 m = __floats2bfloat162_rn(r0, r1);
+    const float2 mf = __bfloat1622float2(m);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(r0 - mf.x, r1 - mf.y);  // exact differences
+    a[i] = bf2_bits(h);
+    b[i] = bf2_bits(m);
+    c[i] = bf2_bits(l);
+  }
+  p0 = make_uint4(a[0], a[1], a[2], a[3]);
+  p1 = make_uint4(b[0], b[1], b[2], b[3]);
+  p2 = make_uint4(c[0], c[1], c[2], c[3]);
+}
+
+__device__ __forceinline__ void store_parts(unsigned char* base, int part_bytes, uint32_t off,
+                                            const float (&x)[8]) {
+  uint4 p0, p1, p2;
+  split8(x, p0, p1, p2);
+  *reinterpret_cast<uint4*>(base + off) = p0;
+  *reinterpret_cast<uint4*>(base + part_bytes + off) = p1;
+  *reinterpret_cast<uint4*>(base + 2 * part_bytes + off) = p2;
+}
+
+// Staging. Every thread copies (cp.async) exactly the fp32 chunks it later splits, into slots of
+// its own, so no barrier separates a copy from its split: a row item (r, kc) -- row r, elements
+// 8 kc .. 8 kc + 7 of Q or K -- as two 16-byte copies, a V^T item (d, g) -- V[8 g .. 8 g + 7][d] --
+// as eight 4-byte copies. Slot j of thread t sits at (j * TC_THREADS + t) * width: a warp's
+// copies and reads of one slot are consecutive.
+// Row items: item c takes row 8 (c / 64) + c % 8 and chunk (c / 8) % 8, so a quarter-warp's parts
+// land in 8 different bank groups of the core-matrix layout and a warp reads 4 x 32 bytes of each
+// of 8 rows.
+__device__ __forceinline__ void row_item(int c, int& r, int& kc) {
+  r = 8 * (c >> 6) + (c & 7);
+  kc = (c >> 3) & 7;
+}
+
+// Copy row item c (slot base `slot`, two 16-byte slots) of a strided operand, rows from r0.
+__device__ __forceinline__ void stage_row_item(unsigned char* st, int slot, int c, const float* src,
+                                               int64_t stride, int r0, int seq) {
+  int r, kc;
+  row_item(c, r, kc);
+  const bool ok = r0 + r < seq;
+  const float* g = src + static_cast<int64_t>(ok ? r0 + r : 0) * stride + 8 * kc;
+  cp_async16(st + 16 * ((2 * slot) * TC_THREADS + threadIdx.x), g, ok ? 16 : 0);
+  cp_async16(st + 16 * ((2 * slot + 1) * TC_THREADS + threadIdx.x), g + 4, ok ? 16 : 0);
+}
+
+__device__ __forceinline__ void split_row_item(unsigned char* parts, int part_bytes,
+                                               const unsigned char* st, int slot, int c) {
+  int r, kc;
+  row_item(c, r, kc);
+  const float4 u = *reinterpret_cast<const float4*>(st + 16 * ((2 * slot) * TC_THREADS + threadIdx.x));
+  const float4 v =
+      *reinterpret_cast<const float4*>(st + 16 * ((2 * slot + 1) * TC_THREADS + threadIdx.x));
+  const float x[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
+  store_parts(parts, part_bytes, kmaj_off(r, kc), x);
+}
+
+// Copy V^T item (d, g) = (tid % 64, tid / 64) of the key tile from k0: 8 column elements.
+__device__ __forceinline__ void stage_vt_item(unsigned char* st, const float* src, int64_t stride,
+                                              int k0, int seq) {
+  const int d = threadIdx.x & 63, g = threadIdx.x >> 6;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int j = k0 + 8 * g + u;
+    const bool ok = j < seq;
+    cp_async4(st + 4 * (u * TC_THREADS + threadIdx.x),
+              src + static_cast<int64_t>(ok ? j : 0) * stride + d, ok ? 4 : 0);
+  }
+}
+
+__device__ __forceinline__ void split_vt_item(unsigned char* parts, const unsigned char* st) {
+  const int d = threadIdx.x & 63, g = threadIdx.x >> 6;
+  float x[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+    x[u] = *reinterpret_cast<const float*>(st + 4 * (u * TC_THREADS + threadIdx.x));
+  store_parts(parts, PART_K, kmaj_off(d, g), x);
+}
+
+// The six (A part, B part) products: A0B0 into the big accumulator, the rest into the small one.
+// A descriptor's start-address field holds the byte address / 16 (shared memory < 256 KB: no
+// carry out of its 14 bits), so the descriptor of base + off is the base's plus off / 16.
+template <int A_PART, int B_PART>
+__device__ __forceinline__ void issue_split_mma(uint32_t d_big, uint32_t d_small, uint32_t a_base,
+                                                uint32_t b_base, uint32_t idesc) {
+  constexpr int PA[6] = {0, 0, 1, 0, 1, 2};
+  constexpr int PB[6] = {0, 1, 0, 2, 1, 0};
+  const uint64_t ad0 = tc::desc_kmajor(a_base, 128, 1024);
+  const uint64_t bd0 = tc::desc_kmajor(b_base, 128, 1024);
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {  // K = 64 in steps of 16 bf16 (two core matrices)
+#pragma unroll
+    for (int p = 0; p < 6; ++p) {
+      const uint64_t ad = ad0 + static_cast<uint64_t>((PA[p] * A_PART + 256 * ks) >> 4);
+      const uint64_t bd = bd0 + static_cast<uint64_t>((PB[p] * B_PART + 256 * ks) >> 4);
+      const uint32_t acc = p == 0 ? (ks > 0) : (ks > 0 || p > 1);
+      tc::mma_bf16(p == 0 ? d_big : d_small, ad, bd, idesc, acc);
+    }
+  }
+}
+
+// Named barriers: 1 = the softmax threads (TC_THREADS), 2 = those plus the MMA warp (TC_BLOCK).
+// Every participant syncs (none only arrives), so no group can run a phase ahead of another even
+// when a bounded wait has expired.
+__device__ __forceinline__ void bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// CW = 16 consecutive fp32 columns of this thread's TMEM lane at `big` and at `small`, one wait.
+__device__ __forceinline__ void tmem_ld2(uint32_t big, uint32_t small, float (&u)[CW],
+                                         float (&v)[CW]) {
+  static_assert(CW == 16, "one 16-column load per accumulator");
+  tc::tmem_ld16(big, u);
+  tc::tmem_ld16(small, v);
+  tc::tmem_wait_ld();
+}
+
+template <bool CAUSAL>
+__global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw = tc::smem_u32(smem_raw);
+  unsigned char* sm = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  unsigned char* Qp = sm + OFF_Q;
+  unsigned char* Vp = sm + OFF_V;
+  unsigned char* Pp = sm + OFF_P;
+  unsigned char* Kst = sm + OFF_KST;
+  unsigned char* Vst = sm + OFF_VST;
+  float* red = reinterpret_cast<float*>(sm + OFF_RED);
+  uint64_t* bar_s = reinterpret_cast<uint64_t*>(sm + OFF_BAR);  // [2]
+  uint64_t* bar_o = bar_s + 2;
+  uint32_t* tbase_p = reinterpret_cast<uint32_t*>(bar_s + 3);
+
+  const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  const int row = 32 * (w & 3) + lane;  // TMEM lane
+  const int cq = w >> 2;                // columns (keys of S, dims of O) CW cq .. CW cq + CW - 1
+  const int BH = a.B * a.H;
+  int qt, bh;
+  if (CAUSAL) {
+    qt = a.n_qtiles - 1 - static_cast<int>(blockIdx.x / BH);  // longest tiles first
+    bh = static_cast<int>(blockIdx.x % BH);
+  } else {
+    qt = static_cast<int>(blockIdx.x % a.n_qtiles);
+    bh = static_cast<int>(blockIdx.x / a.n_qtiles);
+  }
+  const int b = bh / a.H, h = bh % a.H;
+  const int q0 = qt * TC_BM;
+  const int S = a.S;
+  const float* qp = a.q + b * a.q_sb + h * a.q_sh;
+  const float* kp = a.k + b * a.k_sb + h * a.k_sh;
+  const float* vp = a.v + b * a.v_sb + h * a.v_sh;
+  const int k_end = CAUSAL ? min(S, q0 + TC_BM) : S;
+  const int T = (k_end + TC_BN - 1) / TC_BN;  // key tiles, >= 1
+
+  if (tid == 0) {
+    tc::mbar_init(bar_s, 1);
+    tc::mbar_init(bar_s + 1, 1);
+    tc::mbar_init(bar_o, 1);
+    tc::fence_mbar_init();
+  }
+  if (w == 0) {
+    tc::tmem_alloc(tbase_p, TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+
+  griddep_wait();  // q, k, v may come from the previous kernel on the stream
+  griddep_launch_dependents();
+
+  // Schedule. Tile n's softmax runs while the tensor core computes P V(n - 1) and S(n + 1): S is
+  // issued two tiles ahead (two S buffers in TMEM, two K part buffers), and P V(n - 1) is folded
+  // into O one tile late. Per tile n: (a) S(n) -> softmax -> p in registers; (b) P V(n - 1) -> O,
+  // then this thread's items of V(n) and K(n + 2) into their parts (both buffers now released);
+  // (c) p into P's parts; barrier; (d) issue P V(n) and S(n + 2); (e) stage V(n + 1), K(n + 3).
+  static_assert(TC_BM * 8 == 2 * TC_THREADS && TC_BN * 8 == TC_THREADS, "items per thread");
+  const bool mma_warp = w == TC_THREADS / 32;  // warp 16: issues every MMA, nothing else
+  // Prologue: Q (staged in the P buffer's first two slots), K(0), K(1) (its third slot) split;
+  // S(0), S(1) issued; K(2), V(0) in flight.
+  if (!mma_warp) {
+    stage_row_item(Pp, 0, tid, qp, a.q_ss, q0, S);
+    stage_row_item(Pp, 1, tid + TC_THREADS, qp, a.q_ss, q0, S);
+    stage_row_item(Kst, 0, tid, kp, a.k_ss, 0, S);
+    if (T > 1) stage_row_item(Pp, 2, tid, kp, a.k_ss, TC_BN, S);
+    cp_async_commit();
+    cp_async_wait_all();
+    split_row_item(Qp, PART_Q, Pp, 0, tid);
+    split_row_item(Qp, PART_Q, Pp, 1, tid + TC_THREADS);
+    split_row_item(sm + OFF_K, PART_K, Kst, 0, tid);
+    if (T > 1) split_row_item(sm + OFF_K + 3 * PART_K, PART_K, Pp, 2, tid);
+    if (T > 2) stage_row_item(Kst, 0, tid, kp, a.k_ss, 2 * TC_BN, S);
+    stage_vt_item(Vst, vp, a.v_ss, 0, S);
+    cp_async_commit();
+    tc::fence_async_smem();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = *tbase_p;
+  const uint32_t lane_sel = static_cast<uint32_t>(32 * (w & 3)) << 16;
+  const uint32_t t_obig = tbase + 256, t_osmall = tbase + 320;
+  bool err = false;
+
+  if (mma_warp) {
+    // S(0), S(1); then per tile, once its P, V and K(n + 2) parts are in place: P V(n), S(n + 2).
+    const uint32_t idesc = tc::idesc_f32acc(1, TC_BM, TC_BN);
+    const uint32_t sQ = tc::smem_u32(Qp), sV = tc::smem_u32(Vp), sP = tc::smem_u32(Pp);
+    const uint32_t sK0 = tc::smem_u32(sm + OFF_K);
+    if (lane == 0) {
+      issue_split_mma<PART_Q, PART_K>(tbase, tbase + 64, sQ, sK0, idesc);
+      tc::commit(bar_s);
+      if (T > 1) {
+        issue_split_mma<PART_Q, PART_K>(tbase + 128, tbase + 192, sQ, sK0 + 3 * PART_K, idesc);
+        tc::commit(bar_s + 1);
+      }
+    }
+    for (int n = 0; n < T; ++n) {
+      bar_sync(2, TC_BLOCK);
+      tc::fence_after_sync();
+      if (lane == 0) {
+        const int j = n & 1;
+        issue_split_mma<PART_Q, PART_K>(t_obig, t_osmall, sP, sV, idesc);
+        tc::commit(bar_o);
+        if (n + 2 < T) {
+          issue_split_mma<PART_Q, PART_K>(tbase + 128 * j, tbase + 128 * j + 64, sQ,
+                                          sK0 + 3 * PART_K * j, idesc);
+          tc::commit(bar_s + j);
+        }
+      }
+      __syncwarp();
+    }
+  }
+
+  // Online-softmax state of this thread's columns: acc holds O[row][CW cq + c] (unnormalised).
+  float m = -INFINITY, lpart = 0.0f, alpha_prev = 1.0f;
+  float acc[CW];
+#pragma unroll
+  for (int c = 0; c < CW; ++c) acc[c] = 0.0f;
+  const int qi = q0 + row;
+  float sv[CW], sw[CW];
+
+  // Every softmax thread waits for every commit itself; an expired wait is remembered (the outputs
+  // are then invalid) and the block runs on, so all threads keep to the same barriers.
+  for (int n = 0; n < T && !mma_warp; ++n) {
+    const int k0 = n * TC_BN, j = n & 1;
+    // (a) S(n) from TMEM; the online softmax.
+    err |= !tc::mbar_wait(bar_s + j, (n >> 1) & 1, WAIT_TIMEOUT_NS);
+    tc::fence_after_sync();
+    tmem_ld2(tbase + 128 * j + lane_sel + CW * cq, tbase + 128 * j + 64 + lane_sel + CW * cq, sv,
+             sw);
+    const bool edge = (k0 + TC_BN > S) || (CAUSAL && k0 + TC_BN - 1 > q0);
+    float tmax = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < CW; ++c) {
+      float x = (sv[c] + sw[c]) * a.scale;
+      if (edge) {
+        const int jj = k0 + CW * cq + c;
+        if (!(jj < S && !(CAUSAL && jj > qi))) x = -INFINITY;
+      }
+      sv[c] = x;
+      tmax = fmaxf(tmax, x);
+    }
+    red[NQ * row + cq] = tmax;
+    bar_sync(1, TC_THREADS);
+    tmax = red[NQ * row];
+#pragma unroll
+    for (int g = 1; g < NQ; ++g) tmax = fmaxf(tmax, red[NQ * row + g]);
+    const float m_new = fmaxf(m, tmax);
+    const float mu = m_new == -INFINITY ? 0.0f : m_new;  // a fully masked row keeps p = 0
+    const float alpha = expf(m - mu);
+    float psum = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CW; ++c) {
+      sv[c] = expf(sv[c] - mu);
+      psum += sv[c];
+    }
+    lpart = fmaf(lpart, alpha, psum);
+    m = m_new;
+    // (b) O += P V(n - 1); V(n), K(n + 2) into the parts P V(n - 1) and S(n) have released.
+    cp_async_wait_all();
+    if (n > 0) {
+      err |= !tc::mbar_wait(bar_o, (n - 1) & 1, WAIT_TIMEOUT_NS);
+      tc::fence_after_sync();
+      float ob[CW], os[CW];
+      tmem_ld2(t_obig + lane_sel + CW * cq, t_osmall + lane_sel + CW * cq, ob, os);
+#pragma unroll
+      for (int c = 0; c < CW; ++c) acc[c] = fmaf(acc[c], alpha_prev, ob[c] + os[c]);
+    }
+    split_vt_item(Vp, Vst);
+    if (n + 2 < T) split_row_item(sm + OFF_K + 3 * PART_K * j, PART_K, Kst, 0, tid);
+    // (c) p into P's parts; hand the tile to the MMA warp.
+#pragma unroll
+    for (int c8 = 0; c8 < CW / 8; ++c8) {
+      float x[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) x[u] = sv[8 * c8 + u];
+      store_parts(Pp, PART_Q, kmaj_off(row, (CW / 8) * cq + c8), x);
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    bar_sync(2, TC_BLOCK);
+    tc::fence_after_sync();
+    // (e) Refill this thread's staging slots.
+    if (n + 1 < T) stage_vt_item(Vst, vp, a.v_ss, (n + 1) * TC_BN, S);
+    if (n + 3 < T) stage_row_item(Kst, 0, tid, kp, a.k_ss, (n + 3) * TC_BN, S);
+    cp_async_commit();
+    alpha_prev = alpha;
+  }
+  if (!mma_warp) {
+    // The last tile's P V.
+    err |= !tc::mbar_wait(bar_o, (T - 1) & 1, WAIT_TIMEOUT_NS);
+    tc::fence_after_sync();
+    tmem_ld2(t_obig + lane_sel + CW * cq, t_osmall + lane_sel + CW * cq, sv, sw);
+#pragma unroll
+    for (int c = 0; c < CW; ++c) acc[c] = fmaf(acc[c], alpha_prev, sv[c] + sw[c]);
+    cp_async_wait_all();
+    red[NQ * row + cq] = lpart;
+  }
+  if (__syncthreads_or(err)) {
+    // A commit did not arrive in time: flag it, give the tensor core one more bounded wait for
+    // the last commits, free TMEM, write nothing.
+    if (tid == 0) atomicExch(&g_fwd_tc_err, 1);
+    tc::mbar_wait(bar_o, (T - 1) & 1, WAIT_TIMEOUT_NS);
+    tc::mbar_wait(bar_s + ((T - 1) & 1), ((T - 1) >> 1) & 1, WAIT_TIMEOUT_NS);
+  } else if (!mma_warp) {
+    float l = red[NQ * row];
+#pragma unroll
+    for (int g = 1; g < NQ; ++g) l += red[NQ * row + g];
+    if (qi < S) {
+      float* dst = a.o + ((static_cast<int64_t>(b) * S + qi) * a.H + h) * 64 + CW * cq;
+#pragma unroll
+      for (int c4 = 0; c4 < CW / 4; ++c4)
+        reinterpret_cast<float4*>(dst)[c4] =
+            make_float4(__fdiv_rn(acc[4 * c4], l), __fdiv_rn(acc[4 * c4 + 1], l),
+                        __fdiv_rn(acc[4 * c4 + 2], l), __fdiv_rn(acc[4 * c4 + 3], l));
+      if (cq == 0) a.lse[static_cast<int64_t>(bh) * S + qi] = m + logf(l);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (w == 0) tc::tmem_dealloc(tbase, TMEM_COLS);
+}
+
+}  // namespace
+
+int fwd_tc_tile_rows() { return TC_BM; }
+
+cudaError_t setup_fwd_tc_attributes() {
+  cudaError_t e = cudaFuncSetAttribute(fwd_tc_kernel<false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_ALLOC);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(fwd_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              TC_SMEM_ALLOC);
+}
+
+cudaError_t launch_fwd_tc(const FwdArgs& args, int causal, cudaStream_t stream) {
+  FwdArgs a = args;
+  a.n_qtiles = (a.S + TC_BM - 1) / TC_BM;
+  const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(a.n_qtiles) * a.B * a.H));
+  if (causal)
+    return launch_pdl(fwd_tc_kernel<true>, grid, dim3(TC_BLOCK), TC_SMEM_ALLOC, stream, a);
+  return launch_pdl(fwd_tc_kernel<false>, grid, dim3(TC_BLOCK), TC_SMEM_ALLOC, stream, a);
+}
+
+cudaError_t fwd_tc_status(int* flag) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_fwd_tc_err, sizeof(int));
+  if (e != cudaSuccess) return e;
+  *flag = v;
+  if (v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_fwd_tc_err, &zero, sizeof(int));
+  }
+  return e;
+}
+
+}  // namespace cfa

@@ -156,6 +156,15 @@ int cfa_bwd_f32_d64_noalloc(const float* q, const int64_t q_strides[3],
  * used `workspace` expired (its results are then invalid), else CFA_OK (or CFA_ERR_CUDA). */
 int cfa_bwd_status(const void* workspace, void* stream);
 
+/* Head-dim-64 forward implementation for this process: 0 = the CUDA-core FFMA kernel, 1 = the
+ * tensor-core kernel (fp32 from split bf16 products, csrc/fwd_tc.cu). Returns the previous choice,
+ * -1 for any other value. No counterpart in the reference (one kernel, kernels/fused_attn.cu:469). */
+int cfa_fwd_select(int impl);
+
+/* Synchronises `stream` and returns CFA_ERR_TIMEOUT if a bounded wait of a tensor-core forward
+ * since the last call expired (its outputs are then invalid), else CFA_OK; clears the flag. */
+int cfa_fwd_status(void* stream);
+
 /* Self-test of the failure detection (no counterpart in the reference, whose spin has no bound):
  * launches `blocks` blocks whose waits -- the bounded routine of the backward's dQ chain -- can
  * never be satisfied. Block 0 gives up after `timeout_ns`, the others bail out as soon as it has
