@@ -5,7 +5,9 @@ fp64 on canvas-shaped slices (s = 240, d = 64, seeded N(0,1)*0.5 inputs).
 
 Schemes: bf16 x3 split with 6 or 9 products, tf32 x2 (3 products) / x3 (6 products); the MMA
 accumulation modelled as round-to-nearest or truncating, into one accumulator or separate
-high/low-order accumulators.
+high/low-order accumulators; and "promoted" variants, in which the (truncating) TMEM accumulators
+start fresh every W MMA steps and each window's sums are added into fp32 registers with
+round-to-nearest (the scheme csrc/fwd_tc.cu uses, W = 4 steps of 16 = 64 elements).
 
     python baseline/split_precision_model.py
 """
@@ -60,6 +62,32 @@ def tc_gemm(A, B, scheme, rnd, K=16, sep=True):
             else: big = rnd(big + part)
     return rnd(big + small) if sep else big
 
+PAIRS6 = [(0, 0), (0, 1), (1, 0), (0, 2), (1, 1), (2, 0)]
+
+
+def tc_promoted(A, B, kind='bf16', n=3, K=16, W=4, sep=True, tmem_rnd=None):
+    """MMA steps of K reduction elements; TMEM accumulators (big / small, or one) fresh every W
+    steps and truncating per step; at each window's end its sums are added into fp32 registers
+    round-to-nearest; the result is big + small, round-to-nearest."""
+    tmem_rnd = tmem_rnd or rz32
+    sp = split_bf16 if kind == 'bf16' else split_tf32
+    As, Bs = sp(A, n), sp(B, n)
+    pairs = PAIRS6 if n == 3 else [(0, 0), (0, 1), (1, 0)]
+    m, kk = A.shape; nn = B.shape[1]
+    rb = torch.zeros(m, nn, dtype=torch.float64); rs = torch.zeros_like(rb)
+    tb = torch.zeros_like(rb); ts = torch.zeros_like(rb); steps = 0
+    for c in range(0, kk, K):
+        for (i, j) in pairs:
+            part = As[i][:, c:c+K] @ Bs[j][c:c+K, :]
+            if sep and (i, j) != (0, 0): ts = tmem_rnd(ts + part)
+            else: tb = tmem_rnd(tb + part)
+        steps += 1
+        if steps == W or c + K >= kk:
+            rb = rn32(rb + tb); rs = rn32(rs + ts)
+            tb = torch.zeros_like(rb); ts = torch.zeros_like(rb); steps = 0
+    return rn32(rb + rs) if sep else rb
+
+
 def ffma_gemm(A, B):  # sequential fp32 fma over k: emulate with float64 product + rn32 each step
     m, kk = A.shape; nn = B.shape[1]; acc = torch.zeros(m, nn, dtype=torch.float64)
     for c in range(kk):
@@ -105,6 +133,11 @@ for bh in range(4):
                        ('bf16x9 RZ sep', lambda A,B: tc_gemm(A,B,('bf16',9),rz32)),
                        ('tf32x2(3) RN sep', lambda A,B: tc_gemm(A,B,('tf32',2),rn32,K=8)),
                        ('tf32x3(6) RZ sep', lambda A,B: tc_gemm(A,B,('tf32',3),rz32,K=8)),
+                       ('bf16x3(6) RZ sep, promoted W=1', lambda A,B: tc_promoted(A,B,W=1)),
+                       ('bf16x3(6) RZ sep, promoted W=4', lambda A,B: tc_promoted(A,B,W=4)),
+                       ('bf16x3(6) RZ one, promoted W=4', lambda A,B: tc_promoted(A,B,W=4,sep=False)),
+                       ('bf16x3(6) RZ sep, no promotion', lambda A,B: tc_promoted(A,B,W=10**9)),
+                       ('tf32x2(3) RZ sep, promoted W=2', lambda A,B: tc_promoted(A,B,'tf32',2,8,W=2)),
                        ]:
         out = attention(q, k, v, do, 0.125, gemm)
         acc = res.setdefault(name, [[0,0] for _ in range(4)])

@@ -138,14 +138,16 @@ def _stream(dev: torch.device) -> int:
 # Launch wrappers (the src/cuda.rs role, over the C ABI)
 # ---------------------------------------------------------------------------------------------
 
-def attention_forward(q_ptr, qs, k_ptr, ks, v_ptr, vs, dims, scale, causal, device):
+def attention_forward(q_ptr, qs, k_ptr, ks, v_ptr, vs, dims, scale, causal, device,
+                      infer: bool = False):
     """One forward over device operands given as (pointer, (sb, sh, ss)): returns (O [b, s, h, d],
-    L [b, h, s]) as fresh tensors (the role of src/cuda.rs:140-185)."""
+    L [b, h, s]) as fresh tensors (the role of src/cuda.rs:140-185). `infer`: no backward will run
+    on these outputs -- the forward-only entry point (tensor cores at head dim 64)."""
     b, h, s, d = dims
     _check_head_dim(d)
     o = torch.empty((b, s, h, d), dtype=torch.float32, device=device)
     lse = torch.empty((b, h, s), dtype=torch.float32, device=device)
-    fwd = _abi.fwd if d == CUDA_HEAD_DIM else _abi.fwd_hd
+    fwd = _abi.fwd_infer if infer else (_abi.fwd if d == CUDA_HEAD_DIM else _abi.fwd_hd)
     with torch.cuda.device(device):
         st = fwd(q_ptr, qs, k_ptr, ks, v_ptr, vs, o.data_ptr(), lse.data_ptr(),
                  b, h, s, d, float(scale), causal, _stream(device))
@@ -188,13 +190,13 @@ class _FusedAttention(torch.autograd.Function):
     """CustomOp3 `FusedAttention` (src/lib.rs:383-491): [b, h, s, d] in, [b, s, h, d] out."""
 
     @staticmethod
-    def forward(ctx, q, k, v, scale, causal):
+    def forward(ctx, q, k, v, scale, causal, infer):
         dims = _check_shapes(q, k, v)
         dev = _check_device(q, k, v, who="fused_attention")
         if not all(float4_aligned(t) for t in (q, k, v)):
             raise FusedAttentionError("fused_attention: rows must be 16-byte aligned")
         o, lse = attention_forward(q.data_ptr(), _bhs_strides(q), k.data_ptr(), _bhs_strides(k),
-                                   v.data_ptr(), _bhs_strides(v), dims, scale, causal, dev)
+                                   v.data_ptr(), _bhs_strides(v), dims, scale, causal, dev, infer)
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.scale, ctx.causal, ctx.dims = scale, causal, dims
         return o
@@ -209,21 +211,22 @@ class _FusedAttention(torch.autograd.Function):
             _bhs_strides(v), o, lse, grad.data_ptr(), (gb, gh, gs), ctx.dims, ctx.scale,
             ctx.causal, q.device)
         part = lambda i: dqkv[:, :, i].transpose(1, 2)  # noqa: E731  (src/lib.rs:484)
-        return part(0), part(1), part(2), None, None
+        return part(0), part(1), part(2), None, None, None
 
 
 class _FusedAttentionQkv(torch.autograd.Function):
     """CustomOp1 `FusedAttentionQkv` (src/lib.rs:494-590): qkv in, merged [b, s, h*d] out."""
 
     @staticmethod
-    def forward(ctx, qkv, heads, scale, causal):
+    def forward(ctx, qkv, heads, scale, causal, infer):
         _check_device(qkv, who="fused_attention_qkv")
         dims, strides, offs = qkv_geometry(tuple(qkv.shape), qkv.stride(), heads)
         if qkv.storage_offset() % 4 != 0 or any(x % 4 != 0 for x in strides):
             raise FusedAttentionError("fused_attention_qkv: rows must be 16-byte aligned")
         base = qkv.data_ptr()
         o, lse = attention_forward(base + 4 * offs[0], strides, base + 4 * offs[1], strides,
-                                   base + 4 * offs[2], strides, dims, scale, causal, qkv.device)
+                                   base + 4 * offs[2], strides, dims, scale, causal, qkv.device,
+                                   infer)
         ctx.save_for_backward(qkv, o, lse)
         ctx.heads, ctx.scale, ctx.causal = heads, scale, causal
         b, h, s, d = dims
@@ -242,7 +245,14 @@ class _FusedAttentionQkv(torch.autograd.Function):
         dqkv = attention_backward(
             base + 4 * offs[0], strides, base + 4 * offs[1], strides, base + 4 * offs[2], strides,
             o, lse, grad.data_ptr(), (gb, d, gs), dims, ctx.scale, ctx.causal, qkv.device)
-        return dqkv.view(b, s, 3 * h * d), None, None, None
+        return dqkv.view(b, s, 3 * h * d), None, None, None, None
+
+
+def _records_backward(*inputs: torch.Tensor) -> bool:
+    """Whether autograd records this call (grad mode on and an input requiring a gradient). When it
+    does not -- inference, torch.no_grad -- no backward will consume the forward's L, and the
+    forward-only entry point (tensor cores at head dim 64) runs."""
+    return torch.is_grad_enabled() and any(t.requires_grad for t in inputs)
 
 
 def fused_attention_qkv(qkv: torch.Tensor, heads: int, scale: float, causal: bool) -> torch.Tensor:
@@ -253,7 +263,8 @@ def fused_attention_qkv(qkv: torch.Tensor, heads: int, scale: float, causal: boo
                and st[0] % 4 == 0 and st[1] % 4 == 0)
     if not aligned:
         qkv = qkv.contiguous()
-    return _FusedAttentionQkv.apply(qkv, int(heads), float(scale), bool(causal))
+    return _FusedAttentionQkv.apply(qkv, int(heads), float(scale), bool(causal),
+                                    not _records_backward(qkv))
 
 
 def fused_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
@@ -261,7 +272,8 @@ def fused_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
     """src/lib.rs:143-161. q, k, v [batch, heads, seq, d] f32 on CUDA (d in HEAD_DIMS), any
     strides -> [batch, heads, seq, d] (a transposed view of a dense [batch, seq, heads, d] buffer)."""
     q, k, v = _float4_rows(q), _float4_rows(k), _float4_rows(v)
-    return _FusedAttention.apply(q, k, v, float(scale), bool(causal)).transpose(1, 2)
+    return _FusedAttention.apply(q, k, v, float(scale), bool(causal),
+                                 not _records_backward(q, k, v)).transpose(1, 2)
 
 
 from .host_pipeline import HostPipeline  # noqa: E402  (uses _abi; public host-buffer API)

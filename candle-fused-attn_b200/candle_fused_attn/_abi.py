@@ -44,6 +44,7 @@ EXPORTS = (
     "cfa_bwd_f32",
     "cfa_fwd_select",
     "cfa_fwd_status",
+    "cfa_fwd_f32_infer",
 )
 
 # Head-dim-64 forward implementations (cfa_fwd_select).
@@ -104,6 +105,8 @@ def load() -> ctypes.CDLL:
     lib.cfa_fwd_f32.argtypes = lib.cfa_fwd_f32_d64.argtypes
     lib.cfa_bwd_f32.restype = ctypes.c_int
     lib.cfa_bwd_f32.argtypes = lib.cfa_bwd_f32_d64.argtypes
+    lib.cfa_fwd_f32_infer.restype = ctypes.c_int
+    lib.cfa_fwd_f32_infer.argtypes = lib.cfa_fwd_f32_d64.argtypes
     lib.cfa_fwd_select.restype = ctypes.c_int
     lib.cfa_fwd_select.argtypes = [ctypes.c_int]
     lib.cfa_fwd_status.restype = ctypes.c_int
@@ -158,6 +161,14 @@ def fwd_hd(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, b, h, s, d, scale, c
            stream) -> int:
     """cfa_fwd_f32 (head dim d in HEAD_DIMS); returns the status."""
     return load().cfa_fwd_f32(
+        q_ptr, strides3(qs), k_ptr, strides3(ks), v_ptr, strides3(vs), o_ptr, lse_ptr,
+        b, h, s, d, ctypes.c_float(scale), int(bool(causal)), stream)
+
+
+def fwd_infer(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, b, h, s, d, scale, causal,
+              stream) -> int:
+    """cfa_fwd_f32_infer (forward only: the tensor-core kernel at head dim 64); the status."""
+    return load().cfa_fwd_f32_infer(
         q_ptr, strides3(qs), k_ptr, strides3(ks), v_ptr, strides3(vs), o_ptr, lse_ptr,
         b, h, s, d, ctypes.c_float(scale), int(bool(causal)), stream)
 

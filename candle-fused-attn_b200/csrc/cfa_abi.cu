@@ -27,7 +27,9 @@ DeviceOnce g_fwd_once[kMaxDevices];
 DeviceOnce g_bwd_once[kMaxDevices];
 DeviceOnce g_hd_once[kMaxDevices];  // head dims 32 and 128
 DeviceOnce g_fwd_tc_once[kMaxDevices];
-// Head-dim-64 forward: 0 = CUDA-core FFMA kernel, 1 = tensor-core kernel (cfa_fwd_select).
+// Head-dim-64 forward of cfa_fwd_f32_d64 / cfa_fwd_f32: 0 = CUDA-core FFMA kernel (the default:
+// its scores are bit-identical to the backward's recomputation), 1 = tensor-core kernel
+// (cfa_fwd_select). cfa_fwd_f32_infer always takes the tensor-core kernel at head dim 64.
 std::atomic<int> g_fwd_impl{0};
 
 int setup(DeviceOnce* table, cudaError_t (*fn)()) {
@@ -70,7 +72,7 @@ int check_dims(int64_t B, int64_t H, int64_t S, int64_t D, bool any_dim, bool* e
 int fwd_impl(const float* q, const int64_t q_strides[3], const float* k,
              const int64_t k_strides[3], const float* v, const int64_t v_strides[3], float* o,
              float* lse, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, float scale,
-             int causal, void* stream, bool any_dim) {
+             int causal, void* stream, bool any_dim, int impl) {
   bool empty = false;
   int st = check_dims(batch, heads, seq, head_dim, any_dim, &empty);
   if (st != CFA_OK || empty) return st;
@@ -79,7 +81,7 @@ int fwd_impl(const float* q, const int64_t q_strides[3], const float* k,
   if (!strides_ok(q_strides) || !strides_ok(k_strides) || !strides_ok(v_strides))
     return CFA_ERR_ALIGNMENT;
   const bool d64 = head_dim == 64;
-  const bool tc = d64 && g_fwd_impl.load(std::memory_order_relaxed) == 1;
+  const bool tc = d64 && (impl < 0 ? g_fwd_impl.load(std::memory_order_relaxed) : impl) == 1;
   st = tc    ? setup(g_fwd_tc_once, cfa::setup_fwd_tc_attributes)
        : d64 ? setup(g_fwd_once, cfa::setup_fwd_attributes)
              : setup(g_hd_once, cfa::setup_hd_attributes);
@@ -230,7 +232,7 @@ int cfa_fwd_f32_d64(const float* q, const int64_t q_strides[3], const float* k,
                     float* o, float* lse, int64_t batch, int64_t heads, int64_t seq,
                     int64_t head_dim, float scale, int causal, void* stream) {
   return fwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, batch, heads, seq, head_dim,
-                  scale, causal, stream, false);
+                  scale, causal, stream, false, -1);
 }
 
 int cfa_fwd_f32(const float* q, const int64_t q_strides[3], const float* k,
@@ -238,7 +240,15 @@ int cfa_fwd_f32(const float* q, const int64_t q_strides[3], const float* k,
                 float* lse, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                 float scale, int causal, void* stream) {
   return fwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, batch, heads, seq, head_dim,
-                  scale, causal, stream, true);
+                  scale, causal, stream, true, -1);
+}
+
+int cfa_fwd_f32_infer(const float* q, const int64_t q_strides[3], const float* k,
+                      const int64_t k_strides[3], const float* v, const int64_t v_strides[3],
+                      float* o, float* lse, int64_t batch, int64_t heads, int64_t seq,
+                      int64_t head_dim, float scale, int causal, void* stream) {
+  return fwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, batch, heads, seq, head_dim,
+                  scale, causal, stream, true, 1);
 }
 
 size_t cfa_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq) {

@@ -156,10 +156,25 @@ int cfa_bwd_f32_d64_noalloc(const float* q, const int64_t q_strides[3],
  * used `workspace` expired (its results are then invalid), else CFA_OK (or CFA_ERR_CUDA). */
 int cfa_bwd_status(const void* workspace, void* stream);
 
-/* Head-dim-64 forward implementation for this process: 0 = the CUDA-core FFMA kernel, 1 = the
- * tensor-core kernel (fp32 from split bf16 products, csrc/fwd_tc.cu). Returns the previous choice,
- * -1 for any other value. No counterpart in the reference (one kernel, kernels/fused_attn.cu:469). */
+/* Head-dim-64 forward of cfa_fwd_f32_d64 / cfa_fwd_f32 for this process: 0 = the CUDA-core FFMA
+ * kernel (the default), 1 = the tensor-core kernel (fp32 from split bf16 products with fp32
+ * promotion, csrc/fwd_tc.cu). Returns the previous choice, -1 for any other value. No counterpart
+ * in the reference (one kernel, kernels/fused_attn.cu:469). The default keeps the forward's scores
+ * bit-identical to the backward's recomputation of them, which the backward's accuracy relies on. */
 int cfa_fwd_select(int impl);
+
+/* The forward for callers that run no backward on its outputs (inference, evaluation): as
+ * cfa_fwd_f32 (head dims 32, 64, 128), with the tensor-core kernel at head dim 64 -- 1.4-2.3x
+ * faster than the FFMA kernel on the BASELINE configs and closer to fp64 (O 9.4e-8 vs 2.9e-7 at
+ * the canvas shape). L is written too, but a backward fed with it recomputes the scores in another
+ * rounding and drifts from the reference's CPU gradients by up to 1.4x its 5e-6 band. No
+ * counterpart in the reference. */
+int cfa_fwd_f32_infer(const float* q, const int64_t q_strides[3],
+                      const float* k, const int64_t k_strides[3],
+                      const float* v, const int64_t v_strides[3],
+                      float* o, float* lse,
+                      int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                      float scale, int causal, void* stream);
 
 /* Synchronises `stream` and returns CFA_ERR_TIMEOUT if a bounded wait of a tensor-core forward
  * since the last call expired (its outputs are then invalid), else CFA_OK; clears the flag. */

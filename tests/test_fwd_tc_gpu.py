@@ -1,5 +1,7 @@
 # SPDX-License-Identifier: MIT OR Apache-2.0
-"""The tensor-core forward (csrc/fwd_tc.cu, selected with cfa_fwd_select(1)) against the CPU oracle.
+"""The tensor-core forward (csrc/fwd_tc.cu) against the CPU oracle. It runs for forward-only calls
+(cfa_fwd_f32_infer; the Python API takes it when no input needs a gradient) and, selected with
+cfa_fwd_select(1), for every head-dim-64 forward.
 
 Same bar as the FFMA forward (tests/parity.rs:161-167, :210-221 and the north star): 1e-5
 normwise and a 5e-6 max-abs band (scaled by the output magnitude) against the fp32 composed path
@@ -105,7 +107,7 @@ def test_accuracy_vs_fp64(tc):
     o_tc = cfa.fused_attention_qkv(x, h, 0.125, False).cpu().double()
     status_ok()
     _abi.fwd_select(_abi.FWD_FFMA)
-    o_ff = cfa.fused_attention_qkv(x, h, 0.125, False).cpu().double()
+    o_ff = cfa.fused_attention_qkv(x.requires_grad_(True), h, 0.125, False).detach().cpu().double()
     _abi.fwd_select(_abi.FWD_TC)
     e_tc, e_ff = oracle.normwise(o_tc, o64), oracle.normwise(o_ff, o64)
     print(f"O vs fp64: tensor cores {e_tc:.3e}, FFMA {e_ff:.3e}")
@@ -121,3 +123,22 @@ def test_long_causal_slice(tc):
     out = cfa.fused_attention_qkv(qkv.to(tc), h, 0.125, True)
     status_ok()
     check(out.cpu(), o_ref.reshape(b, s, -1), "O")
+
+
+def test_forward_only_calls_take_the_tensor_cores(cuda):
+    """Default selection: a call that records no backward (no input needs a gradient) runs the
+    tensor-core kernel; one that does runs the FFMA kernel, whose scores the backward recomputes
+    bit for bit."""
+    assert _abi.fwd_select(_abi.FWD_FFMA) == _abi.FWD_FFMA  # the default
+    qkv, _ = oracle.seeded_inputs(2, 6, 240, 9, 0.5)
+    x = qkv.to(cuda)
+    o_infer = cfa.fused_attention_qkv(x, 6, 0.125, False)
+    with torch.no_grad():
+        o_nograd = cfa.fused_attention_qkv(x.clone().requires_grad_(True), 6, 0.125, False)
+    o_train = cfa.fused_attention_qkv(x.clone().requires_grad_(True), 6, 0.125, False).detach()
+    _abi.fwd_select(_abi.FWD_TC)
+    o_tc = cfa.fused_attention_qkv(x.clone().requires_grad_(True), 6, 0.125, False).detach()
+    _abi.fwd_select(_abi.FWD_FFMA)
+    status_ok()
+    assert torch.equal(o_infer, o_tc) and torch.equal(o_nograd, o_tc)
+    assert not torch.equal(o_train, o_tc)
