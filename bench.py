@@ -65,6 +65,7 @@ def peaks():
     mhz = float(mp.get("sm_max_mhz", 1965.0))
     return {
         "ffma_tflops": 148 * 128 * 2 * mhz * 1e6 / 1e12,
+        "bf16_tflops": float(mp.get("bf16_tflops", 1590.0)),
         "hbm_gbs": float(mp.get("hbm_gbs", 6650.0)),
         "source": ("FFMA: 148 SMs x 128 FMA/clk x 2 x sm_max_mhz " + str(mhz) +
                    (" (MEASURED_PEAKS.json)" if "sm_max_mhz" in mp else " (fallback)")),
@@ -155,6 +156,14 @@ class OursStep:
         rc = self.abi.fwd(self.ptr[0], self.st, self.ptr[1], self.st, self.ptr[2], self.st,
                           self.o.data_ptr(), self.lse.data_ptr(), self.b, H, S, D, SCALE, CAUSAL,
                           stream)
+        if rc:
+            raise RuntimeError(self.abi.strerror(rc))
+
+    def fwd_infer(self, stream):
+        """The forward-only entry point (tensor cores at head dim 64)."""
+        rc = self.abi.fwd_infer(self.ptr[0], self.st, self.ptr[1], self.st, self.ptr[2], self.st,
+                                self.o.data_ptr(), self.lse.data_ptr(), self.b, H, S, D, SCALE,
+                                CAUSAL, stream)
         if rc:
             raise RuntimeError(self.abi.strerror(rc))
 
@@ -351,6 +360,9 @@ def main():
     ap.add_argument("--only", default="", help="suite: run the configs whose name contains this")
     ap.add_argument("--head-dim", type=int, default=D,
                     help="kernels mode: the canvas-shaped projection as heads of this dim (32, 128)")
+    ap.add_argument("--forward", choices=["ffma", "tc"], default="ffma",
+                    help="kernels mode: the head-dim-64 forward of the fwd+bwd step (tc: the "
+                         "tensor-core kernel that forward-only calls take)")
     ap.add_argument("--mode", choices=["full", "kernels", "suite"], default="full",
                     help="kernels: warm-up + `steps` plain steps, no timing (for ncu); "
                          "suite: every BASELINE config, ours vs the reference kernel")
@@ -414,6 +426,8 @@ def main():
     torch.cuda.synchronize()
 
     if args.mode == "kernels":  # a fixed, short launch sequence for ncu
+        from candle_fused_attn import _abi
+        _abi.fwd_select(_abi.FWD_TC if args.forward == "tc" else _abi.FWD_FFMA)
         for i in range(args.steps):
             step(i)
         torch.cuda.synchronize()
@@ -442,6 +456,10 @@ def main():
     # per-kernel split: forward alone, backward alone (prep + main), same rotation
     fwd_ms = timed(lambda i: sets[i % N_SETS].fwd(sh), args.steps, stream)
     bwd_ms = timed(lambda i: sets[i % N_SETS].bwd(sh), args.steps, stream)
+    # the forward-only entry point (tensor-core kernel), which inference calls take
+    infer_ms = timed(lambda i: sets[i % N_SETS].fwd_infer(sh), args.steps, stream)
+    if sets[0].abi.fwd_status(sh) != sets[0].abi.CFA_OK:
+        raise RuntimeError("tensor-core forward: a bounded wait expired")
 
     # e2e through the public API with pinned host buffers: HostPipeline streams batch chunks
     # through H2D / kernels / D2H on three streams (the timed region spans every copy).
@@ -565,6 +583,14 @@ def main():
         "tflops_per_gpu": value / world,
         "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
         "fwd_tflops": flops(b, H, S, D, CAUSAL, "fwd") / (fwd_ms * 1e-3) / 1e12,
+        "forward_only": {
+            "ms": infer_ms, "tflops": flops(b, H, S, D, CAUSAL, "fwd") / (infer_ms * 1e-3) / 1e12,
+            "kernel": "fwd_tc_kernel (cfa_fwd_f32_infer): tcgen05, fp32 from 6 bf16 split products",
+            "tensor_frac": 6 * flops(b, H, S, D, CAUSAL, "fwd") / (infer_ms * 1e-3) / 1e12
+            / pk["bf16_tflops"],
+            "tensor_peak": pk["bf16_tflops"],
+            "note": "not part of the fwd+bwd step: training keeps the FFMA forward, whose scores "
+                    "the backward recomputes bit for bit"},
         "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": (sets[0].qkv.numel() + sets[0].dout.numel()) * 4,
