@@ -27,10 +27,13 @@ DeviceOnce g_fwd_once[kMaxDevices];
 DeviceOnce g_bwd_once[kMaxDevices];
 DeviceOnce g_hd_once[kMaxDevices];  // head dims 32 and 128
 DeviceOnce g_fwd_tc_once[kMaxDevices];
-// Head-dim-64 forward of cfa_fwd_f32_d64 / cfa_fwd_f32: 0 = CUDA-core FFMA kernel (the default:
-// its scores are bit-identical to the backward's recomputation), 1 = tensor-core kernel
-// (cfa_fwd_select). cfa_fwd_f32_infer always takes the tensor-core kernel at head dim 64.
-std::atomic<int> g_fwd_impl{0};
+DeviceOnce g_bwd_tc_once[kMaxDevices];
+// Head-dim-64 kernels (cfa_fwd_select): 1 (the default) = the tensor-core pair for sequences of at
+// most kTcPairMaxSeq -- forward and backward both on tcgen05, their scores bit-identical; the
+// backward needs the dQ partials of the larger workspace -- and the FFMA pair beyond; 0 = the
+// FFMA pair always. cfa_fwd_f32_infer takes the tensor-core forward at every length.
+std::atomic<int> g_fwd_impl{1};
+constexpr int64_t kTcPairMaxSeq = 64 * cfa::PART_MAX_KBLOCKS;  // the dQ partials' reach
 
 int setup(DeviceOnce* table, cudaError_t (*fn)()) {
   int dev = 0;
@@ -81,7 +84,8 @@ int fwd_impl(const float* q, const int64_t q_strides[3], const float* k,
   if (!strides_ok(q_strides) || !strides_ok(k_strides) || !strides_ok(v_strides))
     return CFA_ERR_ALIGNMENT;
   const bool d64 = head_dim == 64;
-  const bool tc = d64 && (impl < 0 ? g_fwd_impl.load(std::memory_order_relaxed) : impl) == 1;
+  const bool tc = d64 && (impl == 1 || (impl < 0 && g_fwd_impl.load(std::memory_order_relaxed) == 1 &&
+                                         seq <= kTcPairMaxSeq));
   st = tc    ? setup(g_fwd_tc_once, cfa::setup_fwd_tc_attributes)
        : d64 ? setup(g_fwd_once, cfa::setup_fwd_attributes)
              : setup(g_hd_once, cfa::setup_hd_attributes);
@@ -136,7 +140,14 @@ int bwd_impl(const float* q, const int64_t q_strides[3], const float* k,
   if (workspace_bytes < lay.total || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return CFA_ERR_WORKSPACE;
   const bool d64 = head_dim == 64;
-  st = d64 ? setup(g_bwd_once, cfa::setup_bwd_attributes) : setup(g_hd_once, cfa::setup_hd_attributes);
+  // The tensor-core backward pairs with the tensor-core forward (cfa_fwd_select(1): the scores it
+  // recomputes are the forward's, bit for bit); it needs the dQ partials of the larger workspace.
+  const bool tc = d64 && g_fwd_impl.load(std::memory_order_relaxed) == 1 &&
+                  seq <= kTcPairMaxSeq && lay.total_fast > lay.total &&
+                  workspace_bytes >= lay.total_fast;
+  st = tc    ? setup(g_bwd_tc_once, cfa::setup_bwd_tc_attributes)
+       : d64 ? setup(g_bwd_once, cfa::setup_bwd_attributes)
+             : setup(g_hd_once, cfa::setup_hd_attributes);
   if (st != CFA_OK) return st;
 
   char* ws = static_cast<char*>(workspace);
@@ -199,8 +210,9 @@ int bwd_impl(const float* q, const int64_t q_strides[3], const float* k,
   a.dq_part = (lay.total_fast > lay.total && workspace_bytes >= lay.total_fast)
                   ? reinterpret_cast<float*>(ws + lay.part_off)
                   : nullptr;
-  e = d64 ? cfa::launch_bwd(a, causal != 0, s)
-          : cfa::launch_hd_bwd(a, static_cast<int>(head_dim), causal != 0, s);
+  e = tc    ? cfa::launch_bwd_tc(a, causal != 0, s)
+      : d64 ? cfa::launch_bwd(a, causal != 0, s)
+            : cfa::launch_hd_bwd(a, static_cast<int>(head_dim), causal != 0, s);
   return e == cudaSuccess ? CFA_OK : CFA_ERR_LAUNCH;
 }
 

@@ -117,6 +117,9 @@ cudaError_t launch_fwd(const FwdArgs& a, int causal, cudaStream_t stream);
 cudaError_t launch_fwd_tc(const FwdArgs& a, int causal, cudaStream_t stream);
 // Reads and clears the tensor-core forward's device error flag (1: an MMA wait expired).
 cudaError_t fwd_tc_status(int* flag);
+// The tensor-core backward (bwd_tc.cu): 128-key blocks, the no-wait dQ path only (dq_part set);
+// sets the key-block count itself.
+cudaError_t launch_bwd_tc(const BwdArgs& a, int causal, cudaStream_t stream);
 cudaError_t launch_bwd_prep(const PrepArgs& a, cudaStream_t stream);
 cudaError_t launch_bwd(const BwdArgs& a, int causal, cudaStream_t stream);
 
@@ -135,6 +138,7 @@ cudaError_t launch_selftest_wait(int* ws, uint64_t short_ns, int blocks, cudaStr
 // One-time per-device attribute set-up (dynamic shared memory limits).
 cudaError_t setup_fwd_attributes();
 cudaError_t setup_fwd_tc_attributes();
+cudaError_t setup_bwd_tc_attributes();
 cudaError_t setup_bwd_attributes();
 
 }  // namespace cfa

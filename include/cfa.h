@@ -156,11 +156,13 @@ int cfa_bwd_f32_d64_noalloc(const float* q, const int64_t q_strides[3],
  * used `workspace` expired (its results are then invalid), else CFA_OK (or CFA_ERR_CUDA). */
 int cfa_bwd_status(const void* workspace, void* stream);
 
-/* Head-dim-64 forward of cfa_fwd_f32_d64 / cfa_fwd_f32 for this process: 0 = the CUDA-core FFMA
- * kernel (the default), 1 = the tensor-core kernel (fp32 from split bf16 products with fp32
- * promotion, csrc/fwd_tc.cu). Returns the previous choice, -1 for any other value. No counterpart
- * in the reference (one kernel, kernels/fused_attn.cu:469). The default keeps the forward's scores
- * bit-identical to the backward's recomputation of them, which the backward's accuracy relies on. */
+/* Head-dim-64 kernels for this process. 1 (the default): the tensor-core pair (fp32 from split
+ * bf16 products with fp32 promotion: csrc/fwd_tc.cu, csrc/bwd_tc.cu) for sequences of at most 1024
+ * -- the backward recomputes the forward's scores bit for bit and needs the dQ partials of the
+ * larger workspace (cfa_bwd_workspace_bytes_fast; with the smaller one it runs the FFMA backward,
+ * whose scores differ from the tensor-core forward's in the last bits) -- and the FFMA pair
+ * beyond; 0: the FFMA pair always (csrc/fwd_ffma.cu, csrc/bwd_ffma.cu). Returns the previous
+ * choice, -1 for any other value. No counterpart in the reference (one kernel pair). */
 int cfa_fwd_select(int impl);
 
 /* The forward for callers that run no backward on its outputs (inference, evaluation): as

@@ -30,6 +30,15 @@ void oracle_bwd_f32(const float* q, const int64_t* qs, const float* k, const int
                     const float* dout, const int64_t* dos, int64_t B, int64_t H, int64_t S,
                     int64_t D, double scale, int causal, float* dqkv, int threads,
                     int64_t bh_begin, int64_t bh_end);
+void oracle_fwd_f64(const float* q, const int64_t* qs, const float* k, const int64_t* ks,
+                    const float* v, const int64_t* vs, int64_t B, int64_t H, int64_t S, int64_t D,
+                    double scale, int causal, double* o, double* lse, int threads,
+                    int64_t bh_begin, int64_t bh_end);
+void oracle_bwd_f64(const float* q, const int64_t* qs, const float* k, const int64_t* ks,
+                    const float* v, const int64_t* vs, const double* o, const double* lse,
+                    const float* dout, const int64_t* dos, int64_t B, int64_t H, int64_t S,
+                    int64_t D, double scale, int causal, double* dqkv, int threads,
+                    int64_t bh_begin, int64_t bh_end);
 }
 
 namespace cfa = candle_fused_attn;
@@ -88,6 +97,38 @@ void oracle(size_t b, size_t s, size_t h, size_t d, bool causal, const std::vect
                  B * H);
 }
 
+// The composed path in fp64 (the accuracy reference) on the same projection.
+void oracle64(size_t b, size_t s, size_t h, size_t d, bool causal, const std::vector<float>& x,
+              const std::vector<float>& w, std::vector<double>& o, std::vector<double>& g) {
+  const int64_t hd = static_cast<int64_t>(h * d);
+  const int64_t st[3] = {static_cast<int64_t>(s) * 3 * hd, static_cast<int64_t>(d), 3 * hd};
+  const int64_t dst[3] = {static_cast<int64_t>(s) * hd, static_cast<int64_t>(d), hd};
+  std::vector<double> lse(b * h * s);
+  o.resize(b * s * h * d);
+  g.resize(b * s * 3 * h * d);
+  const double scale = 1.0 / std::sqrt(static_cast<double>(d));
+  const int64_t B = b, H = h, S = s, D = d;
+  oracle_fwd_f64(x.data(), st, x.data() + hd, st, x.data() + 2 * hd, st, B, H, S, D, scale,
+                 causal, o.data(), lse.data(), 0, 0, B * H);
+  oracle_bwd_f64(x.data(), st, x.data() + hd, st, x.data() + 2 * hd, st, o.data(), lse.data(),
+                 w.data(), dst, B, H, S, D, scale, causal, g.data(), 0, 0, B * H);
+}
+
+// Elements farther than `band` from the fp32 composed path that are also farther from the fp64
+// one than that fp32 result is (by more than 1e-7): the reference's band of tests/parity.rs:218,
+// with the tie going to the exact answer where the fp32 CPU result is itself off by more than the
+// band (its dV sums for the first causal rows at |dV| ~ 5.6: up to 6.5e-6 off fp64).
+size_t band_failures(const std::vector<float>& got, const std::vector<float>& ref32,
+                     const std::vector<double>& ref64, float band) {
+  size_t n = 0;
+  for (size_t i = 0; i < got.size(); ++i) {
+    if (std::fabs(got[i] - ref32[i]) < band) continue;
+    if (std::fabs(got[i] - ref64[i]) > std::fabs(static_cast<double>(ref32[i]) - ref64[i]) + 1e-7)
+      ++n;
+  }
+  return n;
+}
+
 float max_abs(const std::vector<float>& a, const std::vector<float>& b) {
   float m = 0.0f;
   for (size_t i = 0; i < a.size(); ++i) m = std::fmax(m, std::fabs(a[i] - b[i]));
@@ -133,12 +174,17 @@ void attend(Path path, const std::vector<float>& x, const std::vector<float>& w,
 // tests/parity.rs:141-159 / :210-221.
 void check(Path path, size_t b, size_t s, size_t h, size_t d, bool causal, float band) {
   std::vector<float> x, w, o_ref, g_ref, o, g;
+  std::vector<double> o64, g64;
   inputs(b, s, h, d, x, w);
   oracle(b, s, h, d, causal, x, w, o_ref, g_ref);
+  oracle64(b, s, h, d, causal, x, w, o64, g64);
   attend(path, x, w, b, s, h, d, causal, o, g);
-  const float eo = max_abs(o, o_ref), eg = max_abs(g, g_ref);
-  EXPECT(eo < band && eg < band, "%s (%zu,%zu,%zu,%zu) causal=%d: max-abs O %.2e dqkv %.2e",
-         path == Path::Fused ? "fused" : "fused_qkv", b, s, h, d, causal ? 1 : 0, eo, eg);
+  const size_t fo = band_failures(o, o_ref, o64, band), fg = band_failures(g, g_ref, g64, band);
+  EXPECT(fo == 0 && fg == 0,
+         "%s (%zu,%zu,%zu,%zu) causal=%d: max-abs O %.2e dqkv %.2e; beyond the band and farther "
+         "from fp64 than the fp32 CPU result: %zu / %zu elements",
+         path == Path::Fused ? "fused" : "fused_qkv", b, s, h, d, causal ? 1 : 0,
+         max_abs(o, o_ref), max_abs(g, g_ref), fo, fg);
 }
 
 // ---- tests ------------------------------------------------------------------------------------
@@ -266,8 +312,10 @@ void errors_on_device() {
   // (src/lib.rs:111-118): the results match the oracle on the same values.
   const size_t b = 1, s = 40, h = 2, d = 64, row = 3 * h * d;
   std::vector<float> x, w, o_ref, g_ref;
+  std::vector<double> o64, g64;
   inputs(b, s, h, d, x, w);
   oracle(b, s, h, d, false, x, w, o_ref, g_ref);
+  oracle64(b, s, h, d, false, x, w, o64, g64);
   std::vector<float> padded(b * s * (row + 2), 0.0f);
   for (size_t r = 0; r < b * s; ++r)
     std::memcpy(&padded[r * (row + 2)], &x[r * row], row * sizeof(float));
@@ -281,7 +329,8 @@ void errors_on_device() {
          "the op saw a contiguous copy");
   const std::vector<float> o = r.out.to_host();
   const std::vector<float> g = r.backward(Tensor::from_host(w, {b, s, h * d})).to_host();
-  EXPECT(max_abs(o, o_ref) < 5e-6f && max_abs(g, g_ref) < 5e-6f, "padded-row projection");
+  EXPECT(band_failures(o, o_ref, o64, 5e-6f) == 0 && band_failures(g, g_ref, g64, 5e-6f) == 0,
+         "padded-row projection");
 }
 
 }  // namespace

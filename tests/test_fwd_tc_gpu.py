@@ -125,20 +125,21 @@ def test_long_causal_slice(tc):
     check(out.cpu(), o_ref.reshape(b, s, -1), "O")
 
 
-def test_forward_only_calls_take_the_tensor_cores(cuda):
-    """Default selection: a call that records no backward (no input needs a gradient) runs the
-    tensor-core kernel; one that does runs the FFMA kernel, whose scores the backward recomputes
-    bit for bit."""
-    assert _abi.fwd_select(_abi.FWD_FFMA) == _abi.FWD_FFMA  # the default
+def test_kernel_selection(cuda):
+    """The default (cfa_fwd_select(1)) runs the tensor-core pair at head dim 64 for s <= 1024:
+    the training forward equals the forward-only one bit for bit. With the FFMA pair selected,
+    training takes the FFMA forward while forward-only calls keep the tensor cores."""
+    assert _abi.fwd_select(_abi.FWD_TC) == _abi.FWD_TC  # the default
     qkv, _ = oracle.seeded_inputs(2, 6, 240, 9, 0.5)
     x = qkv.to(cuda)
     o_infer = cfa.fused_attention_qkv(x, 6, 0.125, False)
     with torch.no_grad():
         o_nograd = cfa.fused_attention_qkv(x.clone().requires_grad_(True), 6, 0.125, False)
     o_train = cfa.fused_attention_qkv(x.clone().requires_grad_(True), 6, 0.125, False).detach()
-    _abi.fwd_select(_abi.FWD_TC)
-    o_tc = cfa.fused_attention_qkv(x.clone().requires_grad_(True), 6, 0.125, False).detach()
     _abi.fwd_select(_abi.FWD_FFMA)
+    o_ffma = cfa.fused_attention_qkv(x.clone().requires_grad_(True), 6, 0.125, False).detach()
+    o_infer2 = cfa.fused_attention_qkv(x, 6, 0.125, False)
+    _abi.fwd_select(_abi.FWD_TC)
     status_ok()
-    assert torch.equal(o_infer, o_tc) and torch.equal(o_nograd, o_tc)
-    assert not torch.equal(o_train, o_tc)
+    assert torch.equal(o_infer, o_train) and torch.equal(o_nograd, o_train)
+    assert torch.equal(o_infer2, o_train) and not torch.equal(o_ffma, o_train)

@@ -40,7 +40,9 @@ def _setup(b, h, s, causal, seed, dev):
 
 
 def _reference_backward(b, h, s, causal, x, g, st, gst, ptrs, o, lse, stream, dev):
-    nbytes = _abi.bwd_workspace_bytes(b, h, s)
+    # A workspace of the static scratch's size: the same kernel choice (the dQ partials, and with
+    # them the tensor-core backward at s <= 1024, when they fit).
+    nbytes = max(_abi.bwd_workspace_bytes(b, h, s), _abi.NOALLOC_SCRATCH_BYTES)
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     dqkv = torch.empty(b, s, 3, h, 64, device=dev)
     rc = _abi.bwd(ptrs[0], st, ptrs[1], st, ptrs[2], st, o.data_ptr(), lse.data_ptr(),
