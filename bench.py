@@ -17,9 +17,11 @@ One JSON line on rank 0:
              copied in and O, dqkv copied out inside the timed region, batch chunks overlapping
              both copy directions with the kernels); the plain fused_attention_qkv + autograd
              path with unoverlapped copies is reported beside it;
-  roofline   the backward kernel (the dominant one): achieved = 10 b h s^2 d / its event-timed
-             duration, against the FFMA peak (148 SMs x 128 FMA/clk x 2 x the measured max SM
-             clock of MEASURED_PEAKS.json);
+  roofline   the backward kernel (the dominant one; at head dim 64 and s <= 1024 the tensor-core
+             kernel): achieved = 10 b h s^2 d / its event-timed duration, against the split
+             scheme's fp32 ceiling -- the measured bf16 tensor peak of MEASURED_PEAKS.json over
+             the 6 bf16 products each fp32 product takes; the FFMA peak (148 SMs x 128 FMA/clk
+             x 2 x the measured max SM clock) beside it;
   ref_kernel the reference's own kernels (kernels/fused_attn.cu built for sm_100a) on the same
              inputs, same GPU, alternating rounds with ours;
   cpu_baseline  the CPU oracle (a port of the reference's composed path) on every host core.
@@ -360,9 +362,9 @@ def main():
     ap.add_argument("--only", default="", help="suite: run the configs whose name contains this")
     ap.add_argument("--head-dim", type=int, default=D,
                     help="kernels mode: the canvas-shaped projection as heads of this dim (32, 128)")
-    ap.add_argument("--forward", choices=["ffma", "tc"], default="ffma",
-                    help="kernels mode: the head-dim-64 forward of the fwd+bwd step (tc: the "
-                         "tensor-core kernel that forward-only calls take)")
+    ap.add_argument("--pair", choices=["tc", "ffma"], default="tc",
+                    help="kernels mode: the head-dim-64 kernel pair of the fwd+bwd step (tc: the "
+                         "tensor-core pair, the default; ffma: the CUDA-core pair)")
     ap.add_argument("--mode", choices=["full", "kernels", "suite"], default="full",
                     help="kernels: warm-up + `steps` plain steps, no timing (for ncu); "
                          "suite: every BASELINE config, ours vs the reference kernel")
@@ -427,7 +429,7 @@ def main():
 
     if args.mode == "kernels":  # a fixed, short launch sequence for ncu
         from candle_fused_attn import _abi
-        _abi.fwd_select(_abi.FWD_TC if args.forward == "tc" else _abi.FWD_FFMA)
+        _abi.fwd_select(_abi.FWD_TC if args.pair == "tc" else _abi.FWD_FFMA)
         for i in range(args.steps):
             step(i)
         torch.cuda.synchronize()
@@ -604,14 +606,19 @@ def main():
                 "autograd_ms_per_step": autograd_ms,
                 "autograd_path": "fused_attention_qkv + autograd backward, whole batch, copies "
                                  "not overlapped"},
-        "roofline": {"bound": "compute", "pipe": "fp32 FFMA (CUDA cores)",
-                     "kernel": "backward (prep + main, one cfa_bwd_f32_d64 call)",
-                     "achieved": achieved, "peak": pk["ffma_tflops"], "unit": "TFLOP/s",
-                     "frac": achieved / pk["ffma_tflops"], "traffic": traffic,
+        "roofline": {"bound": "tensor",
+                     "pipe": "tcgen05 bf16 (fp32 operands as 3 bf16 parts, 6 products per fp32 "
+                             "product, hi/lo TMEM accumulators promoted into fp32 registers)",
+                     "kernel": "backward (prep + main, one cfa_bwd_f32_d64 call: bwd_tc_kernel)",
+                     "achieved": achieved, "peak": pk["bf16_tflops"] / 6, "unit": "TFLOP/s",
+                     "frac": achieved / (pk["bf16_tflops"] / 6), "traffic": traffic,
                      "traffic_unit": "bytes per backward call (ncu, profiles/roofline_traffic.json)",
-                     "peak_source": pk["source"],
+                     "peak_source": f"MEASURED_PEAKS.json bf16_tflops {pk['bf16_tflops']} / 6 "
+                                    "split products",
+                     "ffma_peak": pk["ffma_tflops"], "ffma_frac": achieved / pk["ffma_tflops"],
+                     "ffma_peak_source": pk["source"],
                      "fwd_frac": flops(b, H, S, D, CAUSAL, "fwd") / (fwd_ms * 1e-3) / 1e12
-                     / pk["ffma_tflops"]},
+                     / (pk["bf16_tflops"] / 6)},
         "gpu_launches": 3 * args.steps,
         "clocks": clk.summary(),
         "ref_kernel": ref,
