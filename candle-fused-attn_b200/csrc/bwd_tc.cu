@@ -4,21 +4,22 @@
 // forward's L and the prep kernel's D, written into ONE [b, s, 3, h, 64] buffer -- the same
 // contract as bwd_ffma.cu (the reference's fattn_bwd_f32_d64, kernels/fused_attn.cu:213-426), with
 // the five products on tcgen05.mma and fp32 from split bf16 parts as in fwd_tc.cu: every fp32
-// operand x = x0 + x1 + x2 (three bf16), A B = A0B0 + (A0B1 + A1B0 + A0B2 + A1B1 + A2B0), the
-// high-order product and the five small ones in separate TMEM accumulators that start fresh every
-// window of at most 128 reduction elements and are added in fp32 registers, round-to-nearest.
+// operand x = x0 + x1 + x2 (three bf16), A B = A0B0 + (A0B1 + A1B0 + A0B2 + A1B1 + A2B0), every
+// product in one TMEM accumulator that starts fresh every window of 64 reduction elements and
+// takes the small products of the window's K-steps first and its A0B0 steps last; each window's
+// sum is added in fp32 registers, round-to-nearest.
 //
 // Block: 512 threads own a key block of KB = 128 keys of one (batch, head) and walk its query
 // tiles of QT = 64. Thread (warp w, lane l) owns key row 32 (w % 4) + l -- its TMEM lane -- and
 // the 16 columns of group w / 4. Per query tile, with thread 0 issuing every MMA:
-//   S^T  = K Q^T      A: K parts (K-major)      B: Q parts (K-major)        -> TMEM 0 / 64
-//   dP^T = V dO^T     A: V parts                B: dO parts                 -> TMEM 128 / 192
+//   S^T  = K Q^T      A: K parts (K-major)      B: Q parts (K-major)        -> TMEM 0
+//   dP^T = V dO^T     A: V parts                B: dO parts                 -> TMEM 64
 //   the threads form P^T = exp(S^T * scale - L) (masked) and dS^T = P^T o (dP^T - D), put P^T's
-//   parts into TMEM (the A operand of dV, over S^T's columns) and dS^T's into shared memory;
-//   dV  += P^T dO     A: P^T parts in TMEM      B: dO parts read MN-major   -> TMEM 256 / 320
-//   dK  += dS^T Q     A: dS^T parts (K-major)   B: Q parts read MN-major    -> TMEM 384 / 448
+//   parts into TMEM (the A operand of dV, over columns 0-95) and dS^T's into shared memory;
+//   dV  += P^T dO     A: P^T parts in TMEM      B: dO parts read MN-major   -> TMEM 128
+//   dK  += dS^T Q     A: dS^T parts (K-major)   B: Q parts read MN-major    -> TMEM 192
 //   dQ_t = dS K       A: dS^T parts read MN-major (M = 64 queries)  B: K parts read MN-major
-//                                                                           -> TMEM 128 / 192
+//                     keys 0-63 -> TMEM 256, keys 64-127 -> TMEM 320 (two windows)
 //   dV and dK fold into fp32 registers per tile; the tile's dQ partial goes to the workspace and
 //   the block that finishes last for its (batch, head) sums the partials in key-block order
 //   (the no-wait path of bwd_ffma.cu: bit-identical for every schedule).
@@ -149,24 +150,28 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Six split products over STEPS K-steps: descriptors advance by A_STEP / B_STEP bytes per step and
-// by A_PART / B_PART bytes per part; part pairs (PA[p], PB[p]) -- (0, 0) into `big`, then (0, 1),
-// (1, 0), (0, 2), (1, 1), (2, 0) into `small` -- or, SWAP, the pairs (PB[p], PA[p]): the order in
-// which the forward forms its products when A and B trade places.
+// One window: six split products over STEPS K-steps into the fresh accumulator `d`; descriptors
+// advance by A_STEP / B_STEP bytes per step and by A_PART / B_PART bytes per part. Part pairs
+// (P0(p), P1(p)) -- the small (0, 1), (1, 0), (0, 2), (1, 1), (2, 0) of every step, then the
+// (0, 0) of every step -- or, SWAP, (P1(p), P0(p)): the order in which the forward forms its
+// products when A and B trade places.
+__host__ __device__ constexpr int P0(int p) { return p == 2 || p == 4 ? 1 : (p == 5 ? 2 : 0); }
+__host__ __device__ constexpr int P1(int p) { return p == 1 || p == 4 ? 1 : (p == 3 ? 2 : 0); }
 template <int STEPS, int A_PART, int B_PART, int A_STEP, int B_STEP, bool SWAP>
-__device__ __forceinline__ void issue6(uint32_t big, uint32_t small, uint64_t ad0, uint64_t bd0,
-                                       uint32_t idesc) {
-  constexpr int P0[6] = {0, 0, 1, 0, 1, 2};
-  constexpr int P1[6] = {0, 1, 0, 2, 1, 0};
+__device__ __forceinline__ void issue6(uint32_t d, uint64_t ad0, uint64_t bd0, uint32_t idesc) {
 #pragma unroll
   for (int ks = 0; ks < STEPS; ++ks)
 #pragma unroll
-    for (int p = 0; p < 6; ++p) {
-      const int pa = SWAP ? P1[p] : P0[p], pb = SWAP ? P0[p] : P1[p];
-      const uint64_t ad = ad0 + static_cast<uint64_t>((pa * A_PART + A_STEP * ks) >> 4);
-      const uint64_t bd = bd0 + static_cast<uint64_t>((pb * B_PART + B_STEP * ks) >> 4);
-      tc::mma_bf16(p == 0 ? big : small, ad, bd, idesc, p == 0 ? (ks > 0) : (ks > 0 || p > 1));
+    for (int p = 1; p < 6; ++p) {
+      const int pa = SWAP ? P1(p) : P0(p), pb = SWAP ? P0(p) : P1(p);
+      tc::mma_bf16(d, ad0 + static_cast<uint64_t>((pa * A_PART + A_STEP * ks) >> 4),
+                   bd0 + static_cast<uint64_t>((pb * B_PART + B_STEP * ks) >> 4), idesc,
+                   ks > 0 || p > 1);
     }
+#pragma unroll
+  for (int ks = 0; ks < STEPS; ++ks)
+    tc::mma_bf16(d, ad0 + static_cast<uint64_t>((A_STEP * ks) >> 4),
+                 bd0 + static_cast<uint64_t>((B_STEP * ks) >> 4), idesc, 1);
 }
 
 template <bool CAUSAL>
@@ -264,8 +269,6 @@ __global__ void __launch_bounds__(NT, 1) bwd_tc_kernel(const BwdArgs a) {
   const uint32_t id_dq = tc::idesc_f32acc(1, QT, 64) | (1u << 15) | (1u << 16);  // M 64, A, B MN
   const uint32_t sK = tc::smem_u32(Kp), sV = tc::smem_u32(Vp), sQ = tc::smem_u32(Qp),
                  sO = tc::smem_u32(dOp), sS = tc::smem_u32(dSp);
-  constexpr int PA[6] = {0, 0, 1, 0, 1, 2};  // part pairs (the dV products: P^T i, dO j)
-  constexpr int PB[6] = {0, 1, 0, 2, 1, 0};
 
   float dv[16], dk[16];
 #pragma unroll
@@ -279,10 +282,9 @@ __global__ void __launch_bounds__(NT, 1) bwd_tc_kernel(const BwdArgs a) {
     // (1) S^T and dP^T.
     if (tid == 0) {
       // S^T in the forward's product order (its pairs (Q i, K j) as (K j, Q i)).
-      issue6<4, PART_K, PART_Q, 256, 256, true>(tbase, tbase + 64, tc::desc_kmajor(sK, 128, 1024),
+      issue6<4, PART_K, PART_Q, 256, 256, true>(tbase, tc::desc_kmajor(sK, 128, 1024),
                                                 tc::desc_kmajor(sQ, 128, 1024), id128);
-      issue6<4, PART_K, PART_Q, 256, 256, false>(tbase + 128, tbase + 192,
-                                                 tc::desc_kmajor(sV, 128, 1024),
+      issue6<4, PART_K, PART_Q, 256, 256, false>(tbase + 64, tc::desc_kmajor(sV, 128, 1024),
                                                  tc::desc_kmajor(sO, 128, 1024), id128);
       tc::commit(bar_a);
     }
@@ -299,25 +301,23 @@ __global__ void __launch_bounds__(NT, 1) bwd_tc_kernel(const BwdArgs a) {
 #pragma unroll
     for (int h8 = 0; h8 < 2; ++h8) {
       const uint32_t col = 16 * cg + 8 * h8;
-      float sb[8], ss[8], gb[8], gs[8];
+      float sb[8], gb[8];
       tmem_ld8(tbase + lane_sel + col, sb);
-      tmem_ld8(tbase + lane_sel + 64 + col, ss);
-      tmem_ld8(tbase + lane_sel + 128 + col, gb);
-      tmem_ld8(tbase + lane_sel + 192 + col, gs);
+      tmem_ld8(tbase + lane_sel + 64 + col, gb);
       tc::tmem_wait_ld();
       float ds[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const int ql = col + u, qi = q0 + ql;
         // P = e^(s * scale - L), one rounding of the argument (as bwd_ffma.cu).
-        float p = expf(fmaf(sb[u] + ss[u], a.scale, -Lt[ql]));
+        float p = expf(fmaf(sb[u], a.scale, -Lt[ql]));
         if (edge && !(qi < S && key < S && !(CAUSAL && key > qi))) p = 0.0f;
         pr[8 * h8 + u] = p;
-        ds[u] = p * ((gb[u] + gs[u]) - Dt[ql]);
+        ds[u] = p * (gb[u] - Dt[ql]);
       }
       store_parts(dSp, PART_K, kmaj_off(row, 2 * cg + h8), ds);
     }
-    // (4) P^T's parts over S^T's columns, once every thread has read S^T and dP^T.
+    // (4) P^T's parts over columns 0-95, once every thread has read S^T and dP^T.
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -350,16 +350,23 @@ __global__ void __launch_bounds__(NT, 1) bwd_tc_kernel(const BwdArgs a) {
       const uint64_t bk_mn = tc::desc_kmajor(sK, 1024, 128);  // K as B, MN-major (K = keys)
       const uint64_t as_k = tc::desc_kmajor(sS, 128, 1024);   // dS^T as A, K-major
       const uint64_t as_mn = tc::desc_kmajor(sS, 1024, 128);  // dS^T as A, MN-major (M = q)
+      // dV: P^T part i of K-step ks at TMEM column 32 i + 8 ks; the same pair order as issue6.
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
 #pragma unroll
-        for (int p = 0; p < 6; ++p) {
-          const uint64_t bd = bo_mn + static_cast<uint64_t>((PB[p] * PART_Q + 2048 * ks) >> 4);
-          mma_bf16_tmem_a(p == 0 ? tbase + 256 : tbase + 320, tbase + 32 * PA[p] + 8 * ks, bd,
-                          id_dv, p == 0 ? (ks > 0) : (ks > 0 || p > 1));
-        }
-      issue6<4, PART_K, PART_Q, 256, 2048, false>(tbase + 384, tbase + 448, as_k, bq_mn, id_dv);
-      issue6<8, PART_K, PART_K, 2048, 2048, false>(tbase + 128, tbase + 192, as_mn, bk_mn, id_dq);
+        for (int p = 1; p < 6; ++p)
+          mma_bf16_tmem_a(tbase + 128, tbase + 32 * P0(p) + 8 * ks,
+                          bo_mn + static_cast<uint64_t>((P1(p) * PART_Q + 2048 * ks) >> 4), id_dv,
+                          ks > 0 || p > 1);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_bf16_tmem_a(tbase + 128, tbase + 8 * ks,
+                        bo_mn + static_cast<uint64_t>((2048 * ks) >> 4), id_dv, 1);
+      issue6<4, PART_K, PART_Q, 256, 2048, false>(tbase + 192, as_k, bq_mn, id_dv);
+      // dQ: keys 0-63 and 64-127 (four K-steps each, 8192 bytes apart in both operands).
+      issue6<4, PART_K, PART_K, 2048, 2048, false>(tbase + 256, as_mn, bk_mn, id_dq);
+      issue6<4, PART_K, PART_K, 2048, 2048, false>(tbase + 320, as_mn + (8192 >> 4),
+                                                   bk_mn + (8192 >> 4), id_dq);
       tc::commit(bar_b);
     }
     // (6) Fold dV, dK; write the dQ partial; the next tile's Q, dO into their parts.
@@ -368,19 +375,17 @@ __global__ void __launch_bounds__(NT, 1) bwd_tc_kernel(const BwdArgs a) {
     tc::fence_after_sync();
     {
       float xb[16], xs[16];
-      tc::tmem_ld16(tbase + lane_sel + 256 + 16 * cg, xb);
-      tc::tmem_ld16(tbase + lane_sel + 320 + 16 * cg, xs);
-      tc::tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < 16; ++c) dv[c] += xb[c] + xs[c];
-      tc::tmem_ld16(tbase + lane_sel + 384 + 16 * cg, xb);
-      tc::tmem_ld16(tbase + lane_sel + 448 + 16 * cg, xs);
-      tc::tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < 16; ++c) dk[c] += xb[c] + xs[c];
-      // dQ (M = 64): query row 16 (w % 4) + lane in lanes 0-15 of each quarter.
       tc::tmem_ld16(tbase + lane_sel + 128 + 16 * cg, xb);
       tc::tmem_ld16(tbase + lane_sel + 192 + 16 * cg, xs);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        dv[c] += xb[c];
+        dk[c] += xs[c];
+      }
+      // dQ (M = 64): query row 16 (w % 4) + lane in lanes 0-15 of each quarter; the two windows.
+      tc::tmem_ld16(tbase + lane_sel + 256 + 16 * cg, xb);
+      tc::tmem_ld16(tbase + lane_sel + 320 + 16 * cg, xs);
       tc::tmem_wait_ld();
       const int qi = q0 + 16 * (w & 3) + lane;
       if (lane < 16 && qi < S && !err) {

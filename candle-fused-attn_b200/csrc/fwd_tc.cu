@@ -8,11 +8,14 @@
 // (each part the round-to-nearest bf16 of what the previous ones leave; the two subtractions are
 // exact), and A B is formed from the six products A0B0 + (A0B1 + A1B0 + A0B2 + A1B1 + A2B0): the
 // dropped terms are below 2^-24 relative. The tensor core accumulates in fp32 by truncation, so
-// A0B0 and the five small products go to two separate TMEM accumulators, each fresh for every
-// window of 64 reduction elements (S: all of d; O: one key tile), and the two are added in
-// registers with round-to-nearest: S = big + small; O = O * alpha + (big + small) per key tile.
-// Modelled against fp64 at the canvas shape (baseline/split_precision_model.py) this lands below
-// plain sequential-FFMA fp32 on every output of the forward and backward.
+// each product goes to a TMEM accumulator that starts fresh for every window of 64 reduction
+// elements (S: all of d; O: one key tile) and takes the five small products of every K-step
+// first, the high-order A0B0 steps last: the small sums truncate at their own magnitude (2^-8 of
+// the result and below) and only the four A0B0 steps truncate at the result's. Each window's sum
+// is added in fp32 registers with round-to-nearest: O = O * alpha + PV per key tile. Modelled
+// against fp64 at the canvas shape (baseline/split_precision_model.py) this lands below plain
+// sequential-FFMA fp32 on every output of the forward and backward, level with separate
+// accumulators for A0B0 and the small products at half the TMEM.
 //
 // Block: 16 softmax warps and one MMA warp own TC_BM = 128 queries of one (batch, head). Softmax
 // thread (warp w < 16, lane l) owns query row 32 (w % 4) + l -- its TMEM lane -- and the 16
@@ -27,8 +30,7 @@
 // Every mbarrier wait is bounded (WAIT_TIMEOUT_NS); on expiry the block sets the device error flag
 // (cfa_fwd_status reads it), waits once more, frees its TMEM and returns without writing.
 //
-// DETERMINISM: the MMA order is fixed by the code; every register sum has one order: S = big +
-// small; the row max over each group's 16 keys in order, then the groups 0..3; p summed over the
+// DETERMINISM: the MMA order is fixed by the code; every register sum has one order: the row max over each group's 16 keys in order, then the groups 0..3; p summed over the
 // group's keys in order, per tile; l = ((l0 + l1) + l2) + l3; O over key tiles in index order.
 #include <cuda_bf16.h>
 
@@ -60,9 +62,8 @@ constexpr int OFF_RED = OFF_VST + TILE_F32;    // float [128][NQ]: the row max p
 constexpr int OFF_BAR = OFF_RED + TC_BM * NQ * 4;  // mbarriers S0, S1, O and the TMEM base
 constexpr int TC_SMEM = OFF_BAR + 32;
 constexpr int TC_SMEM_ALLOC = TC_SMEM + 1024;  // room to align the base to 1024 bytes
-// TMEM columns: S big / small for two key tiles (0-63 / 64-127, 128-191 / 192-255), O big / small
-// (256-319 / 320-383); one block per SM, so it may take all 512.
-constexpr uint32_t TMEM_COLS = 512;
+// TMEM columns: S of two key tiles (0-63, 64-127), O (128-191); one block per SM.
+constexpr uint32_t TMEM_COLS = 256;
 
 // Byte offset of the 16-byte core-matrix row holding elements (row, 8 kc .. 8 kc + 7) of a
 // K-major bf16 operand with 64 elements per row: core matrices of 8 rows x 16 bytes, K-adjacent
@@ -163,26 +164,28 @@ __device__ __forceinline__ void split_vt_item(unsigned char* parts, const unsign
   store_parts(parts, PART_K, kmaj_off(d, g), x);
 }
 
-// The six (A part, B part) products: A0B0 into the big accumulator, the rest into the small one.
-// A descriptor's start-address field holds the byte address / 16 (shared memory < 256 KB: no
+// The six (A part, B part) products of K = 64 (four K-steps of 16 bf16) into one accumulator `d`:
+// the small pairs (0, 1), (1, 0), (0, 2), (1, 1), (2, 0) of every step, then the (0, 0) of every
+// step. A descriptor's start-address field holds the byte address / 16 (shared memory < 256 KB: no
 // carry out of its 14 bits), so the descriptor of base + off is the base's plus off / 16.
 template <int A_PART, int B_PART>
-__device__ __forceinline__ void issue_split_mma(uint32_t d_big, uint32_t d_small, uint32_t a_base,
-                                                uint32_t b_base, uint32_t idesc) {
+__device__ __forceinline__ void issue_split_mma(uint32_t d, uint32_t a_base, uint32_t b_base,
+                                                uint32_t idesc) {
   constexpr int PA[6] = {0, 0, 1, 0, 1, 2};
   constexpr int PB[6] = {0, 1, 0, 2, 1, 0};
   const uint64_t ad0 = tc::desc_kmajor(a_base, 128, 1024);
   const uint64_t bd0 = tc::desc_kmajor(b_base, 128, 1024);
 #pragma unroll
-  for (int ks = 0; ks < 4; ++ks) {  // K = 64 in steps of 16 bf16 (two core matrices)
+  for (int ks = 0; ks < 4; ++ks)
 #pragma unroll
-    for (int p = 0; p < 6; ++p) {
-      const uint64_t ad = ad0 + static_cast<uint64_t>((PA[p] * A_PART + 256 * ks) >> 4);
-      const uint64_t bd = bd0 + static_cast<uint64_t>((PB[p] * B_PART + 256 * ks) >> 4);
-      const uint32_t acc = p == 0 ? (ks > 0) : (ks > 0 || p > 1);
-      tc::mma_bf16(p == 0 ? d_big : d_small, ad, bd, idesc, acc);
-    }
-  }
+    for (int p = 1; p < 6; ++p)
+      tc::mma_bf16(d, ad0 + static_cast<uint64_t>((PA[p] * A_PART + 256 * ks) >> 4),
+                   bd0 + static_cast<uint64_t>((PB[p] * B_PART + 256 * ks) >> 4), idesc,
+                   ks > 0 || p > 1);
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks)
+    tc::mma_bf16(d, ad0 + static_cast<uint64_t>((256 * ks) >> 4),
+                 bd0 + static_cast<uint64_t>((256 * ks) >> 4), idesc, 1);
 }
 
 // Named barriers: 1 = the softmax threads (TC_THREADS), 2 = those plus the MMA warp (TC_BLOCK).
@@ -192,12 +195,10 @@ __device__ __forceinline__ void bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-// CW = 16 consecutive fp32 columns of this thread's TMEM lane at `big` and at `small`, one wait.
-__device__ __forceinline__ void tmem_ld2(uint32_t big, uint32_t small, float (&u)[CW],
-                                         float (&v)[CW]) {
+// CW = 16 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld1(uint32_t taddr, float (&u)[CW]) {
   static_assert(CW == 16, "one 16-column load per accumulator");
-  tc::tmem_ld16(big, u);
-  tc::tmem_ld16(small, v);
+  tc::tmem_ld16(taddr, u);
   tc::tmem_wait_ld();
 }
 
@@ -281,7 +282,7 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
   tc::fence_after_sync();
   const uint32_t tbase = *tbase_p;
   const uint32_t lane_sel = static_cast<uint32_t>(32 * (w & 3)) << 16;
-  const uint32_t t_obig = tbase + 256, t_osmall = tbase + 320;
+  const uint32_t t_o = tbase + 128;
   bool err = false;
 
   if (mma_warp) {
@@ -290,10 +291,10 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
     const uint32_t sQ = tc::smem_u32(Qp), sV = tc::smem_u32(Vp), sP = tc::smem_u32(Pp);
     const uint32_t sK0 = tc::smem_u32(sm + OFF_K);
     if (lane == 0) {
-      issue_split_mma<PART_Q, PART_K>(tbase, tbase + 64, sQ, sK0, idesc);
+      issue_split_mma<PART_Q, PART_K>(tbase, sQ, sK0, idesc);
       tc::commit(bar_s);
       if (T > 1) {
-        issue_split_mma<PART_Q, PART_K>(tbase + 128, tbase + 192, sQ, sK0 + 3 * PART_K, idesc);
+        issue_split_mma<PART_Q, PART_K>(tbase + 64, sQ, sK0 + 3 * PART_K, idesc);
         tc::commit(bar_s + 1);
       }
     }
@@ -302,11 +303,10 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
       tc::fence_after_sync();
       if (lane == 0) {
         const int j = n & 1;
-        issue_split_mma<PART_Q, PART_K>(t_obig, t_osmall, sP, sV, idesc);
+        issue_split_mma<PART_Q, PART_K>(t_o, sP, sV, idesc);
         tc::commit(bar_o);
         if (n + 2 < T) {
-          issue_split_mma<PART_Q, PART_K>(tbase + 128 * j, tbase + 128 * j + 64, sQ,
-                                          sK0 + 3 * PART_K * j, idesc);
+          issue_split_mma<PART_Q, PART_K>(tbase + 64 * j, sQ, sK0 + 3 * PART_K * j, idesc);
           tc::commit(bar_s + j);
         }
       }
@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
 #pragma unroll
   for (int c = 0; c < CW; ++c) acc[c] = 0.0f;
   const int qi = q0 + row;
-  float sv[CW], sw[CW];
+  float sv[CW];
 
   // Every softmax thread waits for every commit itself; an expired wait is remembered (the outputs
   // are then invalid) and the block runs on, so all threads keep to the same barriers.
@@ -329,13 +329,12 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
     // (a) S(n) from TMEM; the online softmax.
     err |= !tc::mbar_wait(bar_s + j, (n >> 1) & 1, WAIT_TIMEOUT_NS);
     tc::fence_after_sync();
-    tmem_ld2(tbase + 128 * j + lane_sel + CW * cq, tbase + 128 * j + 64 + lane_sel + CW * cq, sv,
-             sw);
+    tmem_ld1(tbase + 64 * j + lane_sel + CW * cq, sv);
     const bool edge = (k0 + TC_BN > S) || (CAUSAL && k0 + TC_BN - 1 > q0);
     float tmax = -INFINITY;
 #pragma unroll
     for (int c = 0; c < CW; ++c) {
-      float x = (sv[c] + sw[c]) * a.scale;
+      float x = sv[c] * a.scale;
       if (edge) {
         const int jj = k0 + CW * cq + c;
         if (!(jj < S && !(CAUSAL && jj > qi))) x = -INFINITY;
@@ -364,10 +363,10 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
     if (n > 0) {
       err |= !tc::mbar_wait(bar_o, (n - 1) & 1, WAIT_TIMEOUT_NS);
       tc::fence_after_sync();
-      float ob[CW], os[CW];
-      tmem_ld2(t_obig + lane_sel + CW * cq, t_osmall + lane_sel + CW * cq, ob, os);
+      float ob[CW];
+      tmem_ld1(t_o + lane_sel + CW * cq, ob);
 #pragma unroll
-      for (int c = 0; c < CW; ++c) acc[c] = fmaf(acc[c], alpha_prev, ob[c] + os[c]);
+      for (int c = 0; c < CW; ++c) acc[c] = fmaf(acc[c], alpha_prev, ob[c]);
     }
     split_vt_item(Vp, Vst);
     if (n + 2 < T) split_row_item(sm + OFF_K + 3 * PART_K * j, PART_K, Kst, 0, tid);
@@ -393,9 +392,9 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
     // The last tile's P V.
     err |= !tc::mbar_wait(bar_o, (T - 1) & 1, WAIT_TIMEOUT_NS);
     tc::fence_after_sync();
-    tmem_ld2(t_obig + lane_sel + CW * cq, t_osmall + lane_sel + CW * cq, sv, sw);
+    tmem_ld1(t_o + lane_sel + CW * cq, sv);
 #pragma unroll
-    for (int c = 0; c < CW; ++c) acc[c] = fmaf(acc[c], alpha_prev, sv[c] + sw[c]);
+    for (int c = 0; c < CW; ++c) acc[c] = fmaf(acc[c], alpha_prev, sv[c]);
     cp_async_wait_all();
     red[NQ * row + cq] = lpart;
   }

@@ -143,3 +143,30 @@ def test_kernel_selection(cuda):
     status_ok()
     assert torch.equal(o_infer, o_train) and torch.equal(o_nograd, o_train)
     assert torch.equal(o_infer2, o_train) and not torch.equal(o_ffma, o_train)
+
+
+def test_pair_accuracy_vs_ffma(cuda):
+    """Forward and backward of the tensor-core pair against the fp64 composed path at the canvas
+    shape (8 of its batches): O, dQ, dK, dV each at or below the FFMA pair's error (the north
+    star's condition for a split-precision tensor-core path)."""
+    b, h, s = 8, 6, 240
+    qkv, dout = oracle.seeded_inputs(b, h, s, 0, 0.5)
+    o64, _, g64 = oracle.qkv_forward_backward(qkv, dout, h, 0.125, False, dtype=torch.float64)
+    g64 = g64.reshape(b, s, 3, h * 64)
+
+    def errors(impl):
+        prev = _abi.fwd_select(impl)
+        x = qkv.to(cuda).requires_grad_(True)
+        out = cfa.fused_attention_qkv(x, h, 0.125, False)
+        out.backward(dout.to(cuda))
+        _abi.fwd_select(prev)
+        g = x.grad.cpu().double().reshape(b, s, 3, h * 64)
+        return {"O": oracle.normwise(out.detach().cpu().double(), o64),
+                **{n: oracle.normwise(g[:, :, i], g64[:, :, i]) for i, n in enumerate(("dQ", "dK", "dV"))}}
+
+    e_tc, e_ff = errors(_abi.FWD_TC), errors(_abi.FWD_FFMA)
+    status_ok()
+    print("tensor cores vs fp64:", {k: f"{v:.3e}" for k, v in e_tc.items()})
+    print("FFMA         vs fp64:", {k: f"{v:.3e}" for k, v in e_ff.items()})
+    for k in e_tc:
+        assert e_tc[k] <= e_ff[k], (k, e_tc[k], e_ff[k])
