@@ -9,20 +9,27 @@
 // takes the small products of the window's K-steps first and its A0B0 steps last; each window's
 // sum is added in fp32 registers, round-to-nearest.
 //
-// Block: 512 threads own a key block of KB = 128 keys of one (batch, head) and walk its query
-// tiles of QT = 64. Thread (warp w, lane l) owns key row 32 (w % 4) + l -- its TMEM lane -- and
-// the 16 columns of group w / 4. Per query tile, with thread 0 issuing every MMA:
-//   S^T  = K Q^T      A: K parts (K-major)      B: Q parts (K-major)        -> TMEM 0
-//   dP^T = V dO^T     A: V parts                B: dO parts                 -> TMEM 64
-//   the threads form P^T = exp(S^T * scale - L) (masked) and dS^T = P^T o (dP^T - D), put P^T's
-//   parts into TMEM (the A operand of dV, over columns 0-95) and dS^T's into shared memory;
-//   dV  += P^T dO     A: P^T parts in TMEM      B: dO parts read MN-major   -> TMEM 128
-//   dK  += dS^T Q     A: dS^T parts (K-major)   B: Q parts read MN-major    -> TMEM 192
-//   dQ_t = dS K       A: dS^T parts read MN-major (M = 64 queries)  B: K parts read MN-major
-//                     keys 0-63 -> TMEM 256, keys 64-127 -> TMEM 320 (two windows)
-//   dV and dK fold into fp32 registers per tile; the tile's dQ partial goes to the workspace and
-//   the block that finishes last for its (batch, head) sums the partials in key-block order
-//   (the no-wait path of bwd_ffma.cu: bit-identical for every schedule).
+// Block: 16 compute warps and one MMA warp own a key block of KB = 128 keys of one (batch, head)
+// and walk its query tiles of QT = 64. Compute thread (warp w < 16, lane l) owns key row
+// 32 (w % 4) + l -- its TMEM lane -- and the 16 columns of group w / 4; warp 16 issues every MMA.
+// Per query tile n:
+//   T1:  S^T  = K Q^T      A: K parts (shared, K-major)   B: Q parts (K-major)        -> TMEM S
+//        dP^T = V dO^T     A: V parts (TMEM, loaded once)  B: dO parts                -> TMEM DP
+//   C1:  the threads form P^T = exp(S^T * scale - L) (masked) and dS^T = P^T o (dP^T - D), put
+//        P^T's parts into TMEM over the columns each has just read (the A operand of dV) and
+//        dS^T's into shared memory;
+//   T2:  dV  += P^T dO     A: P^T parts (TMEM)             B: dO parts read MN-major  -> TMEM DV
+//        dK  += dS^T Q     A: dS^T parts (K-major)         B: Q parts read MN-major   -> TMEM DK
+//        dQ_t = dS K       A: dS^T parts read MN-major (M = 64 queries)  B: K parts read MN-major,
+//                          keys 0-63 and 64-127 in two windows                    -> TMEM DQ0, DQ1
+//   C3:  (during T2) the next tile's Q, dO into their parts -- two buffers, by tile parity;
+//   C2:  (during T1 of the next tile) dV, dK fold into fp32 registers; the tile's dQ partial goes
+//        to the workspace.
+// The hand-offs are mbarriers: T1 and T2 commit; the compute warps arrive (one per warp) when
+// C1's operands and the next tile's Q, dO parts are in place. The MMA warp issues T1(n + 1) once
+// T2(n) has completed (it reads P^T(n) from the columns T1(n + 1) writes). The block that finishes
+// last for its (batch, head) sums the dQ partials in key-block order (the no-wait path of
+// bwd_ffma.cu: bit-identical for every schedule).
 // S^T takes its six products in the forward kernel's order (A and B swapped), so the scores match
 // fwd_tc.cu's and the recomputed P matches the forward's L.
 //
@@ -39,21 +46,32 @@ namespace {
 
 constexpr int KB = 128;   // keys per block: MMA M of S^T, dP^T, dV, dK
 constexpr int QT = 64;    // queries per tile: MMA N of S^T, dP^T; M of dQ
-constexpr int NT = 512;   // threads
+constexpr int NT = 512;   // compute threads (16 warps)
+constexpr int NB = NT + 32;  // and the MMA warp
 constexpr int PART_K = KB * 64 * 2;  // one bf16 part of a [128][64] operand
 constexpr int PART_Q = QT * 64 * 2;  // one bf16 part of a [64][64] operand
 constexpr int OFF_K = 0;                      // K parts [128 keys][64 d]
-constexpr int OFF_V = OFF_K + 3 * PART_K;     // V parts [128 keys][64 d]
-constexpr int OFF_Q = OFF_V + 3 * PART_K;     // Q parts [64 q][64 d]
-constexpr int OFF_DO = OFF_Q + 3 * PART_Q;    // dO parts [64 q][64 d]
-constexpr int OFF_DS = OFF_DO + 3 * PART_Q;   // dS^T parts [128 keys][64 q] (first: K staged)
-constexpr int OFF_ST = OFF_DS + 3 * PART_K;   // staging: next Q, dO (fp32; first: V staged)
+constexpr int OFF_Q = OFF_K + 3 * PART_K;     // Q parts [64 q][64 d], two tiles
+constexpr int OFF_DO = OFF_Q + 6 * PART_Q;    // dO parts [64 q][64 d], two tiles
+constexpr int OFF_DS = OFF_DO + 6 * PART_Q;   // dS^T parts [128 keys][64 q] (first: K staged)
+constexpr int OFF_ST = OFF_DS + 3 * PART_K;   // staging: the next tile's Q, dO (fp32)
 constexpr int OFF_LD = OFF_ST + 2 * QT * 64 * 4;  // L, D of two tiles: float [2][2][64]
-constexpr int OFF_BAR = OFF_LD + 2 * 2 * QT * 4;  // mbarriers A (S, dP), B (dV, dK, dQ); TMEM base
-constexpr int SMEM = OFF_BAR + 32;
+constexpr int OFF_BAR = OFF_LD + 2 * 2 * QT * 4;  // four mbarriers, the TMEM base, two ints
+constexpr int SMEM = OFF_BAR + 64;
 constexpr int SMEM_ALLOC = SMEM + 1024;
-constexpr uint32_t TMEM_COLS = 512;
 static_assert(SMEM_ALLOC <= 232448, "shared memory per block");
+// TMEM columns (lane = key row). V's parts, the A operand of dP^T: part i, K-step ks (16 dims) in
+// the 8 columns T_V + 32 i + 8 ks. S^T, dP^T of the current tile; P^T's parts (the A operand of
+// dV) then over the columns each thread has read (pt_col); dV, dK; dQ's two 64-key windows (M = 64).
+constexpr uint32_t T_V = 0, T_S = 96, T_DP = 160, T_DV = 224, T_DK = 288, T_DQ0 = 352,
+                   T_DQ1 = 416;
+constexpr uint32_t TMEM_COLS = 512;
+
+// P^T part i of K-step ks (queries 16 ks .. 16 ks + 15: the columns of group ks): parts 0, 1 over
+// that group's S^T columns, part 2 over its first 8 dP^T columns.
+__host__ __device__ constexpr uint32_t pt_col(int i, int ks) {
+  return i < 2 ? T_S + 16 * ks + 8 * i : T_DP + 16 * ks;
+}
 
 __device__ __forceinline__ uint32_t kmaj_off(int row, int kc) {
   return static_cast<uint32_t>((((row >> 3) * 8 + kc) << 7) + ((row & 7) << 4));
@@ -82,6 +100,24 @@ __device__ __forceinline__ void split8(const float (&x)[8], uint4& p0, uint4& p1
   p0 = make_uint4(a[0], a[1], a[2], a[3]);
   p1 = make_uint4(b[0], b[1], b[2], b[3]);
   p2 = make_uint4(c[0], c[1], c[2], c[3]);
+}
+
+// x[0..15] -> the three parts as packed bf16 pairs (TMEM operand columns, even element low).
+__device__ __forceinline__ void split16(const float (&x)[16], uint32_t (&p)[3][8]) {
+  float lo[8], hi[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    lo[u] = x[u];
+    hi[u] = x[8 + u];
+  }
+  uint4 l[3], h[3];
+  split8(lo, l[0], l[1], l[2]);
+  split8(hi, h[0], h[1], h[2]);
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    p[i][0] = l[i].x, p[i][1] = l[i].y, p[i][2] = l[i].z, p[i][3] = l[i].w;
+    p[i][4] = h[i].x, p[i][5] = h[i].y, p[i][6] = h[i].z, p[i][7] = h[i].w;
+  }
 }
 
 __device__ __forceinline__ void store_parts(unsigned char* base, int part_bytes, uint32_t off,
@@ -122,16 +158,6 @@ __device__ __forceinline__ void split_row_item(unsigned char* parts, int part_by
   store_parts(parts, part_bytes, kmaj_off(r, kc), x);
 }
 
-// MMA with the A operand in TMEM (lane r = row r; a K step of 16 bf16 in 8 columns of packed
-// pairs, the even element in the low half).
-__device__ __forceinline__ void mma_bf16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
-                                                uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
-}
-
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
@@ -154,46 +180,68 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
 // advance by A_STEP / B_STEP bytes per step and by A_PART / B_PART bytes per part. Part pairs
 // (P0(p), P1(p)) -- the small (0, 1), (1, 0), (0, 2), (1, 1), (2, 0) of every step, then the
 // (0, 0) of every step -- or, SWAP, (P1(p), P0(p)): the order in which the forward forms its
-// products when A and B trade places.
+// products when A and B trade places. Called by the whole MMA warp (tc::mma_bf16_warp).
 __host__ __device__ constexpr int P0(int p) { return p == 2 || p == 4 ? 1 : (p == 5 ? 2 : 0); }
 __host__ __device__ constexpr int P1(int p) { return p == 1 || p == 4 ? 1 : (p == 3 ? 2 : 0); }
 template <int STEPS, int A_PART, int B_PART, int A_STEP, int B_STEP, bool SWAP>
-__device__ __forceinline__ void issue6(uint32_t d, uint64_t ad0, uint64_t bd0, uint32_t idesc) {
+__device__ __forceinline__ void issue6(uint32_t d, tc::Desc ad, tc::Desc bd, uint32_t idesc) {
+  const uint32_t alo = tc::opaque(ad.lo), blo = tc::opaque(bd.lo);
 #pragma unroll
   for (int ks = 0; ks < STEPS; ++ks)
 #pragma unroll
     for (int p = 1; p < 6; ++p) {
       const int pa = SWAP ? P1(p) : P0(p), pb = SWAP ? P0(p) : P1(p);
-      tc::mma_bf16(d, ad0 + static_cast<uint64_t>((pa * A_PART + A_STEP * ks) >> 4),
-                   bd0 + static_cast<uint64_t>((pb * B_PART + B_STEP * ks) >> 4), idesc,
-                   ks > 0 || p > 1);
+      tc::mma_bf16_warp(d, alo + ((pa * A_PART + A_STEP * ks) >> 4), ad.hi,
+                        blo + ((pb * B_PART + B_STEP * ks) >> 4), bd.hi, idesc, ks > 0 || p > 1);
     }
 #pragma unroll
   for (int ks = 0; ks < STEPS; ++ks)
-    tc::mma_bf16(d, ad0 + static_cast<uint64_t>((A_STEP * ks) >> 4),
-                 bd0 + static_cast<uint64_t>((B_STEP * ks) >> 4), idesc, 1);
+    tc::mma_bf16_warp(d, alo + ((A_STEP * ks) >> 4), ad.hi, blo + ((B_STEP * ks) >> 4), bd.hi,
+                      idesc, 1);
+}
+
+// The same window with the A operand in TMEM: part i of K-step ks at column acol(i, ks).
+template <int B_PART, int B_STEP, typename ACol>
+__device__ __forceinline__ void issue6_tmem_a(uint32_t d, ACol acol, tc::Desc bd, uint32_t idesc) {
+  const uint32_t blo = tc::opaque(bd.lo);
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+    for (int p = 1; p < 6; ++p)
+      tc::mma_bf16_tmem_a_warp(d, acol(P0(p), ks), blo + ((P1(p) * B_PART + B_STEP * ks) >> 4),
+                               bd.hi, idesc, ks > 0 || p > 1);
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks)
+    tc::mma_bf16_tmem_a_warp(d, acol(0, ks), blo + ((B_STEP * ks) >> 4), bd.hi, idesc, 1);
+}
+
+// Named barrier 1: the 16 compute warps (the MMA warp never takes part).
+__device__ __forceinline__ void bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 template <bool CAUSAL>
-__global__ void __launch_bounds__(NT, 1) bwd_tc_kernel(const BwdArgs a) {
+__global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = tc::smem_u32(smem_raw);
   unsigned char* sm = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
   unsigned char* Kp = sm + OFF_K;
-  unsigned char* Vp = sm + OFF_V;
   unsigned char* Qp = sm + OFF_Q;
   unsigned char* dOp = sm + OFF_DO;
   unsigned char* dSp = sm + OFF_DS;
   unsigned char* st = sm + OFF_ST;
   float* ld = reinterpret_cast<float*>(sm + OFF_LD);  // [buf][0: L, 1: D][64]
-  uint64_t* bar_a = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
-  uint64_t* bar_b = bar_a + 1;
-  uint32_t* tbase_p = reinterpret_cast<uint32_t*>(bar_a + 2);
-  int* s_int = reinterpret_cast<int*>(bar_a + 3);
+  uint64_t* bar_s = reinterpret_cast<uint64_t*>(sm + OFF_BAR);  // S^T, dP^T of a tile done
+  uint64_t* bar_t2 = bar_s + 1;  // dV, dK, dQ of a tile done
+  uint64_t* bar_c1 = bar_s + 2;  // P^T, dS^T of a tile in place (one arrival per compute warp)
+  uint64_t* bar_q = bar_s + 3;   // Q, dO parts of the next tile in place (same)
+  uint32_t* tbase_p = reinterpret_cast<uint32_t*>(bar_s + 4);
+  int* s_int = reinterpret_cast<int*>(bar_s + 5);
 
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
-  const int row = 32 * (w & 3) + lane;  // key row: TMEM lane
-  const int cg = w >> 2;                // column group: 16 queries (S, dP) or dims (dV, dK, dQ)
+  const bool mma_warp = w == NT / 32;   // warp 16 issues every MMA
+  const int row = 32 * (w & 3) + lane;  // key row: TMEM lane (compute warps)
+  const int cg = (w >> 2) & 3;          // column group: 16 queries (S, dP) or dims (dV, dK, dQ)
   const int S = a.S;
   const int nkb = a.n_kblocks;
   // (b, h)-major: a (b, h)'s key blocks run side by side and its last one finishes early.
@@ -207,12 +255,14 @@ __global__ void __launch_bounds__(NT, 1) bwd_tc_kernel(const BwdArgs a) {
   const float* gp = a.d_o + b * a.do_sb + h * a.do_sh;
   const float* lp = a.lse + static_cast<int64_t>(bh) * S;
   const float* dp = a.dsum + static_cast<int64_t>(bh) * S;
-  const int n_tiles = (S + QT - 1) / QT;
   const int t_begin = CAUSAL ? k0 / QT : 0;  // queries before the block's first key see none
+  const int N = (S + QT - 1) / QT - t_begin;  // query tiles, >= 1 (k0 < S)
 
   if (tid == 0) {
-    tc::mbar_init(bar_a, 1);
-    tc::mbar_init(bar_b, 1);
+    tc::mbar_init(bar_s, 1);
+    tc::mbar_init(bar_t2, 1);
+    tc::mbar_init(bar_c1, NT / 32);
+    tc::mbar_init(bar_q, NT / 32);
     tc::fence_mbar_init();
   }
   if (w == 0) {
@@ -221,162 +271,189 @@ __global__ void __launch_bounds__(NT, 1) bwd_tc_kernel(const BwdArgs a) {
   }
   griddep_launch_dependents();
 
-  // Q, dO, L, D of tile t into this thread's staging slots (Q: slots 0-1, dO: 2-3 of the staging
-  // area) and L / D buffer `buf` (threads 0-127).
-  auto stage_tile = [&](int t, int buf) {
-    const int q0 = t * QT;
-    stage_row_item(st, 0, tid, qp, a.q_ss, q0, S);
-    stage_row_item(st, 1, tid, gp, a.do_ss, q0, S);
+  // Q, dO of tile n into this thread's staging slots (Q: slots 0-1, dO: 2-3) and its L, D into
+  // L / D buffer n % 2 (threads 0-127).
+  auto stage_ld = [&](int n) {
     if (tid < 2 * QT) {
-      const int r = tid & 63, i = q0 + r;
+      const int r = tid & 63, i = (t_begin + n) * QT + r;
       const bool ok = i < S;
-      cp_async4(ld + buf * 128 + (tid < QT ? 0 : QT) + r, (tid < QT ? lp : dp) + (ok ? i : 0),
+      cp_async4(ld + (n & 1) * 128 + (tid < QT ? 0 : QT) + r, (tid < QT ? lp : dp) + (ok ? i : 0),
                 ok ? 4 : 0);
     }
   };
-  auto split_tile = [&]() {
-    split_row_item(Qp, PART_Q, st, 0, tid);
-    split_row_item(dOp, PART_Q, st, 1, tid);
+  auto stage_tile = [&](int n) {
+    const int q0 = (t_begin + n) * QT;
+    stage_row_item(st, 0, tid, qp, a.q_ss, q0, S);
+    stage_row_item(st, 1, tid, gp, a.do_ss, q0, S);
+    stage_ld(n);
+  };
+  auto split_tile = [&](int n) {
+    split_row_item(Qp + (n & 1) * 3 * PART_Q, PART_Q, st, 0, tid);
+    split_row_item(dOp + (n & 1) * 3 * PART_Q, PART_Q, st, 1, tid);
   };
 
-  // Prologue: K (staged in the dS^T buffer), V (in the staging area) and the first query tile.
-  // K and V are caller inputs; L, D and the cleared counters come after the prep kernel's wait.
-  stage_row_item(dSp, 0, tid, kp, a.k_ss, k0, S);
-  stage_row_item(dSp, 1, tid + NT, kp, a.k_ss, k0, S);
-  stage_row_item(st, 0, tid, vp, a.v_ss, k0, S);
-  stage_row_item(st, 1, tid + NT, vp, a.v_ss, k0, S);
-  cp_async_commit();
-  cp_async_wait_all();
-  split_row_item(Kp, PART_K, dSp, 0, tid);
-  split_row_item(Kp, PART_K, dSp, 1, tid + NT);
-  split_row_item(Vp, PART_K, st, 0, tid);
-  split_row_item(Vp, PART_K, st, 1, tid + NT);
-  __syncthreads();  // staging free
-  griddep_wait();   // L, D, the cleared counters: the prep kernel's writes
-  if (t_begin < n_tiles) stage_tile(t_begin, 0);
-  cp_async_commit();
-  cp_async_wait_all();
-  split_tile();
-  tc::fence_async_smem();
+  // Prologue: K's parts into shared memory (staged in the dS^T buffer), V's into TMEM (this
+  // thread's key row and 16 dims: K-step cg of the A operand of dP^T), tile 0's Q and dO parts,
+  // tile 1 in flight. K, V, Q, dO are caller inputs and travel together; L, D and the cleared
+  // counters come after the prep kernel's wait.
+  float vx[16];
+  if (!mma_warp) {
+    stage_row_item(dSp, 0, tid, kp, a.k_ss, k0, S);
+    stage_row_item(dSp, 1, tid + NT, kp, a.k_ss, k0, S);
+    stage_row_item(st, 0, tid, qp, a.q_ss, t_begin * QT, S);
+    stage_row_item(st, 1, tid, gp, a.do_ss, t_begin * QT, S);
+    cp_async_commit();
+    const bool ok = k0 + row < S;
+    const float4* vr =
+        reinterpret_cast<const float4*>(vp + static_cast<int64_t>(ok ? k0 + row : 0) * a.v_ss + 16 * cg);
+#pragma unroll
+    for (int c4 = 0; c4 < 4; ++c4) {
+      const float4 u = ok ? vr[c4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      vx[4 * c4] = u.x;
+      vx[4 * c4 + 1] = u.y;
+      vx[4 * c4 + 2] = u.z;
+      vx[4 * c4 + 3] = u.w;
+    }
+    griddep_wait();  // L, D, the cleared counters: the prep kernel's writes
+    stage_ld(0);
+    cp_async_commit();
+    cp_async_wait_all();
+    split_row_item(Kp, PART_K, dSp, 0, tid);
+    split_row_item(Kp, PART_K, dSp, 1, tid + NT);
+    split_tile(0);
+    tc::fence_async_smem();
+  }
+  tc::fence_before_sync();
+  __syncthreads();  // the TMEM base; L, D of tile 0 (threads 0-127); the K staging read
+  tc::fence_after_sync();
+  const uint32_t tbase = *tbase_p;
+  const uint32_t lane_sel = static_cast<uint32_t>(32 * (w & 3)) << 16;
+  if (!mma_warp) {
+    uint32_t vparts[3][8];
+    split16(vx, vparts);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) tmem_st8(tbase + lane_sel + T_V + 32 * i + 8 * cg, vparts[i]);
+    tc::tmem_wait_st();
+    if (N > 1) stage_tile(1);
+    cp_async_commit();
+  }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
 
-  const uint32_t tbase = *tbase_p;
-  const uint32_t lane_sel = static_cast<uint32_t>(32 * (w & 3)) << 16;
-  const uint32_t id128 = tc::idesc_f32acc(1, KB, QT);           // M 128, N 64, both K-major
-  const uint32_t id_dv = id128 | (1u << 16);                     // B MN-major
-  const uint32_t id_dq = tc::idesc_f32acc(1, QT, 64) | (1u << 15) | (1u << 16);  // M 64, A, B MN
-  const uint32_t sK = tc::smem_u32(Kp), sV = tc::smem_u32(Vp), sQ = tc::smem_u32(Qp),
-                 sO = tc::smem_u32(dOp), sS = tc::smem_u32(dSp);
-
-  float dv[16], dk[16];
-#pragma unroll
-  for (int c = 0; c < 16; ++c) dv[c] = dk[c] = 0.0f;
   bool err = false;
   const int key = k0 + row;
-
-  int n = 0;  // tiles done: the mbarrier phase
-  for (int t = t_begin; t < n_tiles; ++t, ++n) {
-    const int q0 = t * QT, buf = n & 1;
-    // (1) S^T and dP^T.
-    if (tid == 0) {
-      // S^T in the forward's product order (its pairs (Q i, K j) as (K j, Q i)).
-      issue6<4, PART_K, PART_Q, 256, 256, true>(tbase, tc::desc_kmajor(sK, 128, 1024),
-                                                tc::desc_kmajor(sQ, 128, 1024), id128);
-      issue6<4, PART_K, PART_Q, 256, 256, false>(tbase + 64, tc::desc_kmajor(sV, 128, 1024),
-                                                 tc::desc_kmajor(sO, 128, 1024), id128);
-      tc::commit(bar_a);
-    }
-    // (2) the next tile travels.
-    if (t + 1 < n_tiles) stage_tile(t + 1, buf ^ 1);
-    cp_async_commit();
-    // (3) P^T and dS^T for this thread's 16 queries.
-    err |= !tc::mbar_wait(bar_a, n & 1, WAIT_TIMEOUT_NS);
-    tc::fence_after_sync();
-    const float* Lt = ld + buf * 128;
-    const float* Dt = Lt + QT;
-    const bool edge = (q0 + QT > S) || (k0 + KB > S) || (CAUSAL && k0 + KB - 1 > q0);
-    float pr[16];
+  float dv[16], dk[16];  // compute threads: dV, dK of the key row, this thread's 16 dims
 #pragma unroll
-    for (int h8 = 0; h8 < 2; ++h8) {
-      const uint32_t col = 16 * cg + 8 * h8;
-      float sb[8], gb[8];
-      tmem_ld8(tbase + lane_sel + col, sb);
-      tmem_ld8(tbase + lane_sel + 64 + col, gb);
-      tc::tmem_wait_ld();
-      float ds[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int ql = col + u, qi = q0 + ql;
-        // P = e^(s * scale - L), one rounding of the argument (as bwd_ffma.cu).
-        float p = expf(fmaf(sb[u], a.scale, -Lt[ql]));
-        if (edge && !(qi < S && key < S && !(CAUSAL && key > qi))) p = 0.0f;
-        pr[8 * h8 + u] = p;
-        ds[u] = p * (gb[u] - Dt[ql]);
+  for (int c = 0; c < 16; ++c) dv[c] = dk[c] = 0.0f;
+  if (mma_warp) {
+    {  // every lane runs the loop (warp-uniform); one elected lane issues each MMA and commit
+      const uint32_t id128 = tc::idesc_f32acc(1, KB, QT);                       // M 128, N 64
+      const uint32_t id_mn = id128 | (1u << 16);                                 // B MN-major
+      const uint32_t id_dq = tc::idesc_f32acc(1, QT, 64) | (1u << 15) | (1u << 16);  // M 64
+      const uint32_t sK = tc::smem_u32(Kp), sS = tc::smem_u32(dSp);
+      // S^T (the forward's product order) and dP^T (A: V's parts in TMEM) of tile n.
+      auto issue_t1 = [&](int n) {
+        const uint32_t sQ = tc::smem_u32(Qp + (n & 1) * 3 * PART_Q);
+        const uint32_t sO = tc::smem_u32(dOp + (n & 1) * 3 * PART_Q);
+        issue6<4, PART_K, PART_Q, 256, 256, true>(tbase + T_S,
+                                                  tc::split_desc(tc::desc_kmajor(sK, 128, 1024)),
+                                                  tc::split_desc(tc::desc_kmajor(sQ, 128, 1024)), id128);
+        issue6_tmem_a<PART_Q, 256>(
+            tbase + T_DP, [&](int i, int ks) { return tbase + T_V + 32 * i + 8 * ks; },
+            tc::split_desc(tc::desc_kmajor(sO, 128, 1024)), id128);
+        tc::commit_warp(bar_s);
+      };
+      // dV (A: P^T's parts in TMEM), dK, dQ (two windows of 64 keys) of tile n.
+      auto issue_t2 = [&](int n) {
+        const uint32_t sQ = tc::smem_u32(Qp + (n & 1) * 3 * PART_Q);
+        const uint32_t sO = tc::smem_u32(dOp + (n & 1) * 3 * PART_Q);
+        issue6_tmem_a<PART_Q, 2048>(tbase + T_DV, [&](int i, int ks) { return tbase + pt_col(i, ks); },
+                                    tc::split_desc(tc::desc_kmajor(sO, 1024, 128)), id_mn);
+        issue6<4, PART_K, PART_Q, 256, 2048, false>(tbase + T_DK,
+                                                    tc::split_desc(tc::desc_kmajor(sS, 128, 1024)),
+                                                    tc::split_desc(tc::desc_kmajor(sQ, 1024, 128)), id_mn);
+        const tc::Desc as_mn = tc::split_desc(tc::desc_kmajor(sS, 1024, 128));
+        const tc::Desc bk_mn = tc::split_desc(tc::desc_kmajor(sK, 1024, 128));
+        issue6<4, PART_K, PART_K, 2048, 2048, false>(tbase + T_DQ0, as_mn, bk_mn, id_dq);
+        issue6<4, PART_K, PART_K, 2048, 2048, false>(
+            tbase + T_DQ1, {as_mn.lo + (8192 >> 4), as_mn.hi}, {bk_mn.lo + (8192 >> 4), bk_mn.hi},
+            id_dq);
+        tc::commit_warp(bar_t2);
+      };
+      issue_t1(0);
+      for (int n = 0; n < N; ++n) {
+        err |= !tc::mbar_wait(bar_c1, n & 1, WAIT_TIMEOUT_NS);
+        tc::fence_after_sync();
+        issue_t2(n);
+        if (n + 1 < N) {
+          err |= !tc::mbar_wait(bar_q, n & 1, WAIT_TIMEOUT_NS);
+          err |= !tc::mbar_wait(bar_t2, n & 1, WAIT_TIMEOUT_NS);  // T2(n) has read P^T(n)
+          tc::fence_after_sync();
+          issue_t1(n + 1);
+        }
       }
-      store_parts(dSp, PART_K, kmaj_off(row, 2 * cg + h8), ds);
     }
-    // (4) P^T's parts over columns 0-95, once every thread has read S^T and dP^T.
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    {
-      uint4 lo[3], hi[3];
-      float x0[8], x1[8];
+  } else {
+    for (int n = 0; n < N; ++n) {
+      const int q0 = (t_begin + n) * QT;
+      // (C1) P^T and dS^T for this thread's 16 queries.
+      err |= !tc::mbar_wait(bar_s, n & 1, WAIT_TIMEOUT_NS);
+      tc::fence_after_sync();
+      const float* Lt = ld + (n & 1) * 128;
+      const float* Dt = Lt + QT;
+      const bool edge = (q0 + QT > S) || (k0 + KB > S) || (CAUSAL && k0 + KB - 1 > q0);
+      float pr[16];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        x0[u] = pr[u];
-        x1[u] = pr[8 + u];
+      for (int h8 = 0; h8 < 2; ++h8) {
+        const uint32_t col = 16 * cg + 8 * h8;
+        float sb[8], gb[8];
+        tmem_ld8(tbase + lane_sel + T_S + col, sb);
+        tmem_ld8(tbase + lane_sel + T_DP + col, gb);
+        tc::tmem_wait_ld();
+        float ds[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int ql = col + u, qi = q0 + ql;
+          // P = e^(s * scale - L), one rounding of the argument (as bwd_ffma.cu).
+          float p = expf(fmaf(sb[u], a.scale, -Lt[ql]));
+          if (edge && !(qi < S && key < S && !(CAUSAL && key > qi))) p = 0.0f;
+          pr[8 * h8 + u] = p;
+          ds[u] = p * (gb[u] - Dt[ql]);
+        }
+        store_parts(dSp, PART_K, kmaj_off(row, 2 * cg + h8), ds);
       }
-      split8(x0, lo[0], lo[1], lo[2]);
-      split8(x1, hi[0], hi[1], hi[2]);
-#pragma unroll
-      for (int pt = 0; pt < 3; ++pt) {
-        const uint32_t v[8] = {lo[pt].x, lo[pt].y, lo[pt].z, lo[pt].w,
-                               hi[pt].x, hi[pt].y, hi[pt].z, hi[pt].w};
-        tmem_st8(tbase + lane_sel + 32 * pt + 8 * cg, v);
+      // P^T's parts over the S^T / dP^T columns this thread has just read (pt_col).
+      {
+        uint32_t pp[3][8];
+        split16(pr, pp);
+        tmem_st8(tbase + lane_sel + pt_col(0, cg), pp[0]);
+        tmem_st8(tbase + lane_sel + pt_col(1, cg), pp[1]);
+        tmem_st8(tbase + lane_sel + pt_col(2, cg), pp[2]);
+        tc::tmem_wait_st();
       }
-      tc::tmem_wait_st();
-    }
-    tc::fence_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    // (5) dV, dK, dQ.
-    if (tid == 0) {
-      const uint64_t bo_mn = tc::desc_kmajor(sO, 1024, 128);  // dO as B, MN-major (N = d)
-      const uint64_t bq_mn = tc::desc_kmajor(sQ, 1024, 128);  // Q as B, MN-major
-      const uint64_t bk_mn = tc::desc_kmajor(sK, 1024, 128);  // K as B, MN-major (K = keys)
-      const uint64_t as_k = tc::desc_kmajor(sS, 128, 1024);   // dS^T as A, K-major
-      const uint64_t as_mn = tc::desc_kmajor(sS, 1024, 128);  // dS^T as A, MN-major (M = q)
-      // dV: P^T part i of K-step ks at TMEM column 32 i + 8 ks; the same pair order as issue6.
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-#pragma unroll
-        for (int p = 1; p < 6; ++p)
-          mma_bf16_tmem_a(tbase + 128, tbase + 32 * P0(p) + 8 * ks,
-                          bo_mn + static_cast<uint64_t>((P1(p) * PART_Q + 2048 * ks) >> 4), id_dv,
-                          ks > 0 || p > 1);
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        mma_bf16_tmem_a(tbase + 128, tbase + 8 * ks,
-                        bo_mn + static_cast<uint64_t>((2048 * ks) >> 4), id_dv, 1);
-      issue6<4, PART_K, PART_Q, 256, 2048, false>(tbase + 192, as_k, bq_mn, id_dv);
-      // dQ: keys 0-63 and 64-127 (four K-steps each, 8192 bytes apart in both operands).
-      issue6<4, PART_K, PART_K, 2048, 2048, false>(tbase + 256, as_mn, bk_mn, id_dq);
-      issue6<4, PART_K, PART_K, 2048, 2048, false>(tbase + 320, as_mn + (8192 >> 4),
-                                                   bk_mn + (8192 >> 4), id_dq);
-      tc::commit(bar_b);
-    }
-    // (6) Fold dV, dK; write the dQ partial; the next tile's Q, dO into their parts.
-    cp_async_wait_all();
-    err |= !tc::mbar_wait(bar_b, n & 1, WAIT_TIMEOUT_NS);
-    tc::fence_after_sync();
-    {
+      tc::fence_async_smem();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(bar_c1);
+      // (C3) The next tile's Q, dO into their parts (its buffer was last read by T2(n - 1)), while
+      // the tensor core computes dV, dK, dQ; the tile after it travels.
+      if (n + 1 < N) {
+        cp_async_wait_all();
+        bar_sync(1, NT);  // L, D of tile n + 1 in place; every thread is past C1(n)
+        split_tile(n + 1);
+        tc::fence_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(bar_q);
+        if (n + 2 < N) stage_tile(n + 2);
+        cp_async_commit();
+      }
+      // (C2) Fold dV, dK; write the dQ partial.
+      err |= !tc::mbar_wait(bar_t2, n & 1, WAIT_TIMEOUT_NS);
+      tc::fence_after_sync();
       float xb[16], xs[16];
-      tc::tmem_ld16(tbase + lane_sel + 128 + 16 * cg, xb);
-      tc::tmem_ld16(tbase + lane_sel + 192 + 16 * cg, xs);
+      tc::tmem_ld16(tbase + lane_sel + T_DV + 16 * cg, xb);
+      tc::tmem_ld16(tbase + lane_sel + T_DK + 16 * cg, xs);
       tc::tmem_wait_ld();
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
@@ -384,8 +461,8 @@ __global__ void __launch_bounds__(NT, 1) bwd_tc_kernel(const BwdArgs a) {
         dk[c] += xs[c];
       }
       // dQ (M = 64): query row 16 (w % 4) + lane in lanes 0-15 of each quarter; the two windows.
-      tc::tmem_ld16(tbase + lane_sel + 256 + 16 * cg, xb);
-      tc::tmem_ld16(tbase + lane_sel + 320 + 16 * cg, xs);
+      tc::tmem_ld16(tbase + lane_sel + T_DQ0 + 16 * cg, xb);
+      tc::tmem_ld16(tbase + lane_sel + T_DQ1 + 16 * cg, xs);
       tc::tmem_wait_ld();
       const int qi = q0 + 16 * (w & 3) + lane;
       if (lane < 16 && qi < S && !err) {
@@ -397,19 +474,21 @@ __global__ void __launch_bounds__(NT, 1) bwd_tc_kernel(const BwdArgs a) {
                              xb[4 * c4 + 2] + xs[4 * c4 + 2], xb[4 * c4 + 3] + xs[4 * c4 + 3]));
       }
     }
-    if (t + 1 < n_tiles) split_tile();
-    tc::fence_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
   }
   cp_async_wait_all();
-
-  if (__syncthreads_or(err)) {
+  err = __syncthreads_or(err);  // any expired wait in the block: nothing is written
+  if (err) {
     if (tid == 0) atomicExch(a.err, CFA_ERR_TIMEOUT);
+    tc::mbar_wait(bar_t2, (N - 1) & 1, WAIT_TIMEOUT_NS);  // no MMA left in flight
   } else {
+    // The last of the (b, h)'s key blocks to finish sums its dQ partials in key-block order; the
+    // fence covers the partials only (dV, dK are stored after the count).
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_int[0] = atomicAdd(a.turn + bh, 1);
+    __syncthreads();
     // dV into slot 2, dK * scale into slot 1 of dqkv [b, s, 3, h, 64].
-    if (key < S) {
+    if (!mma_warp && key < S) {
       const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * 64;
       float* base = a.dqkv + (static_cast<int64_t>(b) * S + key) * row_stride + h * 64 + 16 * cg;
 #pragma unroll
@@ -421,29 +500,52 @@ __global__ void __launch_bounds__(NT, 1) bwd_tc_kernel(const BwdArgs a) {
                         dk[4 * c4 + 3] * a.scale);
       }
     }
-    // The last of the (b, h)'s key blocks to finish sums its dQ partials in key-block order.
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_int[0] = atomicAdd(a.turn + bh, 1);
-    __syncthreads();
     if (s_int[0] == nkb - 1) {
       __threadfence();
       const float* part = a.dq_part + static_cast<int64_t>(bh) * nkb * S * 64;
       const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * 64;
       float* dq_base = a.dqkv + static_cast<int64_t>(b) * S * row_stride + h * 64;
       // DETERMINISM: dQ = (((p0 + p1) + p2) + ...) * scale over the key blocks holding a key <=
-      // the row (causal) or all of them.
-      for (int idx = tid; idx < S * 16; idx += NT) {
-        const int i = idx >> 4, c4 = idx & 15;
-        const int last = CAUSAL ? min(nkb - 1, i / KB) : nkb - 1;
-        float4 v = __ldcg(reinterpret_cast<const float4*>(part + static_cast<int64_t>(i) * 64) + c4);
-        for (int j = 1; j <= last; ++j) {
-          const float4 p = __ldcg(
-              reinterpret_cast<const float4*>(part + (static_cast<int64_t>(j) * S + i) * 64) + c4);
-          v = make_float4(v.x + p.x, v.y + p.y, v.z + p.z, v.w + p.w);
+      // the row (causal) or all of them. Four float4 items per thread at a time, each key
+      // block's loads for the four issued together.
+      constexpr int U = 4;
+      const int items = S * 16;
+      for (int base = tid; base < items; base += U * NB) {
+        float4 v[U];
+        int last[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int idx = base + u * NB;
+          const int i = idx >> 4;
+          last[u] = idx < items ? (CAUSAL ? min(nkb - 1, i / KB) : nkb - 1) : -1;
+          v[u] = last[u] >= 0
+                     ? __ldcg(reinterpret_cast<const float4*>(part + static_cast<int64_t>(i) * 64) +
+                              (idx & 15))
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        reinterpret_cast<float4*>(dq_base + i * row_stride)[c4] =
-            make_float4(v.x * a.scale, v.y * a.scale, v.z * a.scale, v.w * a.scale);
+        for (int j = 1; j < nkb; ++j) {
+          float4 p[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int idx = base + u * NB;
+            p[u] = j <= last[u] ? __ldcg(reinterpret_cast<const float4*>(
+                                             part + (static_cast<int64_t>(j) * S + (idx >> 4)) * 64) +
+                                         (idx & 15))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (j <= last[u]) v[u] = make_float4(v[u].x + p[u].x, v[u].y + p[u].y, v[u].z + p[u].z,
+                                                 v[u].w + p[u].w);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int idx = base + u * NB;
+          if (last[u] >= 0)
+            reinterpret_cast<float4*>(dq_base + (idx >> 4) * row_stride)[idx & 15] =
+                make_float4(v[u].x * a.scale, v[u].y * a.scale, v[u].z * a.scale,
+                            v[u].w * a.scale);
+        }
       }
     }
   }
@@ -467,8 +569,8 @@ cudaError_t launch_bwd_tc(const BwdArgs& args, int causal, cudaStream_t stream) 
   BwdArgs a = args;
   a.n_kblocks = (a.S + KB - 1) / KB;
   const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(a.n_kblocks) * a.B * a.H));
-  if (causal) return launch_pdl(bwd_tc_kernel<true>, grid, dim3(NT), SMEM_ALLOC, stream, a);
-  return launch_pdl(bwd_tc_kernel<false>, grid, dim3(NT), SMEM_ALLOC, stream, a);
+  if (causal) return launch_pdl(bwd_tc_kernel<true>, grid, dim3(NB), SMEM_ALLOC, stream, a);
+  return launch_pdl(bwd_tc_kernel<false>, grid, dim3(NB), SMEM_ALLOC, stream, a);
 }
 
 }  // namespace cfa

@@ -46,6 +46,74 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
+// The same, called by a whole converged warp with warp-uniform operands: one lane (elect.sync)
+// issues. Keeping the caller's control flow uniform keeps the descriptor arithmetic off the
+// per-lane path.
+__device__ __forceinline__ void mma_bf16_warp(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Descriptors as two 32-bit words. A shared-memory descriptor's start-address field (bytes / 16)
+// is its low 14 bits and, shared memory being < 256 KB, an in-range offset never carries out of
+// it: offsetting a descriptor only changes the low word. The issue helpers below take the words
+// and offset the low ones with immediates, so a tile's many descriptors need not live in registers.
+struct Desc {
+  uint32_t lo, hi;
+};
+__device__ __forceinline__ Desc split_desc(uint64_t d) {
+  return {static_cast<uint32_t>(d), static_cast<uint32_t>(d >> 32)};
+}
+// An opaque copy: the compiler cannot fold it into, or hoist it above, the surrounding issue code.
+__device__ __forceinline__ uint32_t opaque(uint32_t x) {
+  asm volatile("" : "+r"(x));
+  return x;
+}
+
+// mma_bf16_warp on descriptor words (a_lo / b_lo already offset).
+__device__ __forceinline__ void mma_bf16_warp(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi,
+                                              uint32_t b_lo, uint32_t b_hi, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b64 ad, bd;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\tmov.b64 ad, {%1, %2};\n\tmov.b64 bd, {%3, %4};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate));
+}
+
+// A in TMEM (lane r = row r), B from descriptor words; one elected lane of the warp.
+__device__ __forceinline__ void mma_bf16_tmem_a_warp(uint32_t d_tmem, uint32_t a_tmem,
+                                                     uint32_t b_lo, uint32_t b_hi, uint32_t idesc,
+                                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b64 bd;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\tmov.b64 bd, {%2, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], bd, %4, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate));
+}
+
+// A in TMEM (lane r = row r), B from a shared-memory descriptor; one elected lane of the warp.
+__device__ __forceinline__ void mma_bf16_tmem_a_warp(uint32_t d_tmem, uint32_t a_tmem,
+                                                     uint64_t bdesc, uint32_t idesc,
+                                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// commit() by one elected lane of a converged warp.
+__device__ __forceinline__ void commit_warp(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
 // The same with tf32 inputs (fp32 containers; the low 13 mantissa bits are not used).
 __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                          uint32_t idesc, uint32_t accumulate) {
@@ -66,6 +134,15 @@ __device__ __forceinline__ void commit(uint64_t* bar) {
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
                : "memory");
+}
+
+// One arrival on `bar` (release at CTA scope: this thread's earlier writes, and those of the
+// threads it synchronised with, are visible to a thread whose wait sees the phase complete).
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\tmbarrier.arrive.release.cta.shared::cta.b64 st, [%0];\n\t}\n" ::"r"(
+          smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void fence_mbar_init() {

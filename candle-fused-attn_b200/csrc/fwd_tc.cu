@@ -173,19 +173,18 @@ __device__ __forceinline__ void issue_split_mma(uint32_t d, uint32_t a_base, uin
                                                 uint32_t idesc) {
   constexpr int PA[6] = {0, 0, 1, 0, 1, 2};
   constexpr int PB[6] = {0, 1, 0, 2, 1, 0};
-  const uint64_t ad0 = tc::desc_kmajor(a_base, 128, 1024);
-  const uint64_t bd0 = tc::desc_kmajor(b_base, 128, 1024);
+  const tc::Desc ad = tc::split_desc(tc::desc_kmajor(a_base, 128, 1024));
+  const tc::Desc bd = tc::split_desc(tc::desc_kmajor(b_base, 128, 1024));
+  const uint32_t alo = tc::opaque(ad.lo), blo = tc::opaque(bd.lo);
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks)
 #pragma unroll
     for (int p = 1; p < 6; ++p)
-      tc::mma_bf16(d, ad0 + static_cast<uint64_t>((PA[p] * A_PART + 256 * ks) >> 4),
-                   bd0 + static_cast<uint64_t>((PB[p] * B_PART + 256 * ks) >> 4), idesc,
-                   ks > 0 || p > 1);
+      tc::mma_bf16_warp(d, alo + ((PA[p] * A_PART + 256 * ks) >> 4), ad.hi,
+                        blo + ((PB[p] * B_PART + 256 * ks) >> 4), bd.hi, idesc, ks > 0 || p > 1);
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks)
-    tc::mma_bf16(d, ad0 + static_cast<uint64_t>((256 * ks) >> 4),
-                 bd0 + static_cast<uint64_t>((256 * ks) >> 4), idesc, 1);
+    tc::mma_bf16_warp(d, alo + ((256 * ks) >> 4), ad.hi, blo + ((256 * ks) >> 4), bd.hi, idesc, 1);
 }
 
 // Named barriers: 1 = the softmax threads (TC_THREADS), 2 = those plus the MMA warp (TC_BLOCK).
@@ -290,27 +289,23 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
     const uint32_t idesc = tc::idesc_f32acc(1, TC_BM, TC_BN);
     const uint32_t sQ = tc::smem_u32(Qp), sV = tc::smem_u32(Vp), sP = tc::smem_u32(Pp);
     const uint32_t sK0 = tc::smem_u32(sm + OFF_K);
-    if (lane == 0) {
-      issue_split_mma<PART_Q, PART_K>(tbase, sQ, sK0, idesc);
-      tc::commit(bar_s);
-      if (T > 1) {
-        issue_split_mma<PART_Q, PART_K>(tbase + 64, sQ, sK0 + 3 * PART_K, idesc);
-        tc::commit(bar_s + 1);
-      }
+    // The whole warp runs the issue code (warp-uniform operands); one elected lane issues.
+    issue_split_mma<PART_Q, PART_K>(tbase, sQ, sK0, idesc);
+    tc::commit_warp(bar_s);
+    if (T > 1) {
+      issue_split_mma<PART_Q, PART_K>(tbase + 64, sQ, sK0 + 3 * PART_K, idesc);
+      tc::commit_warp(bar_s + 1);
     }
     for (int n = 0; n < T; ++n) {
       bar_sync(2, TC_BLOCK);
       tc::fence_after_sync();
-      if (lane == 0) {
-        const int j = n & 1;
-        issue_split_mma<PART_Q, PART_K>(t_o, sP, sV, idesc);
-        tc::commit(bar_o);
-        if (n + 2 < T) {
-          issue_split_mma<PART_Q, PART_K>(tbase + 64 * j, sQ, sK0 + 3 * PART_K * j, idesc);
-          tc::commit(bar_s + j);
-        }
+      const int j = n & 1;
+      issue_split_mma<PART_Q, PART_K>(t_o, sP, sV, idesc);
+      tc::commit_warp(bar_o);
+      if (n + 2 < T) {
+        issue_split_mma<PART_Q, PART_K>(tbase + 64 * j, sQ, sK0 + 3 * PART_K * j, idesc);
+        tc::commit_warp(bar_s + j);
       }
-      __syncwarp();
     }
   }
 
