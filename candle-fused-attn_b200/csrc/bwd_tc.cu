@@ -39,9 +39,16 @@
 
 #include "cfa_common.cuh"
 #include "cfa_internal.h"
+#include "cfa_split.cuh"
 #include "cfa_tc.cuh"
 
 namespace cfa {
+using tc::kmaj_off;
+using tc::split16;
+using tc::split8;
+using tc::store_parts;
+using tc::tmem_ld8;
+using tc::tmem_st8;
 namespace {
 
 constexpr int KB = 128;   // keys per block: MMA M of S^T, dP^T, dV, dK
@@ -56,7 +63,7 @@ constexpr int OFF_DO = OFF_Q + 6 * PART_Q;    // dO parts [64 q][64 d], two tile
 constexpr int OFF_DS = OFF_DO + 6 * PART_Q;   // dS^T parts [128 keys][64 q] (first: K staged)
 constexpr int OFF_ST = OFF_DS + 3 * PART_K;   // staging: the next tile's Q, dO (fp32)
 constexpr int OFF_LD = OFF_ST + 2 * QT * 64 * 4;  // L, D of two tiles: float [2][2][64]
-constexpr int OFF_BAR = OFF_LD + 2 * 2 * QT * 4;  // four mbarriers, the TMEM base, two ints
+constexpr int OFF_BAR = OFF_LD + 2 * 2 * QT * 4;  // five mbarriers, the TMEM base, two ints
 constexpr int SMEM = OFF_BAR + 64;
 constexpr int SMEM_ALLOC = SMEM + 1024;
 static_assert(SMEM_ALLOC <= 232448, "shared memory per block");
@@ -71,62 +78,6 @@ constexpr uint32_t TMEM_COLS = 512;
 // that group's S^T columns, part 2 over its first 8 dP^T columns.
 __host__ __device__ constexpr uint32_t pt_col(int i, int ks) {
   return i < 2 ? T_S + 16 * ks + 8 * i : T_DP + 16 * ks;
-}
-
-__device__ __forceinline__ uint32_t kmaj_off(int row, int kc) {
-  return static_cast<uint32_t>((((row >> 3) * 8 + kc) << 7) + ((row & 7) << 4));
-}
-
-__device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) {
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
-// x[0..7] -> three rows of 8 bf16 parts (x = p0 + p1 + p2 + below 2^-24 relative).
-__device__ __forceinline__ void split8(const float (&x)[8], uint4& p0, uint4& p1, uint4& p2) {
-  uint32_t a[4], b[4], c[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float x0 = x[2 * i], x1 = x[2 * i + 1];
-    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-    const float2 hf = __bfloat1622float2(h);
-    const float r0 = x0 - hf.x, r1 = x1 - hf.y;
-    const __nv_bfloat162 m = __floats2bfloat162_rn(r0, r1);
-    const float2 mf = __bfloat1622float2(m);
-    const __nv_bfloat162 l = __floats2bfloat162_rn(r0 - mf.x, r1 - mf.y);
-    a[i] = bf2_bits(h);
-    b[i] = bf2_bits(m);
-    c[i] = bf2_bits(l);
-  }
-  p0 = make_uint4(a[0], a[1], a[2], a[3]);
-  p1 = make_uint4(b[0], b[1], b[2], b[3]);
-  p2 = make_uint4(c[0], c[1], c[2], c[3]);
-}
-
-// x[0..15] -> the three parts as packed bf16 pairs (TMEM operand columns, even element low).
-__device__ __forceinline__ void split16(const float (&x)[16], uint32_t (&p)[3][8]) {
-  float lo[8], hi[8];
-#pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    lo[u] = x[u];
-    hi[u] = x[8 + u];
-  }
-  uint4 l[3], h[3];
-  split8(lo, l[0], l[1], l[2]);
-  split8(hi, h[0], h[1], h[2]);
-#pragma unroll
-  for (int i = 0; i < 3; ++i) {
-    p[i][0] = l[i].x, p[i][1] = l[i].y, p[i][2] = l[i].z, p[i][3] = l[i].w;
-    p[i][4] = h[i].x, p[i][5] = h[i].y, p[i][6] = h[i].z, p[i][7] = h[i].w;
-  }
-}
-
-__device__ __forceinline__ void store_parts(unsigned char* base, int part_bytes, uint32_t off,
-                                            const float (&x)[8]) {
-  uint4 p0, p1, p2;
-  split8(x, p0, p1, p2);
-  *reinterpret_cast<uint4*>(base + off) = p0;
-  *reinterpret_cast<uint4*>(base + part_bytes + off) = p1;
-  *reinterpret_cast<uint4*>(base + 2 * part_bytes + off) = p2;
 }
 
 // Row items (row r, elements 8 kc .. 8 kc + 7): item c takes row 8 (c / 64) + c % 8 and chunk
@@ -158,22 +109,22 @@ __device__ __forceinline__ void split_row_item(unsigned char* parts, int part_by
   store_parts(parts, part_bytes, kmaj_off(r, kc), x);
 }
 
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
-  uint32_t r[8];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7])
-      : "r"(taddr));
+// Row item c of a row-major staging area with rows of 68 floats (rows >= valid read as zeros) into
+// the K-major parts at part_bytes apart.
+__device__ __forceinline__ void split_staged_row(unsigned char* parts, int part_bytes,
+                                                 const float* rows, int c, int valid) {
+  int r, kc;
+  row_item(c, r, kc);
+  float x[8];
+  if (r < valid) {
+    const float4 u = reinterpret_cast<const float4*>(rows + r * 68 + 8 * kc)[0];
+    const float4 v = reinterpret_cast<const float4*>(rows + r * 68 + 8 * kc)[1];
+    x[0] = u.x, x[1] = u.y, x[2] = u.z, x[3] = u.w, x[4] = v.x, x[5] = v.y, x[6] = v.z, x[7] = v.w;
+  } else {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 8; ++i) x[i] = 0.0f;
+  }
+  store_parts(parts, part_bytes, kmaj_off(r, kc), x);
 }
 
 // One window: six split products over STEPS K-steps into the fresh accumulator `d`; descriptors
@@ -215,6 +166,13 @@ __device__ __forceinline__ void issue6_tmem_a(uint32_t d, ACol acol, tc::Desc bd
     tc::mma_bf16_tmem_a_warp(d, acol(0, ks), blo + ((B_STEP * ks) >> 4), bd.hi, idesc, 1);
 }
 
+// atomicAdd with acquire-release semantics at GPU scope.
+__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 // Named barrier 1: the 16 compute warps (the MMA warp never takes part).
 __device__ __forceinline__ void bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -235,8 +193,9 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
   uint64_t* bar_t2 = bar_s + 1;  // dV, dK, dQ of a tile done
   uint64_t* bar_c1 = bar_s + 2;  // P^T, dS^T of a tile in place (one arrival per compute warp)
   uint64_t* bar_q = bar_s + 3;   // Q, dO parts of the next tile in place (same)
-  uint32_t* tbase_p = reinterpret_cast<uint32_t*>(bar_s + 4);
-  int* s_int = reinterpret_cast<int*>(bar_s + 5);
+  uint64_t* bar_ld = bar_s + 4;  // the prologue's bulk row copies
+  uint32_t* tbase_p = reinterpret_cast<uint32_t*>(bar_s + 5);
+  int* s_int = reinterpret_cast<int*>(bar_s + 6);
 
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
   const bool mma_warp = w == NT / 32;   // warp 16 issues every MMA
@@ -257,13 +216,16 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
   const float* dp = a.dsum + static_cast<int64_t>(bh) * S;
   const int t_begin = CAUSAL ? k0 / QT : 0;  // queries before the block's first key see none
   const int N = (S + QT - 1) / QT - t_begin;  // query tiles, >= 1 (k0 < S)
+  bool err0 = false;
 
   if (tid == 0) {
     tc::mbar_init(bar_s, 1);
     tc::mbar_init(bar_t2, 1);
     tc::mbar_init(bar_c1, NT / 32);
     tc::mbar_init(bar_q, NT / 32);
+    tc::mbar_init(bar_ld, 1);
     tc::fence_mbar_init();
+    tc::mbar_arrive_expect_tx(bar_ld, 256u * (2 * min(KB, S - k0) + 2 * min(QT, S - t_begin * QT)));
   }
   if (w == 0) {
     tc::tmem_alloc(tbase_p, TMEM_COLS);
@@ -287,40 +249,76 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
     stage_row_item(st, 1, tid, gp, a.do_ss, q0, S);
     stage_ld(n);
   };
+  // The block one wave later (blockIdx + a.wave_ctas) starts by reading its key block's K, V rows
+  // and its first query tile's Q, dO rows, all at once across the wave: pull them into L2 while
+  // this wave computes and HBM is otherwise idle (one 256-byte row per thread).
+  auto prefetch_next_wave = [&]() {
+    const int nb = static_cast<int>(blockIdx.x) + a.wave_ctas;
+    if (a.wave_ctas <= 0 || nb >= static_cast<int>(gridDim.x) || tid >= 2 * KB + 2 * QT) return;
+    const int nkb2 = nb % nkb, nbh = nb / nkb, nb_b = nbh / a.H, nb_h = nbh % a.H;
+    const int r = tid < 2 * KB ? (tid & (KB - 1)) : (tid & (QT - 1));
+    const int row = tid < 2 * KB ? nkb2 * KB + r : (CAUSAL ? nkb2 * KB : 0) + r;
+    if (row >= S) return;
+    const float* src;
+    if (tid < KB) src = a.k + nb_b * a.k_sb + nb_h * a.k_sh + static_cast<int64_t>(row) * a.k_ss;
+    else if (tid < 2 * KB) src = a.v + nb_b * a.v_sb + nb_h * a.v_sh + static_cast<int64_t>(row) * a.v_ss;
+    else if (tid < 2 * KB + QT) src = a.q + nb_b * a.q_sb + nb_h * a.q_sh + static_cast<int64_t>(row) * a.q_ss;
+    else src = a.d_o + nb_b * a.do_sb + nb_h * a.do_sh + static_cast<int64_t>(row) * a.do_ss;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], 256;" ::"l"(src) : "memory");
+  };
   auto split_tile = [&](int n) {
     split_row_item(Qp + (n & 1) * 3 * PART_Q, PART_Q, st, 0, tid);
     split_row_item(dOp + (n & 1) * 3 * PART_Q, PART_Q, st, 1, tid);
   };
 
-  // Prologue: K's parts into shared memory (staged in the dS^T buffer), V's into TMEM (this
-  // thread's key row and 16 dims: K-step cg of the A operand of dP^T), tile 0's Q and dO parts,
-  // tile 1 in flight. K, V, Q, dO are caller inputs and travel together; L, D and the cleared
+  // Prologue: K's parts into shared memory, V's into TMEM (this thread's key row and 16 dims:
+  // K-step cg of the A operand of dP^T), tile 0's Q and dO parts. The rows of K, V, Q, dO travel
+  // as one bulk copy each (threads 0-383, one row apiece) into row-major staging with rows of
+  // LDP = 68 floats (the dS^T and staging buffers: K, V; the second Q and dO part buffers: Q, dO
+  // of tile 0); rows past the sequence are not copied and read as zeros. L, D and the cleared
   // counters come after the prep kernel's wait.
+  constexpr int LDP = 68;
+  float* k_rows = reinterpret_cast<float*>(dSp);
+  float* v_rows = k_rows + KB * LDP;
+  float* q_rows = reinterpret_cast<float*>(Qp + 3 * PART_Q);
+  float* o_rows = reinterpret_cast<float*>(dOp + 3 * PART_Q);
+  static_assert(2 * KB * LDP * 4 <= 3 * PART_K + 2 * QT * 64 * 4 && QT * LDP * 4 <= 3 * PART_Q,
+                "prologue staging");
+  const int nk = min(KB, S - k0), nq = min(QT, S - t_begin * QT);
+  __syncthreads();  // the mbarriers' initialisation
   float vx[16];
   if (!mma_warp) {
-    stage_row_item(dSp, 0, tid, kp, a.k_ss, k0, S);
-    stage_row_item(dSp, 1, tid + NT, kp, a.k_ss, k0, S);
-    stage_row_item(st, 0, tid, qp, a.q_ss, t_begin * QT, S);
-    stage_row_item(st, 1, tid, gp, a.do_ss, t_begin * QT, S);
+    if (tid < 2 * KB + 2 * QT) {
+      const int r = tid < 2 * KB ? (tid & (KB - 1)) : (tid & (QT - 1));
+      if (tid < KB) {
+        if (r < nk) tc::bulk_load(k_rows + r * LDP, kp + static_cast<int64_t>(k0 + r) * a.k_ss, 256, bar_ld);
+      } else if (tid < 2 * KB) {
+        if (r < nk) tc::bulk_load(v_rows + r * LDP, vp + static_cast<int64_t>(k0 + r) * a.v_ss, 256, bar_ld);
+      } else if (tid < 2 * KB + QT) {
+        if (r < nq)
+          tc::bulk_load(q_rows + r * LDP, qp + static_cast<int64_t>(t_begin * QT + r) * a.q_ss, 256, bar_ld);
+      } else if (r < nq) {
+        tc::bulk_load(o_rows + r * LDP, gp + static_cast<int64_t>(t_begin * QT + r) * a.do_ss, 256, bar_ld);
+      }
+    }
+    griddep_wait();  // L, D, the cleared counters: the prep kernel's writes
+    stage_ld(0);
     cp_async_commit();
-    const bool ok = k0 + row < S;
-    const float4* vr =
-        reinterpret_cast<const float4*>(vp + static_cast<int64_t>(ok ? k0 + row : 0) * a.v_ss + 16 * cg);
+    err0 = !tc::mbar_wait(bar_ld, 0, WAIT_TIMEOUT_NS);
+    cp_async_wait_all();
+    split_staged_row(Kp, PART_K, k_rows, tid, nk);
+    split_staged_row(Kp, PART_K, k_rows, tid + NT, nk);
+    split_staged_row(Qp, PART_Q, q_rows, tid, nq);
+    split_staged_row(dOp, PART_Q, o_rows, tid, nq);
 #pragma unroll
     for (int c4 = 0; c4 < 4; ++c4) {
-      const float4 u = ok ? vr[c4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 u = row < nk ? reinterpret_cast<const float4*>(v_rows + row * LDP + 16 * cg)[c4]
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
       vx[4 * c4] = u.x;
       vx[4 * c4 + 1] = u.y;
       vx[4 * c4 + 2] = u.z;
       vx[4 * c4 + 3] = u.w;
     }
-    griddep_wait();  // L, D, the cleared counters: the prep kernel's writes
-    stage_ld(0);
-    cp_async_commit();
-    cp_async_wait_all();
-    split_row_item(Kp, PART_K, dSp, 0, tid);
-    split_row_item(Kp, PART_K, dSp, 1, tid + NT);
-    split_tile(0);
     tc::fence_async_smem();
   }
   tc::fence_before_sync();
@@ -334,14 +332,12 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
 #pragma unroll
     for (int i = 0; i < 3; ++i) tmem_st8(tbase + lane_sel + T_V + 32 * i + 8 * cg, vparts[i]);
     tc::tmem_wait_st();
-    if (N > 1) stage_tile(1);
-    cp_async_commit();
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
 
-  bool err = false;
+  bool err = err0;
   const int key = k0 + row;
   float dv[16], dk[16];  // compute threads: dV, dK of the key row, this thread's 16 dims
 #pragma unroll
@@ -395,6 +391,8 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
       }
     }
   } else {
+    if (N > 1) stage_tile(1);  // while the MMA warp issues T1(0)
+    cp_async_commit();
     for (int n = 0; n < N; ++n) {
       const int q0 = (t_begin + n) * QT;
       // (C1) P^T and dS^T for this thread's 16 queries.
@@ -436,6 +434,7 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(bar_c1);
+      if (n == 0) prefetch_next_wave();
       // (C3) The next tile's Q, dO into their parts (its buffer was last read by T2(n - 1)), while
       // the tensor core computes dV, dK, dQ; the tile after it travels.
       if (n + 1 < N) {
@@ -481,34 +480,37 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
     if (tid == 0) atomicExch(a.err, CFA_ERR_TIMEOUT);
     tc::mbar_wait(bar_t2, (N - 1) & 1, WAIT_TIMEOUT_NS);  // no MMA left in flight
   } else {
-    // The last of the (b, h)'s key blocks to finish sums its dQ partials in key-block order; the
-    // fence covers the partials only (dV, dK are stored after the count).
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_int[0] = atomicAdd(a.turn + bh, 1);
-    __syncthreads();
-    // dV into slot 2, dK * scale into slot 1 of dqkv [b, s, 3, h, 64].
-    if (!mma_warp && key < S) {
-      const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * 64;
-      float* base = a.dqkv + (static_cast<int64_t>(b) * S + key) * row_stride + h * 64 + 16 * cg;
+    // The dQ partials' hand-off: after the barrier above, thread 0's acquire-release count
+    // publishes every thread's partial stores (the barrier orders them before it) and, for the
+    // last of the (b, h)'s key blocks, makes the other blocks' visible; that block sums them in
+    // key-block order (the loads bypass L1).
+    // dV into slot 2, dK * scale into slot 1 of dqkv [b, s, 3, h, 64] go through shared memory (the
+    // dS^T and staging buffers, free since the last T2): rows of 68 floats (a 16-byte rotation per
+    // row keeps both passes conflict-free), stored as whole rows at the end.
+    constexpr int LDS = 68;
+    float* sv = reinterpret_cast<float*>(dSp);
+    float* sk = sv + KB * LDS;
+    static_assert(2 * KB * LDS * 4 <= 3 * PART_K + 2 * QT * 64 * 4, "dV, dK rows fit");
+    if (!mma_warp) {
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
-        reinterpret_cast<float4*>(base + 2 * a.H * 64)[c4] =
+        reinterpret_cast<float4*>(sv + row * LDS + 16 * cg)[c4] =
             make_float4(dv[4 * c4], dv[4 * c4 + 1], dv[4 * c4 + 2], dv[4 * c4 + 3]);
-        reinterpret_cast<float4*>(base + a.H * 64)[c4] =
+        reinterpret_cast<float4*>(sk + row * LDS + 16 * cg)[c4] =
             make_float4(dk[4 * c4] * a.scale, dk[4 * c4 + 1] * a.scale, dk[4 * c4 + 2] * a.scale,
                         dk[4 * c4 + 3] * a.scale);
       }
     }
+    if (tid == 0) s_int[0] = atom_add_acq_rel(a.turn + bh, 1);
+    __syncthreads();
     if (s_int[0] == nkb - 1) {
-      __threadfence();
       const float* part = a.dq_part + static_cast<int64_t>(bh) * nkb * S * 64;
       const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * 64;
       float* dq_base = a.dqkv + static_cast<int64_t>(b) * S * row_stride + h * 64;
       // DETERMINISM: dQ = (((p0 + p1) + p2) + ...) * scale over the key blocks holding a key <=
-      // the row (causal) or all of them. Four float4 items per thread at a time, each key
-      // block's loads for the four issued together.
-      constexpr int U = 4;
+      // the row (causal) or all of them. Eight float4 items per thread at a time, each key
+      // block's loads for the eight issued together.
+      constexpr int U = 8;
       const int items = S * 16;
       for (int base = tid; base < items; base += U * NB) {
         float4 v[U];
@@ -548,6 +550,19 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
         }
       }
     }
+    // dV, dK rows out of shared memory: every 16 threads store one whole row.
+    {
+      const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * 64;
+      for (int f = tid; f < 2 * KB * 16; f += NB) {
+        const int which = f / (KB * 16), r = (f >> 4) & (KB - 1), c4 = f & 15;
+        if (k0 + r < S) {
+          float* dst = a.dqkv + (static_cast<int64_t>(b) * S + k0 + r) * row_stride +
+                       (2 - which) * a.H * 64 + h * 64;
+          reinterpret_cast<float4*>(dst)[c4] =
+              reinterpret_cast<const float4*>((which ? sk : sv) + r * LDS)[c4];
+        }
+      }
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -568,6 +583,12 @@ cudaError_t setup_bwd_tc_attributes() {
 cudaError_t launch_bwd_tc(const BwdArgs& args, int causal, cudaStream_t stream) {
   BwdArgs a = args;
   a.n_kblocks = (a.S + KB - 1) / KB;
+  int dev = 0, sms = 0;  // one block per SM: a wave is the SM count
+  if (cudaGetDevice(&dev) == cudaSuccess &&
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+    a.wave_ctas = sms;
+  else
+    a.wave_ctas = 0;
   const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(a.n_kblocks) * a.B * a.H));
   if (causal) return launch_pdl(bwd_tc_kernel<true>, grid, dim3(NB), SMEM_ALLOC, stream, a);
   return launch_pdl(bwd_tc_kernel<false>, grid, dim3(NB), SMEM_ALLOC, stream, a);

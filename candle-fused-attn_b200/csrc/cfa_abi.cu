@@ -176,7 +176,7 @@ int bwd_impl(const float* q, const int64_t q_strides[3], const float* k,
                       : cfa::launch_hd_bwd_prep(p, static_cast<int>(head_dim), s);
   if (e != cudaSuccess) return CFA_ERR_LAUNCH;
 
-  BwdArgs a;
+  BwdArgs a{};
   a.q = q;
   a.k = k;
   a.v = v;

@@ -68,6 +68,7 @@ struct BwdArgs {
   float scale;
   int n_qtiles;  // ceil(S / BWD_BM)
   int n_kblocks; // ceil(S / BWD_BN)
+  int wave_ctas;  // tensor-core backward: blocks resident at once (one per SM); 0: none
   uint64_t timeout_ns;
 };
 

@@ -145,6 +145,28 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
       : "memory");
 }
 
+// One arrival on `bar` that also expects `bytes` more transaction bytes in the current phase (the
+// bulk copies below complete them).
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}\n" ::"r"(
+          smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+// Bulk asynchronous copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global
+// memory into this block's shared memory, completing as transaction bytes on `bar`. One
+// instruction per row instead of a copy per 16 bytes: the copy engine keeps the row in flight.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }

@@ -19,25 +19,36 @@
 //
 // Block: 16 softmax warps and one MMA warp own TC_BM = 128 queries of one (batch, head). Softmax
 // thread (warp w < 16, lane l) owns query row 32 (w % 4) + l -- its TMEM lane -- and the 16
-// columns (keys of S, dims of O) of group w / 4; warp 16 issues every MMA. Per key tile of 64 the
-// softmax threads read S from TMEM, run the online softmax (row max of the four column groups
-// through shared memory), split P into shared memory and split their items of V (transposed: the
-// P V product reads V^T K-major) and K; the MMA warp then issues P V(n) and S(n + 2). S is issued
-// two tiles ahead (two S buffers in TMEM, two K part buffers) and P V(n - 1) is folded into the
-// fp32 O registers one tile late, so the tensor core works while the softmax runs. Every thread
-// copies (cp.async) the fp32 chunks it splits itself, a tile ahead of use.
+// columns (keys of S, dims of O) of group w / 4; warp 16 issues every MMA. The A operands live in
+// TMEM -- Q's parts (stored once) for S = Q K^T, P's parts for O = P V -- so an MMA reads only its
+// B operand (2 KB) from shared memory and runs at the tensor rate (with both operands in shared
+// memory, 6 KB per M128 N64 K16 MMA at 128 B per clock made it 1.5x slower). Per key tile of 64
+// the softmax threads read S from TMEM, run the online softmax (row max of the four column groups
+// through shared memory), put P's parts into TMEM and split their items of V (transposed: the P V
+// product reads V's rows as an MN-major B operand) and K into shared memory; the MMA warp then issues P V(n) and
+// S(n + 2). S is issued two tiles ahead (two S buffers in TMEM, two K part buffers) and P V(n - 1)
+// is folded into the fp32 O registers one tile late, so the tensor core works while the softmax
+// runs. Every thread copies (cp.async) the fp32 chunks it splits itself, a tile ahead of use.
 //
 // Every mbarrier wait is bounded (WAIT_TIMEOUT_NS); on expiry the block sets the device error flag
 // (cfa_fwd_status reads it), waits once more, frees its TMEM and returns without writing.
 //
-// DETERMINISM: the MMA order is fixed by the code; every register sum has one order: the row max over each group's 16 keys in order, then the groups 0..3; p summed over the
-// group's keys in order, per tile; l = ((l0 + l1) + l2) + l3; O over key tiles in index order.
+// DETERMINISM: the MMA order is fixed by the code; every register sum has one order: the row
+// max over each group's 16 keys in order, then the groups 0..3; p summed over the group's keys in
+// order, per tile; l = ((l0 + l1) + l2) + l3; O over key tiles in index order.
 #include <cuda_bf16.h>
 
 #include "cfa_common.cuh"
+#include "cfa_split.cuh"
 #include "cfa_tc.cuh"
 
 namespace cfa {
+using tc::kmaj_off;
+using tc::split16;
+using tc::split8;
+using tc::store_parts;
+using tc::tmem_ld8;
+using tc::tmem_st8;
 
 __device__ int g_fwd_tc_err = 0;
 
@@ -49,69 +60,27 @@ constexpr int TC_THREADS = 512;  // the softmax / split threads; one more warp i
 constexpr int TC_BLOCK = TC_THREADS + 32;
 constexpr int NQ = TC_THREADS / 128;  // threads per query row
 constexpr int CW = 64 / NQ;           // columns (keys of S, dims of O) per thread
-constexpr int PART_Q = TC_BM * 64 * 2;  // bytes of one bf16 part of a [128][64] operand
 constexpr int PART_K = TC_BN * 64 * 2;  // bytes of one bf16 part of a [64][64] operand
 constexpr int TILE_F32 = TC_BN * 64 * 4;  // bytes of one fp32 [64][64] tile
-constexpr int OFF_Q = 0;                       // Q parts, [128 rows][64 d], K-major
-constexpr int OFF_K = OFF_Q + 3 * PART_Q;      // two buffers of K parts, [64 keys][64 d]
-constexpr int OFF_V = OFF_K + 6 * PART_K;      // V^T parts, [64 d][64 keys], K-major
-constexpr int OFF_P = OFF_V + 3 * PART_K;      // P parts, [128 rows][64 keys] (first: Q in fp32)
-constexpr int OFF_KST = OFF_P + 3 * PART_Q;    // fp32 K tile in flight, [64][64]
+constexpr int OFF_K = 0;                       // two buffers of K parts, [64 keys][64 d]
+constexpr int OFF_V = OFF_K + 6 * PART_K;      // V parts, [64 keys][64 d], rows as K's
+constexpr int OFF_KST = OFF_V + 3 * PART_K;    // fp32 K tile in flight, [64][64]
 constexpr int OFF_VST = OFF_KST + TILE_F32;    // fp32 V tile in flight, [64][64]
-constexpr int OFF_RED = OFF_VST + TILE_F32;    // float [128][NQ]: the row max per column group, then l
+constexpr int OFF_K1ST = OFF_VST + TILE_F32;   // prologue: fp32 K(1)
+constexpr int OFF_RED = OFF_K1ST + TILE_F32;   // float [128][NQ]: the row max per column group, then l
 constexpr int OFF_BAR = OFF_RED + TC_BM * NQ * 4;  // mbarriers S0, S1, O and the TMEM base
 constexpr int TC_SMEM = OFF_BAR + 32;
 constexpr int TC_SMEM_ALLOC = TC_SMEM + 1024;  // room to align the base to 1024 bytes
-// TMEM columns: S of two key tiles (0-63, 64-127), O (128-191); one block per SM.
-constexpr uint32_t TMEM_COLS = 256;
-
-// Byte offset of the 16-byte core-matrix row holding elements (row, 8 kc .. 8 kc + 7) of a
-// K-major bf16 operand with 64 elements per row: core matrices of 8 rows x 16 bytes, K-adjacent
-// core matrices 128 bytes apart, row groups of 8 rows 1024 bytes apart (the layout of
-// tc::desc_kmajor with LBO 128, SBO 1024).
-__device__ __forceinline__ uint32_t kmaj_off(int row, int kc) {
-  return static_cast<uint32_t>((((row >> 3) * 8 + kc) << 7) + ((row & 7) << 4));
-}
-
-__device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) {
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
-// x[0..7] -> three 16-byte rows of bf16 parts: x = p0 + p1 + p2 (+ below 2^-24 relative).
-__device__ __forceinline__ void split8(const float (&x)[8], uint4& p0, uint4& p1, uint4& p2) {
-  uint32_t a[4], b[4], c[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float x0 = x[2 * i], x1 = x[2 * i + 1];
-    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-    const float2 hf = __bfloat1622float2(h);
-    const float r0 = x0 - hf.x, r1 = x1 - hf.y;  // exact
-    const __nv_bfloat162 m = __floats2bfloat162_rn(r0, r1);
-    const float2 mf = __bfloat1622float2(m);
-    const __nv_bfloat162 l = __floats2bfloat162_rn(r0 - mf.x, r1 - mf.y);  // exact differences
-    a[i] = bf2_bits(h);
-    b[i] = bf2_bits(m);
-    c[i] = bf2_bits(l);
-  }
-  p0 = make_uint4(a[0], a[1], a[2], a[3]);
-  p1 = make_uint4(b[0], b[1], b[2], b[3]);
-  p2 = make_uint4(c[0], c[1], c[2], c[3]);
-}
-
-__device__ __forceinline__ void store_parts(unsigned char* base, int part_bytes, uint32_t off,
-                                            const float (&x)[8]) {
-  uint4 p0, p1, p2;
-  split8(x, p0, p1, p2);
-  *reinterpret_cast<uint4*>(base + off) = p0;
-  *reinterpret_cast<uint4*>(base + part_bytes + off) = p1;
-  *reinterpret_cast<uint4*>(base + 2 * part_bytes + off) = p2;
-}
+// TMEM columns (lane = query row). Q's parts, the A operand of S: part i, K-step ks (16 dims) in
+// the 8 columns T_Q + 32 i + 8 ks. S of two key tiles (T_S, T_S + 64). O. P's parts, the A operand
+// of P V: part i, K-step ks (16 keys) at T_P + 32 i + 8 ks. One block per SM.
+constexpr uint32_t T_Q = 0, T_S = 96, T_O = 224, T_P = 288;
+constexpr uint32_t TMEM_COLS = 512;
 
 // Staging. Every thread copies (cp.async) exactly the fp32 chunks it later splits, into slots of
 // its own, so no barrier separates a copy from its split: a row item (r, kc) -- row r, elements
-// 8 kc .. 8 kc + 7 of Q or K -- as two 16-byte copies, a V^T item (d, g) -- V[8 g .. 8 g + 7][d] --
-// as eight 4-byte copies. Slot j of thread t sits at (j * TC_THREADS + t) * width: a warp's
-// copies and reads of one slot are consecutive.
+// 8 kc .. 8 kc + 7 of K or V -- as two 16-byte copies. Slot j of thread t sits at
+// (j * TC_THREADS + t) * 16 bytes: a warp's copies and reads of one slot are consecutive.
 // Row items: item c takes row 8 (c / 64) + c % 8 and chunk (c / 8) % 8, so a quarter-warp's parts
 // land in 8 different bank groups of the core-matrix layout and a warp reads 4 x 32 bytes of each
 // of 8 rows.
@@ -142,49 +111,33 @@ __device__ __forceinline__ void split_row_item(unsigned char* parts, int part_by
   store_parts(parts, part_bytes, kmaj_off(r, kc), x);
 }
 
-// Copy V^T item (d, g) = (tid % 64, tid / 64) of the key tile from k0: 8 column elements.
-__device__ __forceinline__ void stage_vt_item(unsigned char* st, const float* src, int64_t stride,
-                                              int k0, int seq) {
-  const int d = threadIdx.x & 63, g = threadIdx.x >> 6;
-#pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    const int j = k0 + 8 * g + u;
-    const bool ok = j < seq;
-    cp_async4(st + 4 * (u * TC_THREADS + threadIdx.x),
-              src + static_cast<int64_t>(ok ? j : 0) * stride + d, ok ? 4 : 0);
-  }
-}
-
-__device__ __forceinline__ void split_vt_item(unsigned char* parts, const unsigned char* st) {
-  const int d = threadIdx.x & 63, g = threadIdx.x >> 6;
-  float x[8];
-#pragma unroll
-  for (int u = 0; u < 8; ++u)
-    x[u] = *reinterpret_cast<const float*>(st + 4 * (u * TC_THREADS + threadIdx.x));
-  store_parts(parts, PART_K, kmaj_off(d, g), x);
-}
-
-// The six (A part, B part) products of K = 64 (four K-steps of 16 bf16) into one accumulator `d`:
+// The six (A part, B part) products of K = 64 (four K-steps of 16 bf16) into one accumulator `d`,
+// A in TMEM (part i, K-step ks at column a_tmem + 32 i + 8 ks), B in shared memory from b_base:
 // the small pairs (0, 1), (1, 0), (0, 2), (1, 1), (2, 0) of every step, then the (0, 0) of every
-// step. A descriptor's start-address field holds the byte address / 16 (shared memory < 256 KB: no
-// carry out of its 14 bits), so the descriptor of base + off is the base's plus off / 16.
-template <int A_PART, int B_PART>
-__device__ __forceinline__ void issue_split_mma(uint32_t d, uint32_t a_base, uint32_t b_base,
+// step. With A in TMEM an MMA reads only B's 2 KB from shared memory, so it runs at the tensor
+// rate. Called by the whole MMA warp (one elected lane issues).
+// B is K's parts read K-major (S = Q K^T: K-steps 256 bytes apart) or, B_MN, V's parts -- the same
+// row layout -- read MN-major (O = P V, N = d: K-steps of 16 keys 2048 bytes apart).
+template <bool B_MN>
+__device__ __forceinline__ void issue_split_mma(uint32_t d, uint32_t a_tmem, uint32_t b_base,
                                                 uint32_t idesc) {
   constexpr int PA[6] = {0, 0, 1, 0, 1, 2};
   constexpr int PB[6] = {0, 1, 0, 2, 1, 0};
-  const tc::Desc ad = tc::split_desc(tc::desc_kmajor(a_base, 128, 1024));
-  const tc::Desc bd = tc::split_desc(tc::desc_kmajor(b_base, 128, 1024));
-  const uint32_t alo = tc::opaque(ad.lo), blo = tc::opaque(bd.lo);
+  constexpr int STEP = B_MN ? 2048 : 256;
+  const tc::Desc bd = tc::split_desc(B_MN ? tc::desc_kmajor(b_base, 1024, 128)
+                                          : tc::desc_kmajor(b_base, 128, 1024));
+  const uint32_t id = B_MN ? idesc | (1u << 16) : idesc;
+  const uint32_t blo = tc::opaque(bd.lo);
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks)
 #pragma unroll
     for (int p = 1; p < 6; ++p)
-      tc::mma_bf16_warp(d, alo + ((PA[p] * A_PART + 256 * ks) >> 4), ad.hi,
-                        blo + ((PB[p] * B_PART + 256 * ks) >> 4), bd.hi, idesc, ks > 0 || p > 1);
+      tc::mma_bf16_tmem_a_warp(d, a_tmem + 32 * PA[p] + 8 * ks,
+                               blo + ((PB[p] * PART_K + STEP * ks) >> 4), bd.hi, id,
+                               ks > 0 || p > 1);
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks)
-    tc::mma_bf16_warp(d, alo + ((256 * ks) >> 4), ad.hi, blo + ((256 * ks) >> 4), bd.hi, idesc, 1);
+    tc::mma_bf16_tmem_a_warp(d, a_tmem + 8 * ks, blo + ((STEP * ks) >> 4), bd.hi, id, 1);
 }
 
 // Named barriers: 1 = the softmax threads (TC_THREADS), 2 = those plus the MMA warp (TC_BLOCK).
@@ -206,9 +159,7 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = tc::smem_u32(smem_raw);
   unsigned char* sm = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-  unsigned char* Qp = sm + OFF_Q;
   unsigned char* Vp = sm + OFF_V;
-  unsigned char* Pp = sm + OFF_P;
   unsigned char* Kst = sm + OFF_KST;
   unsigned char* Vst = sm + OFF_VST;
   float* red = reinterpret_cast<float*>(sm + OFF_RED);
@@ -258,21 +209,29 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
   // (c) p into P's parts; barrier; (d) issue P V(n) and S(n + 2); (e) stage V(n + 1), K(n + 3).
   static_assert(TC_BM * 8 == 2 * TC_THREADS && TC_BN * 8 == TC_THREADS, "items per thread");
   const bool mma_warp = w == TC_THREADS / 32;  // warp 16: issues every MMA, nothing else
-  // Prologue: Q (staged in the P buffer's first two slots), K(0), K(1) (its third slot) split;
-  // S(0), S(1) issued; K(2), V(0) in flight.
+  // Prologue: K(0), K(1) split; Q (this thread's row and 16 dims: K-step cq of S's A operand)
+  // into TMEM; S(0), S(1) issued; K(2), V(0) in flight.
+  float qx[CW];
   if (!mma_warp) {
-    stage_row_item(Pp, 0, tid, qp, a.q_ss, q0, S);
-    stage_row_item(Pp, 1, tid + TC_THREADS, qp, a.q_ss, q0, S);
     stage_row_item(Kst, 0, tid, kp, a.k_ss, 0, S);
-    if (T > 1) stage_row_item(Pp, 2, tid, kp, a.k_ss, TC_BN, S);
+    if (T > 1) stage_row_item(sm + OFF_K1ST, 0, tid, kp, a.k_ss, TC_BN, S);
     cp_async_commit();
+    const bool ok = q0 + row < S;
+    const float4* qr =
+        reinterpret_cast<const float4*>(qp + static_cast<int64_t>(ok ? q0 + row : 0) * a.q_ss + CW * cq);
+#pragma unroll
+    for (int c4 = 0; c4 < CW / 4; ++c4) {
+      const float4 u = ok ? qr[c4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      qx[4 * c4] = u.x;
+      qx[4 * c4 + 1] = u.y;
+      qx[4 * c4 + 2] = u.z;
+      qx[4 * c4 + 3] = u.w;
+    }
     cp_async_wait_all();
-    split_row_item(Qp, PART_Q, Pp, 0, tid);
-    split_row_item(Qp, PART_Q, Pp, 1, tid + TC_THREADS);
     split_row_item(sm + OFF_K, PART_K, Kst, 0, tid);
-    if (T > 1) split_row_item(sm + OFF_K + 3 * PART_K, PART_K, Pp, 2, tid);
+    if (T > 1) split_row_item(sm + OFF_K + 3 * PART_K, PART_K, sm + OFF_K1ST, 0, tid);
     if (T > 2) stage_row_item(Kst, 0, tid, kp, a.k_ss, 2 * TC_BN, S);
-    stage_vt_item(Vst, vp, a.v_ss, 0, S);
+    stage_row_item(Vst, 0, tid, vp, a.v_ss, 0, S);
     cp_async_commit();
     tc::fence_async_smem();
   }
@@ -281,29 +240,38 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
   tc::fence_after_sync();
   const uint32_t tbase = *tbase_p;
   const uint32_t lane_sel = static_cast<uint32_t>(32 * (w & 3)) << 16;
-  const uint32_t t_o = tbase + 128;
+  const uint32_t t_o = tbase + T_O;
+  if (!mma_warp) {
+    uint32_t qparts[3][8];
+    split16(qx, qparts);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) tmem_st8(tbase + lane_sel + T_Q + 32 * i + 8 * cq, qparts[i]);
+    tc::tmem_wait_st();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
   bool err = false;
 
   if (mma_warp) {
     // S(0), S(1); then per tile, once its P, V and K(n + 2) parts are in place: P V(n), S(n + 2).
     const uint32_t idesc = tc::idesc_f32acc(1, TC_BM, TC_BN);
-    const uint32_t sQ = tc::smem_u32(Qp), sV = tc::smem_u32(Vp), sP = tc::smem_u32(Pp);
-    const uint32_t sK0 = tc::smem_u32(sm + OFF_K);
+    const uint32_t sV = tc::smem_u32(Vp), sK0 = tc::smem_u32(sm + OFF_K);
     // The whole warp runs the issue code (warp-uniform operands); one elected lane issues.
-    issue_split_mma<PART_Q, PART_K>(tbase, sQ, sK0, idesc);
+    issue_split_mma<false>(tbase + T_S, tbase + T_Q, sK0, idesc);
     tc::commit_warp(bar_s);
     if (T > 1) {
-      issue_split_mma<PART_Q, PART_K>(tbase + 64, sQ, sK0 + 3 * PART_K, idesc);
+      issue_split_mma<false>(tbase + T_S + 64, tbase + T_Q, sK0 + 3 * PART_K, idesc);
       tc::commit_warp(bar_s + 1);
     }
     for (int n = 0; n < T; ++n) {
       bar_sync(2, TC_BLOCK);
       tc::fence_after_sync();
       const int j = n & 1;
-      issue_split_mma<PART_Q, PART_K>(t_o, sP, sV, idesc);
+      issue_split_mma<true>(t_o, tbase + T_P, sV, idesc);
       tc::commit_warp(bar_o);
       if (n + 2 < T) {
-        issue_split_mma<PART_Q, PART_K>(tbase + 64 * j, sQ, sK0 + 3 * PART_K * j, idesc);
+        issue_split_mma<false>(tbase + T_S + 64 * j, tbase + T_Q, sK0 + 3 * PART_K * j, idesc);
         tc::commit_warp(bar_s + j);
       }
     }
@@ -324,7 +292,7 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
     // (a) S(n) from TMEM; the online softmax.
     err |= !tc::mbar_wait(bar_s + j, (n >> 1) & 1, WAIT_TIMEOUT_NS);
     tc::fence_after_sync();
-    tmem_ld1(tbase + 64 * j + lane_sel + CW * cq, sv);
+    tmem_ld1(tbase + T_S + 64 * j + lane_sel + CW * cq, sv);
     const bool edge = (k0 + TC_BN > S) || (CAUSAL && k0 + TC_BN - 1 > q0);
     float tmax = -INFINITY;
 #pragma unroll
@@ -363,22 +331,23 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
 #pragma unroll
       for (int c = 0; c < CW; ++c) acc[c] = fmaf(acc[c], alpha_prev, ob[c]);
     }
-    split_vt_item(Vp, Vst);
+    split_row_item(Vp, PART_K, Vst, 0, tid);
     if (n + 2 < T) split_row_item(sm + OFF_K + 3 * PART_K * j, PART_K, Kst, 0, tid);
-    // (c) p into P's parts; hand the tile to the MMA warp.
+    // (c) p into P's parts in TMEM (K-step cq of P V's A operand; P V(n - 1) has read the last
+    // ones); hand the tile to the MMA warp.
+    {
+      uint32_t pparts[3][8];
+      split16(sv, pparts);
 #pragma unroll
-    for (int c8 = 0; c8 < CW / 8; ++c8) {
-      float x[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) x[u] = sv[8 * c8 + u];
-      store_parts(Pp, PART_Q, kmaj_off(row, (CW / 8) * cq + c8), x);
+      for (int i = 0; i < 3; ++i) tmem_st8(tbase + lane_sel + T_P + 32 * i + 8 * cq, pparts[i]);
+      tc::tmem_wait_st();
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
     bar_sync(2, TC_BLOCK);
     tc::fence_after_sync();
     // (e) Refill this thread's staging slots.
-    if (n + 1 < T) stage_vt_item(Vst, vp, a.v_ss, (n + 1) * TC_BN, S);
+    if (n + 1 < T) stage_row_item(Vst, 0, tid, vp, a.v_ss, (n + 1) * TC_BN, S);
     if (n + 3 < T) stage_row_item(Kst, 0, tid, kp, a.k_ss, (n + 3) * TC_BN, S);
     cp_async_commit();
     alpha_prev = alpha;
