@@ -91,7 +91,7 @@ int fwd_impl(const float* q, const int64_t q_strides[3], const float* k,
              : setup(g_hd_once, cfa::setup_hd_attributes);
   if (st != CFA_OK) return st;
 
-  FwdArgs a;
+  FwdArgs a{};
   a.q = q;
   a.k = k;
   a.v = v;

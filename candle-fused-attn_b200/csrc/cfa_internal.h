@@ -46,6 +46,7 @@ struct FwdArgs {
   int B, H, S;
   float scale;
   int n_qtiles;
+  int wave_ctas;  // tensor-core forward: blocks resident at once (one per SM); 0: none
 };
 
 struct BwdArgs {

@@ -66,10 +66,11 @@ constexpr int OFF_K = 0;                       // two buffers of K parts, [64 ke
 constexpr int OFF_V = OFF_K + 6 * PART_K;      // V parts, [64 keys][64 d], rows as K's
 constexpr int OFF_KST = OFF_V + 3 * PART_K;    // fp32 K tile in flight, [64][64]
 constexpr int OFF_VST = OFF_KST + TILE_F32;    // fp32 V tile in flight, [64][64]
-constexpr int OFF_K1ST = OFF_VST + TILE_F32;   // prologue: fp32 K(1)
-constexpr int OFF_RED = OFF_K1ST + TILE_F32;   // float [128][NQ]: the row max per column group, then l
-constexpr int OFF_BAR = OFF_RED + TC_BM * NQ * 4;  // mbarriers S0, S1, O and the TMEM base
-constexpr int TC_SMEM = OFF_BAR + 32;
+constexpr int LDP = 68;                        // prologue staging: rows of 64 floats, 68 apart
+constexpr int OFF_ROWS = OFF_VST + TILE_F32;   // prologue: fp32 rows of Q, K(0), K(1)
+constexpr int OFF_RED = OFF_ROWS + (TC_BM + 2 * TC_BN) * LDP * 4;  // float [128][NQ]: row max, l
+constexpr int OFF_BAR = OFF_RED + TC_BM * NQ * 4;  // mbarriers S0, S1, O, rows; the TMEM base
+constexpr int TC_SMEM = OFF_BAR + 40;
 constexpr int TC_SMEM_ALLOC = TC_SMEM + 1024;  // room to align the base to 1024 bytes
 // TMEM columns (lane = query row). Q's parts, the A operand of S: part i, K-step ks (16 dims) in
 // the 8 columns T_Q + 32 i + 8 ks. S of two key tiles (T_S, T_S + 64). O. P's parts, the A operand
@@ -87,6 +88,24 @@ constexpr uint32_t TMEM_COLS = 512;
 __device__ __forceinline__ void row_item(int c, int& r, int& kc) {
   r = 8 * (c >> 6) + (c & 7);
   kc = (c >> 3) & 7;
+}
+
+// Row item c of the prologue's row-major staging (rows LDP floats apart; rows >= valid read as
+// zeros) into K-major parts.
+__device__ __forceinline__ void split_staged_row(unsigned char* parts, const float* rows, int c,
+                                                 int valid) {
+  int r, kc;
+  row_item(c, r, kc);
+  float x[8];
+  if (r < valid) {
+    const float4 u = reinterpret_cast<const float4*>(rows + r * LDP + 8 * kc)[0];
+    const float4 v = reinterpret_cast<const float4*>(rows + r * LDP + 8 * kc)[1];
+    x[0] = u.x, x[1] = u.y, x[2] = u.z, x[3] = u.w, x[4] = v.x, x[5] = v.y, x[6] = v.z, x[7] = v.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = 0.0f;
+  }
+  store_parts(parts, PART_K, kmaj_off(r, kc), x);
 }
 
 // Copy row item c (slot base `slot`, two 16-byte slots) of a strided operand, rows from r0.
@@ -165,7 +184,8 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
   float* red = reinterpret_cast<float*>(sm + OFF_RED);
   uint64_t* bar_s = reinterpret_cast<uint64_t*>(sm + OFF_BAR);  // [2]
   uint64_t* bar_o = bar_s + 2;
-  uint32_t* tbase_p = reinterpret_cast<uint32_t*>(bar_s + 3);
+  uint64_t* bar_ld = bar_s + 3;  // the prologue's bulk row copies
+  uint32_t* tbase_p = reinterpret_cast<uint32_t*>(bar_s + 4);
 
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
   const int row = 32 * (w & 3) + lane;  // TMEM lane
@@ -187,12 +207,16 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
   const float* vp = a.v + b * a.v_sb + h * a.v_sh;
   const int k_end = CAUSAL ? min(S, q0 + TC_BM) : S;
   const int T = (k_end + TC_BN - 1) / TC_BN;  // key tiles, >= 1
+  bool err0 = false;
 
   if (tid == 0) {
     tc::mbar_init(bar_s, 1);
     tc::mbar_init(bar_s + 1, 1);
     tc::mbar_init(bar_o, 1);
+    tc::mbar_init(bar_ld, 1);
     tc::fence_mbar_init();
+    tc::mbar_arrive_expect_tx(bar_ld, 256u * (min(TC_BM, S - q0) + min(TC_BN, S) +
+                                              (T > 1 ? min(TC_BN, S - TC_BN) : 0)));
   }
   if (w == 0) {
     tc::tmem_alloc(tbase_p, TMEM_COLS);
@@ -209,30 +233,39 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
   // (c) p into P's parts; barrier; (d) issue P V(n) and S(n + 2); (e) stage V(n + 1), K(n + 3).
   static_assert(TC_BM * 8 == 2 * TC_THREADS && TC_BN * 8 == TC_THREADS, "items per thread");
   const bool mma_warp = w == TC_THREADS / 32;  // warp 16: issues every MMA, nothing else
-  // Prologue: K(0), K(1) split; Q (this thread's row and 16 dims: K-step cq of S's A operand)
-  // into TMEM; S(0), S(1) issued; K(2), V(0) in flight.
+  // Prologue: the rows of Q, K(0), K(1) travel as one bulk copy each (threads 0-255, one row
+  // apiece) into row-major staging (rows past the sequence are not copied and read as zeros);
+  // K(0), K(1) split into their parts; Q (this thread's row and 16 dims: K-step cq of S's A
+  // operand) into TMEM; S(0), S(1) issued; K(2), V(0) in flight.
+  float* q_rows = reinterpret_cast<float*>(sm + OFF_ROWS);
+  float* k_rows = q_rows + TC_BM * LDP;
+  const int nq = min(TC_BM, S - q0), nk0 = min(TC_BN, S), nk1 = T > 1 ? min(TC_BN, S - TC_BN) : 0;
+  __syncthreads();  // the mbarriers' initialisation
   float qx[CW];
   if (!mma_warp) {
-    stage_row_item(Kst, 0, tid, kp, a.k_ss, 0, S);
-    if (T > 1) stage_row_item(sm + OFF_K1ST, 0, tid, kp, a.k_ss, TC_BN, S);
+    if (tid < TC_BM) {
+      if (tid < nq)
+        tc::bulk_load(q_rows + tid * LDP, qp + static_cast<int64_t>(q0 + tid) * a.q_ss, 256, bar_ld);
+    } else if (tid < TC_BM + 2 * TC_BN) {
+      const int r = tid - TC_BM;  // key row 0 .. 127 of K(0), K(1)
+      if (r < (r < TC_BN ? nk0 : TC_BN + nk1))
+        tc::bulk_load(k_rows + r * LDP, kp + static_cast<int64_t>(r) * a.k_ss, 256, bar_ld);
+    }
+    if (T > 2) stage_row_item(Kst, 0, tid, kp, a.k_ss, 2 * TC_BN, S);
+    stage_row_item(Vst, 0, tid, vp, a.v_ss, 0, S);
     cp_async_commit();
-    const bool ok = q0 + row < S;
-    const float4* qr =
-        reinterpret_cast<const float4*>(qp + static_cast<int64_t>(ok ? q0 + row : 0) * a.q_ss + CW * cq);
+    err0 = !tc::mbar_wait(bar_ld, 0, WAIT_TIMEOUT_NS);
+    split_staged_row(sm + OFF_K, k_rows, tid, nk0);
+    if (T > 1) split_staged_row(sm + OFF_K + 3 * PART_K, k_rows + TC_BN * LDP, tid, nk1);
 #pragma unroll
     for (int c4 = 0; c4 < CW / 4; ++c4) {
-      const float4 u = ok ? qr[c4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 u = row < nq ? reinterpret_cast<const float4*>(q_rows + row * LDP + CW * cq)[c4]
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
       qx[4 * c4] = u.x;
       qx[4 * c4 + 1] = u.y;
       qx[4 * c4 + 2] = u.z;
       qx[4 * c4 + 3] = u.w;
     }
-    cp_async_wait_all();
-    split_row_item(sm + OFF_K, PART_K, Kst, 0, tid);
-    if (T > 1) split_row_item(sm + OFF_K + 3 * PART_K, PART_K, sm + OFF_K1ST, 0, tid);
-    if (T > 2) stage_row_item(Kst, 0, tid, kp, a.k_ss, 2 * TC_BN, S);
-    stage_row_item(Vst, 0, tid, vp, a.v_ss, 0, S);
-    cp_async_commit();
     tc::fence_async_smem();
   }
   tc::fence_before_sync();
@@ -251,7 +284,7 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  bool err = false;
+  bool err = err0;
 
   if (mma_warp) {
     // S(0), S(1); then per tile, once its P, V and K(n + 2) parts are in place: P V(n), S(n + 2).
@@ -276,6 +309,36 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
       }
     }
   }
+
+  // The block one wave later (blockIdx + a.wave_ctas) starts by reading its 128 Q rows and the
+  // first 128 K rows and 64 V rows of its (batch, head), all at once across the wave: pull them
+  // into L2 while this wave computes (one 256-byte row per thread).
+  auto prefetch_next_wave = [&]() {
+    const int nb = static_cast<int>(blockIdx.x) + a.wave_ctas;
+    if (a.wave_ctas <= 0 || nb >= static_cast<int>(gridDim.x) || tid >= 2 * TC_BM + TC_BN) return;
+    int nqt, nbh;
+    if (CAUSAL) {
+      nqt = a.n_qtiles - 1 - nb / BH;
+      nbh = nb % BH;
+    } else {
+      nqt = nb % a.n_qtiles;
+      nbh = nb / a.n_qtiles;
+    }
+    const int nb_b = nbh / a.H, nb_h = nbh % a.H;
+    const float* src;
+    int r;
+    if (tid < TC_BM) {
+      r = nqt * TC_BM + tid;
+      src = a.q + nb_b * a.q_sb + nb_h * a.q_sh + static_cast<int64_t>(r) * a.q_ss;
+    } else if (tid < 2 * TC_BM) {
+      r = tid - TC_BM;
+      src = a.k + nb_b * a.k_sb + nb_h * a.k_sh + static_cast<int64_t>(r) * a.k_ss;
+    } else {
+      r = tid - 2 * TC_BM;
+      src = a.v + nb_b * a.v_sb + nb_h * a.v_sh + static_cast<int64_t>(r) * a.v_ss;
+    }
+    if (r < S) asm volatile("cp.async.bulk.prefetch.L2.global [%0], 256;" ::"l"(src) : "memory");
+  };
 
   // Online-softmax state of this thread's columns: acc holds O[row][CW cq + c] (unnormalised).
   float m = -INFINITY, lpart = 0.0f, alpha_prev = 1.0f;
@@ -346,6 +409,7 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
     tc::fence_before_sync();
     bar_sync(2, TC_BLOCK);
     tc::fence_after_sync();
+    if (n == 0) prefetch_next_wave();
     // (e) Refill this thread's staging slots.
     if (n + 1 < T) stage_row_item(Vst, 0, tid, vp, a.v_ss, (n + 1) * TC_BN, S);
     if (n + 3 < T) stage_row_item(Kst, 0, tid, kp, a.k_ss, (n + 3) * TC_BN, S);
@@ -368,18 +432,29 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
     if (tid == 0) atomicExch(&g_fwd_tc_err, 1);
     tc::mbar_wait(bar_o, (T - 1) & 1, WAIT_TIMEOUT_NS);
     tc::mbar_wait(bar_s + ((T - 1) & 1), ((T - 1) >> 1) & 1, WAIT_TIMEOUT_NS);
-  } else if (!mma_warp) {
-    float l = red[NQ * row];
+  } else {
+    // O = acc / l through shared memory (the K and V part buffers: no MMA is left to read them),
+    // rows of LDP floats (a 16-byte rotation per row keeps both passes conflict-free); then every
+    // 16 threads store one whole row of O [b, s, h, 64].
+    float* o_rows = reinterpret_cast<float*>(sm + OFF_K);
+    static_assert(TC_BM * LDP * 4 <= 9 * PART_K, "O rows fit the part buffers");
+    if (!mma_warp) {
+      float l = red[NQ * row];
 #pragma unroll
-    for (int g = 1; g < NQ; ++g) l += red[NQ * row + g];
-    if (qi < S) {
-      float* dst = a.o + ((static_cast<int64_t>(b) * S + qi) * a.H + h) * 64 + CW * cq;
+      for (int g = 1; g < NQ; ++g) l += red[NQ * row + g];
 #pragma unroll
       for (int c4 = 0; c4 < CW / 4; ++c4)
-        reinterpret_cast<float4*>(dst)[c4] =
+        reinterpret_cast<float4*>(o_rows + row * LDP + CW * cq)[c4] =
             make_float4(__fdiv_rn(acc[4 * c4], l), __fdiv_rn(acc[4 * c4 + 1], l),
                         __fdiv_rn(acc[4 * c4 + 2], l), __fdiv_rn(acc[4 * c4 + 3], l));
-      if (cq == 0) a.lse[static_cast<int64_t>(bh) * S + qi] = m + logf(l);
+      if (cq == 0 && qi < S) a.lse[static_cast<int64_t>(bh) * S + qi] = m + logf(l);
+    }
+    __syncthreads();
+    for (int f = tid; f < TC_BM * 16; f += TC_BLOCK) {
+      const int r = f >> 4, c4 = f & 15;
+      if (q0 + r < S)
+        reinterpret_cast<float4*>(a.o + ((static_cast<int64_t>(b) * S + q0 + r) * a.H + h) * 64)[c4] =
+            reinterpret_cast<const float4*>(o_rows + r * LDP)[c4];
     }
   }
   tc::fence_before_sync();
@@ -403,6 +478,12 @@ cudaError_t setup_fwd_tc_attributes() {
 cudaError_t launch_fwd_tc(const FwdArgs& args, int causal, cudaStream_t stream) {
   FwdArgs a = args;
   a.n_qtiles = (a.S + TC_BM - 1) / TC_BM;
+  int dev = 0, sms = 0;  // one block per SM: a wave is the SM count
+  if (cudaGetDevice(&dev) == cudaSuccess &&
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+    a.wave_ctas = sms;
+  else
+    a.wave_ctas = 0;
   const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(a.n_qtiles) * a.B * a.H));
   if (causal)
     return launch_pdl(fwd_tc_kernel<true>, grid, dim3(TC_BLOCK), TC_SMEM_ALLOC, stream, a);
