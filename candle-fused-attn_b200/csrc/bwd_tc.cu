@@ -227,10 +227,6 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
     tc::fence_mbar_init();
     tc::mbar_arrive_expect_tx(bar_ld, 256u * (2 * min(KB, S - k0) + 2 * min(QT, S - t_begin * QT)));
   }
-  if (w == 0) {
-    tc::tmem_alloc(tbase_p, TMEM_COLS);
-    tc::tmem_relinquish();
-  }
   griddep_launch_dependents();
 
   // Q, dO of tile n into this thread's staging slots (Q: slots 0-1, dO: 2-3) and its L, D into
@@ -300,6 +296,11 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
       } else if (r < nq) {
         tc::bulk_load(o_rows + r * LDP, gp + static_cast<int64_t>(t_begin * QT + r) * a.do_ss, 256, bar_ld);
       }
+    }
+    if (w == 0) {  // TMEM while the rows travel
+      __syncwarp();
+      tc::tmem_alloc(tbase_p, TMEM_COLS);
+      tc::tmem_relinquish();
     }
     griddep_wait();  // L, D, the cleared counters: the prep kernel's writes
     stage_ld(0);
@@ -503,7 +504,34 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
     }
     if (tid == 0) s_int[0] = atom_add_acq_rel(a.turn + bh, 1);
     __syncthreads();
-    if (s_int[0] == nkb - 1) {
+    const int64_t part_bytes = static_cast<int64_t>(nkb) * S * 64 * 4;
+    if (s_int[0] == nkb - 1 && part_bytes <= OFF_DS) {
+      // The (b, h)'s partials, contiguous [nkb][S][64], as one bulk copy into shared memory (the
+      // part buffers, free since the last T2; the dS^T buffer holds dV, dK), then summed there.
+      const float* part = a.dq_part + static_cast<int64_t>(bh) * nkb * S * 64;
+      const float* sp = reinterpret_cast<const float*>(sm);
+      if (tid == 0) {
+        tc::fence_async_global();  // the partials the count made visible, for the copy engine
+        tc::mbar_arrive_expect_tx(bar_ld, static_cast<uint32_t>(part_bytes));
+        tc::bulk_load(sm, part, static_cast<uint32_t>(part_bytes), bar_ld);
+      }
+      const bool ok = tc::mbar_wait(bar_ld, 1, WAIT_TIMEOUT_NS);
+      const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * 64;
+      float* dq_base = a.dqkv + static_cast<int64_t>(b) * S * row_stride + h * 64;
+      // DETERMINISM: dQ = (((p0 + p1) + p2) + ...) * scale, as below.
+      for (int idx = tid; idx < S * 16 && ok; idx += NB) {
+        const int i = idx >> 4, c4 = idx & 15;
+        const int last = CAUSAL ? min(nkb - 1, i / KB) : nkb - 1;
+        float4 v = reinterpret_cast<const float4*>(sp + i * 64)[c4];
+        for (int j = 1; j <= last; ++j) {
+          const float4 q = reinterpret_cast<const float4*>(sp + (j * S + i) * 64)[c4];
+          v = make_float4(v.x + q.x, v.y + q.y, v.z + q.z, v.w + q.w);
+        }
+        reinterpret_cast<float4*>(dq_base + i * row_stride)[c4] =
+            make_float4(v.x * a.scale, v.y * a.scale, v.z * a.scale, v.w * a.scale);
+      }
+      if (!ok && tid == 0) atomicExch(a.err, CFA_ERR_TIMEOUT);
+    } else if (s_int[0] == nkb - 1) {
       const float* part = a.dq_part + static_cast<int64_t>(bh) * nkb * S * 64;
       const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * 64;
       float* dq_base = a.dqkv + static_cast<int64_t>(b) * S * row_stride + h * 64;

@@ -224,6 +224,12 @@ __device__ __forceinline__ void fence_after_sync() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// Order this thread's generic-proxy view of global memory (including what an acquire made visible)
+// before its later async-proxy accesses of global memory (bulk copies).
+__device__ __forceinline__ void fence_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Make this thread's generic-proxy shared-memory writes visible to the async proxy (the MMA).
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -218,10 +218,6 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
     tc::mbar_arrive_expect_tx(bar_ld, 256u * (min(TC_BM, S - q0) + min(TC_BN, S) +
                                               (T > 1 ? min(TC_BN, S - TC_BN) : 0)));
   }
-  if (w == 0) {
-    tc::tmem_alloc(tbase_p, TMEM_COLS);
-    tc::tmem_relinquish();
-  }
 
   griddep_wait();  // q, k, v may come from the previous kernel on the stream
   griddep_launch_dependents();
@@ -254,6 +250,11 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
     if (T > 2) stage_row_item(Kst, 0, tid, kp, a.k_ss, 2 * TC_BN, S);
     stage_row_item(Vst, 0, tid, vp, a.v_ss, 0, S);
     cp_async_commit();
+    if (w == 0) {  // TMEM while the rows travel
+      __syncwarp();
+      tc::tmem_alloc(tbase_p, TMEM_COLS);
+      tc::tmem_relinquish();
+    }
     err0 = !tc::mbar_wait(bar_ld, 0, WAIT_TIMEOUT_NS);
     split_staged_row(sm + OFF_K, k_rows, tid, nk0);
     if (T > 1) split_staged_row(sm + OFF_K + 3 * PART_K, k_rows + TC_BN * LDP, tid, nk1);
