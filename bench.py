@@ -591,8 +591,8 @@ def main():
             "tensor_frac": 6 * flops(b, H, S, D, CAUSAL, "fwd") / (infer_ms * 1e-3) / 1e12
             / pk["bf16_tflops"],
             "tensor_peak": pk["bf16_tflops"],
-            "note": "not part of the fwd+bwd step: training keeps the FFMA forward, whose scores "
-                    "the backward recomputes bit for bit"},
+            "note": "the forward-only entry point (inference); the fwd+bwd step runs the same "
+                    "kernel as the forward of the tensor-core pair"},
         "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": (sets[0].qkv.numel() + sets[0].dout.numel()) * 4,
@@ -608,7 +608,8 @@ def main():
                                  "not overlapped"},
         "roofline": {"bound": "tensor",
                      "pipe": "tcgen05 bf16 (fp32 operands as 3 bf16 parts, 6 products per fp32 "
-                             "product, hi/lo TMEM accumulators promoted into fp32 registers)",
+                             "product, one TMEM accumulator per 64-element window, small products "
+                             "first, promoted into fp32 registers)",
                      "kernel": "backward (prep + main, one cfa_bwd_f32_d64 call: bwd_tc_kernel)",
                      "achieved": achieved, "peak": pk["bf16_tflops"] / 6, "unit": "TFLOP/s",
                      "frac": achieved / (pk["bf16_tflops"] / 6), "traffic": traffic,
