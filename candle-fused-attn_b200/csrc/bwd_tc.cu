@@ -203,9 +203,23 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
   const int cg = (w >> 2) & 3;          // column group: 16 queries (S, dP) or dims (dV, dK, dQ)
   const int S = a.S;
   const int nkb = a.n_kblocks;
-  // (b, h)-major: a (b, h)'s key blocks run side by side and its last one finishes early.
-  const int kb = static_cast<int>(blockIdx.x) % nkb;
-  const int bh = static_cast<int>(blockIdx.x) / nkb;
+  const int BH = a.B * a.H;
+  // The work item. With the dQ partials (no-wait path): the block index, (b, h)-major, so a
+  // (b, h)'s key blocks run side by side and its last one finishes early. With the turn chain: a
+  // ticket drawn after the prep kernel's wait, key-block-major -- a block waits only on key block
+  // kb - 1 of its (b, h), which holds a smaller ticket, so it is running or done.
+  const bool chain = a.dq_part == nullptr;
+  int ticket = static_cast<int>(blockIdx.x);
+  if (chain) {
+    if (tid == 0) {
+      griddep_wait();  // the cleared ticket and counters
+      s_int[1] = atomicAdd(a.ticket, 1);
+    }
+    __syncthreads();
+    ticket = s_int[1];
+  }
+  const int kb = chain ? ticket / BH : ticket % nkb;
+  const int bh = chain ? ticket % BH : ticket / nkb;
   const int b = bh / a.H, h = bh % a.H;
   const int k0 = kb * KB;
   const float* qp = a.q + b * a.q_sb + h * a.q_sh;
@@ -215,6 +229,9 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
   const float* lp = a.lse + static_cast<int64_t>(bh) * S;
   const float* dp = a.dsum + static_cast<int64_t>(bh) * S;
   const int t_begin = CAUSAL ? k0 / QT : 0;  // queries before the block's first key see none
+  int* turn = a.turn + static_cast<int64_t>(bh) * a.n_qtiles;  // turn chain: per 64-query tile
+  const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * 64;  // dqkv floats per (b, s)
+  float* dq_base = a.dqkv + static_cast<int64_t>(b) * S * row_stride + h * 64;
   const int N = (S + QT - 1) / QT - t_begin;  // query tiles, >= 1 (k0 < S)
   bool err0 = false;
 
@@ -245,13 +262,14 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
     stage_row_item(st, 1, tid, gp, a.do_ss, q0, S);
     stage_ld(n);
   };
-  // The block one wave later (blockIdx + a.wave_ctas) starts by reading its key block's K, V rows
+  // The block one wave later (work item + a.wave_ctas) starts by reading its key block's K, V rows
   // and its first query tile's Q, dO rows, all at once across the wave: pull them into L2 while
   // this wave computes and HBM is otherwise idle (one 256-byte row per thread).
   auto prefetch_next_wave = [&]() {
-    const int nb = static_cast<int>(blockIdx.x) + a.wave_ctas;
+    const int nb = ticket + a.wave_ctas;
     if (a.wave_ctas <= 0 || nb >= static_cast<int>(gridDim.x) || tid >= 2 * KB + 2 * QT) return;
-    const int nkb2 = nb % nkb, nbh = nb / nkb, nb_b = nbh / a.H, nb_h = nbh % a.H;
+    const int nkb2 = chain ? nb / BH : nb % nkb, nbh = chain ? nb % BH : nb / nkb;
+    const int nb_b = nbh / a.H, nb_h = nbh % a.H;
     const int r = tid < 2 * KB ? (tid & (KB - 1)) : (tid & (QT - 1));
     const int row = tid < 2 * KB ? nkb2 * KB + r : (CAUSAL ? nkb2 * KB : 0) + r;
     if (row >= S) return;
@@ -465,13 +483,55 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
       tc::tmem_ld16(tbase + lane_sel + T_DQ1 + 16 * cg, xs);
       tc::tmem_wait_ld();
       const int qi = q0 + 16 * (w & 3) + lane;
-      if (lane < 16 && qi < S && !err) {
-        float* dst = a.dq_part + ((static_cast<int64_t>(bh) * nkb + kb) * S + qi) * 64 + 16 * cg;
+      if (!chain) {
+        if (lane < 16 && qi < S && !err) {
+          float* dst = a.dq_part + ((static_cast<int64_t>(bh) * nkb + kb) * S + qi) * 64 + 16 * cg;
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4)
-          __stcg(reinterpret_cast<float4*>(dst) + c4,
-                 make_float4(xb[4 * c4] + xs[4 * c4], xb[4 * c4 + 1] + xs[4 * c4 + 1],
-                             xb[4 * c4 + 2] + xs[4 * c4 + 2], xb[4 * c4 + 3] + xs[4 * c4 + 3]));
+          for (int c4 = 0; c4 < 4; ++c4)
+            __stcg(reinterpret_cast<float4*>(dst) + c4,
+                   make_float4(xb[4 * c4] + xs[4 * c4], xb[4 * c4 + 1] + xs[4 * c4 + 1],
+                               xb[4 * c4 + 2] + xs[4 * c4 + 2], xb[4 * c4 + 3] + xs[4 * c4 + 3]));
+        }
+      } else {
+        // Turn chain: query tile t's contributors are key blocks 0 .. last (causal: those holding
+        // a key <= the tile's last query); each adds its partial into dQ on its turn, through L2
+        // (__ldcg / __stcg), and the last multiplies by `scale`: dQ = ((p0 + p1) + ...) * scale,
+        // the no-wait path's sums bit for bit.
+        const int t = t_begin + n;
+        const int last = CAUSAL ? min(nkb - 1, min(S - 1, q0 + QT - 1) / KB) : nkb - 1;
+        bool go = true;
+        if (kb > 0) {
+          if (tid == 0) {
+            // (slot by tile parity: a thread may still read the last tile's flag)
+            s_int[2 + (n & 1)] = wait_turn_bounded(turn + t, kb, a.err, a.timeout_ns) ? 1 : 0;
+            // ORDER: with the barrier below, extends thread 0's acquire to the compute warps.
+            __threadfence();
+          }
+          bar_sync(1, NT);
+          go = s_int[2 + (n & 1)] != 0;
+        }
+        if (go && lane < 16 && qi < S) {
+          float4* dst = reinterpret_cast<float4*>(dq_base + qi * row_stride + 16 * cg);
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            float4 v = make_float4(xb[4 * c4] + xs[4 * c4], xb[4 * c4 + 1] + xs[4 * c4 + 1],
+                                   xb[4 * c4 + 2] + xs[4 * c4 + 2], xb[4 * c4 + 3] + xs[4 * c4 + 3]);
+            if (kb > 0) {
+              const float4 prev = __ldcg(dst + c4);
+              v = make_float4(prev.x + v.x, prev.y + v.y, prev.z + v.z, prev.w + v.w);
+            }
+            if (kb == last) v = make_float4(v.x * a.scale, v.y * a.scale, v.z * a.scale, v.w * a.scale);
+            __stcg(dst + c4, v);
+          }
+        }
+        err |= !go;
+        if (kb < last) {
+          // ORDER: every thread's dQ stores are visible GPU-wide before thread 0 hands the tile to
+          // key block kb + 1 (its acquire in wait_turn_bounded).
+          __threadfence();
+          bar_sync(1, NT);
+          if (tid == 0) st_release_gpu(turn + t, kb + 1);
+        }
       }
     }
   }
@@ -502,7 +562,7 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
                         dk[4 * c4 + 3] * a.scale);
       }
     }
-    if (tid == 0) s_int[0] = atom_add_acq_rel(a.turn + bh, 1);
+    if (tid == 0) s_int[0] = chain ? -1 : atom_add_acq_rel(a.turn + bh, 1);
     __syncthreads();
     const int64_t part_bytes = static_cast<int64_t>(nkb) * S * 64 * 4;
     if (s_int[0] == nkb - 1 && part_bytes <= OFF_DS) {

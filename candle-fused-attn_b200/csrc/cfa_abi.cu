@@ -28,12 +28,11 @@ DeviceOnce g_bwd_once[kMaxDevices];
 DeviceOnce g_hd_once[kMaxDevices];  // head dims 32 and 128
 DeviceOnce g_fwd_tc_once[kMaxDevices];
 DeviceOnce g_bwd_tc_once[kMaxDevices];
-// Head-dim-64 kernels (cfa_fwd_select): 1 (the default) = the tensor-core pair for sequences of at
-// most kTcPairMaxSeq -- forward and backward both on tcgen05, their scores bit-identical; the
-// backward needs the dQ partials of the larger workspace -- and the FFMA pair beyond; 0 = the
-// FFMA pair always. cfa_fwd_f32_infer takes the tensor-core forward at every length.
+// Head-dim-64 kernels (cfa_fwd_select): 1 (the default) = the tensor-core pair -- forward and
+// backward both on tcgen05, their scores bit-identical; the backward's dQ takes the no-wait
+// partials where the workspace holds them (cfa_bwd_workspace_bytes_fast, s <= 1024), else the
+// turn chain; 0 = the FFMA pair. cfa_fwd_f32_infer takes the tensor-core forward either way.
 std::atomic<int> g_fwd_impl{1};
-constexpr int64_t kTcPairMaxSeq = 64 * cfa::PART_MAX_KBLOCKS;  // the dQ partials' reach
 
 int setup(DeviceOnce* table, cudaError_t (*fn)()) {
   int dev = 0;
@@ -84,8 +83,7 @@ int fwd_impl(const float* q, const int64_t q_strides[3], const float* k,
   if (!strides_ok(q_strides) || !strides_ok(k_strides) || !strides_ok(v_strides))
     return CFA_ERR_ALIGNMENT;
   const bool d64 = head_dim == 64;
-  const bool tc = d64 && (impl == 1 || (impl < 0 && g_fwd_impl.load(std::memory_order_relaxed) == 1 &&
-                                         seq <= kTcPairMaxSeq));
+  const bool tc = d64 && (impl == 1 || (impl < 0 && g_fwd_impl.load(std::memory_order_relaxed) == 1));
   st = tc    ? setup(g_fwd_tc_once, cfa::setup_fwd_tc_attributes)
        : d64 ? setup(g_fwd_once, cfa::setup_fwd_attributes)
              : setup(g_hd_once, cfa::setup_hd_attributes);
@@ -141,10 +139,9 @@ int bwd_impl(const float* q, const int64_t q_strides[3], const float* k,
     return CFA_ERR_WORKSPACE;
   const bool d64 = head_dim == 64;
   // The tensor-core backward pairs with the tensor-core forward (cfa_fwd_select(1): the scores it
-  // recomputes are the forward's, bit for bit); it needs the dQ partials of the larger workspace.
-  const bool tc = d64 && g_fwd_impl.load(std::memory_order_relaxed) == 1 &&
-                  seq <= kTcPairMaxSeq && lay.total_fast > lay.total &&
-                  workspace_bytes >= lay.total_fast;
+  // recomputes are the forward's, bit for bit), at every length: its dQ takes the no-wait
+  // partials when the workspace holds them, else the turn chain (the same sums, bit for bit).
+  const bool tc = d64 && g_fwd_impl.load(std::memory_order_relaxed) == 1;
   st = tc    ? setup(g_bwd_tc_once, cfa::setup_bwd_tc_attributes)
        : d64 ? setup(g_bwd_once, cfa::setup_bwd_attributes)
              : setup(g_hd_once, cfa::setup_hd_attributes);

@@ -157,21 +157,21 @@ int cfa_bwd_f32_d64_noalloc(const float* q, const int64_t q_strides[3],
 int cfa_bwd_status(const void* workspace, void* stream);
 
 /* Head-dim-64 kernels for this process. 1 (the default): the tensor-core pair (fp32 from split
- * bf16 products with fp32 promotion: csrc/fwd_tc.cu, csrc/bwd_tc.cu) for sequences of at most 1024
- * -- the backward recomputes the forward's scores bit for bit and needs the dQ partials of the
- * larger workspace (cfa_bwd_workspace_bytes_fast; with the smaller one it runs the FFMA backward,
- * whose scores differ from the tensor-core forward's in the last bits) -- and the FFMA pair
- * beyond; 0: the FFMA pair always (csrc/fwd_ffma.cu, csrc/bwd_ffma.cu). Returns the previous
- * choice, -1 for any other value. No counterpart in the reference (one kernel pair). */
+ * bf16 products with fp32 promotion: csrc/fwd_tc.cu, csrc/bwd_tc.cu) at every length -- the
+ * backward recomputes the forward's scores bit for bit; its dQ takes the no-wait partials where
+ * the workspace holds them (cfa_bwd_workspace_bytes_fast, seq <= 1024), else the key-block turn
+ * chain, the same sums bit for bit. 0: the FFMA pair (csrc/fwd_ffma.cu, csrc/bwd_ffma.cu). The
+ * choice must not change between a forward and its backward. Returns the previous choice, -1 for
+ * any other value. No counterpart in the reference (one kernel pair). */
 int cfa_fwd_select(int impl);
 
 /* The forward for callers that run no backward on its outputs (inference, evaluation): as
  * cfa_fwd_f32 (head dims 32, 64, 128), with the tensor-core kernel at head dim 64 -- 1.4-2.3x
  * faster than the FFMA kernel on the BASELINE configs and closer to fp64 (O 9.4e-8 vs 2.9e-7 at
- * the canvas shape). L is written too; a backward fed with it recomputes the same scores only when
- * it runs the tensor-core backward (cfa_fwd_select(1), s <= 1024, the larger workspace) -- the FFMA
- * backward rounds them differently and drifts from the reference's CPU gradients by up to 1.4x its
- * 5e-6 band. No counterpart in the reference. */
+ * the canvas shape). L is written too; a backward fed with it recomputes the same scores when it
+ * runs the tensor-core backward (cfa_fwd_select(1)) -- the FFMA backward rounds them differently
+ * and drifts from the reference's CPU gradients by up to 1.4x its 5e-6 band. No counterpart in
+ * the reference. */
 int cfa_fwd_f32_infer(const float* q, const int64_t q_strides[3],
                       const float* k, const int64_t k_strides[3],
                       const float* v, const int64_t v_strides[3],

@@ -217,6 +217,39 @@ def test_no_wait_dq_path_equals_turn_chain(cuda, b, h, s, causal):
         _abi.fwd_select(prev)
 
 
+@pytest.mark.parametrize("b,h,s,causal", [(64, 6, 240, False), (3, 2, 200, True),
+                                          (2, 2, 512, True), (2, 3, 65, False),
+                                          (3, 4, 1024, True), (2, 2, 1000, False)])
+def test_tc_no_wait_dq_path_equals_turn_chain(cuda, b, h, s, causal):
+    """The tensor-core backward's two dQ orderings -- the key-block turn chain (the minimal
+    workspace; the only one past s = 1024) and the partials summed by the last block
+    (cfa_bwd_workspace_bytes_fast) -- give the same bits."""
+    prev = _abi.fwd_select(_abi.FWD_TC)
+    try:
+        _no_wait_vs_turn_chain(cuda, b, h, s, causal)
+    finally:
+        _abi.fwd_select(prev)
+
+
+@pytest.mark.parametrize("s,causal", [(2048, True), (1536, False)])
+def test_tc_pair_long_sequences(cuda, s, causal):
+    """Past s = 1024 the tensor-core pair runs with the turn chain: forward and backward within
+    the band of the fp32 composed path (normwise, and the max-abs band with the fp64 tie-break)."""
+    b, h = 1, 2
+    qkv, dout = oracle.seeded_inputs(b, h, s, 7, 0.5)
+    o_ref, _, g_ref = oracle.qkv_forward_backward(qkv, dout, h, 0.125, causal)
+    o64, _, g64 = oracle.qkv_forward_backward(qkv, dout, h, 0.125, causal, dtype=torch.float64)
+    o, g = run("fused_qkv", qkv, dout, h, 0.125, causal, cuda)
+    for got, r32, r64, name in ((o, o_ref, o64, "O"), (g, g_ref, g64, "dqkv")):
+        off = (got - r32).abs() >= BAND_MAXABS * max(1.0, r32.abs().max().item())
+        worse = (got.double() - r64).abs() > (r32.double() - r64).abs() + 1e-7
+        assert int((off & worse).sum()) == 0, f"{name}: beyond the band and farther from fp64"
+        assert oracle.normwise(got, r32) < BAND_NORMWISE, name
+    # and bit-identical on a rerun
+    o2, g2 = run("fused_qkv", qkv, dout, h, 0.125, causal, cuda)
+    assert torch.equal(o, o2) and torch.equal(g, g2)
+
+
 def _no_wait_vs_turn_chain(cuda, b, h, s, causal):
     qkv, dout = oracle.seeded_inputs(b, h, s, 4)
     x, g = qkv.to(cuda), dout.to(cuda)
