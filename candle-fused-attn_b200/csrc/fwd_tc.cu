@@ -62,9 +62,9 @@ constexpr int NQ = TC_THREADS / 128;  // threads per query row
 constexpr int CW = 64 / NQ;           // columns (keys of S, dims of O) per thread
 constexpr int PART_K = TC_BN * 64 * 2;  // bytes of one bf16 part of a [64][64] operand
 constexpr int TILE_F32 = TC_BN * 64 * 4;  // bytes of one fp32 [64][64] tile
-constexpr int OFF_K = 0;                       // two buffers of K parts, [64 keys][64 d]
-constexpr int OFF_V = OFF_K + 6 * PART_K;      // V parts, [64 keys][64 d], rows as K's
-constexpr int OFF_KST = OFF_V + 3 * PART_K;    // fp32 K tile in flight, [64][64]
+constexpr int OFF_K = 0;                       // three buffers of K parts, [64 keys][64 d]
+constexpr int OFF_V = OFF_K + 9 * PART_K;      // two buffers of V parts, [64 keys][64 d], rows as K's
+constexpr int OFF_KST = OFF_V + 6 * PART_K;    // fp32 K tile in flight, [64][64]
 constexpr int OFF_VST = OFF_KST + TILE_F32;    // fp32 V tile in flight, [64][64]
 constexpr int LDP = 68;                        // prologue staging: rows of 64 floats, 68 apart
 constexpr int OFF_ROWS = OFF_VST + TILE_F32;   // prologue: fp32 rows of Q, K(0), K(1)
@@ -223,16 +223,17 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
   griddep_launch_dependents();
 
   // Schedule. Tile n's softmax runs while the tensor core computes P V(n - 1) and S(n + 1): S is
-  // issued two tiles ahead (two S buffers in TMEM, two K part buffers), and P V(n - 1) is folded
-  // into O one tile late. Per tile n: (a) S(n) -> softmax -> p in registers; (b) P V(n - 1) -> O,
-  // then this thread's items of V(n) and K(n + 2) into their parts (both buffers now released);
-  // (c) p into P's parts; barrier; (d) issue P V(n) and S(n + 2); (e) stage V(n + 1), K(n + 3).
+  // issued two tiles ahead (two S buffers in TMEM, three K part buffers), and P V(n - 1) is folded
+  // into O one tile late. Per tile n: (a) S(n) -> softmax -> p in registers; (b) P V(n - 1) -> O;
+  // (c) p into P's parts; barrier; (d) issue P V(n) and S(n + 2); (e) this thread's items of
+  // V(n + 1) and K(n + 3) into their parts (two V buffers, three K buffers: both released) while
+  // S(n + 1) completes, then stage V(n + 2), K(n + 4).
   static_assert(TC_BM * 8 == 2 * TC_THREADS && TC_BN * 8 == TC_THREADS, "items per thread");
   const bool mma_warp = w == TC_THREADS / 32;  // warp 16: issues every MMA, nothing else
   // Prologue: the rows of Q, K(0), K(1) travel as one bulk copy each (threads 0-255, one row
-  // apiece) into row-major staging (rows past the sequence are not copied and read as zeros);
-  // K(0), K(1) split into their parts; Q (this thread's row and 16 dims: K-step cq of S's A
-  // operand) into TMEM; S(0), S(1) issued; K(2), V(0) in flight.
+  // apiece) into row-major staging (rows past the sequence are not copied and read as zeros),
+  // K(2) and V(0) by cp.async; K(0..2), V(0) split into their parts; Q (this thread's row and 16
+  // dims: K-step cq of S's A operand) into TMEM; S(0), S(1) issued; V(1), K(3) in flight.
   float* q_rows = reinterpret_cast<float*>(sm + OFF_ROWS);
   float* k_rows = q_rows + TC_BM * LDP;
   const int nq = min(TC_BM, S - q0), nk0 = min(TC_BN, S), nk1 = T > 1 ? min(TC_BN, S - TC_BN) : 0;
@@ -256,8 +257,14 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
       tc::tmem_relinquish();
     }
     err0 = !tc::mbar_wait(bar_ld, 0, WAIT_TIMEOUT_NS);
+    cp_async_wait_all();
     split_staged_row(sm + OFF_K, k_rows, tid, nk0);
     if (T > 1) split_staged_row(sm + OFF_K + 3 * PART_K, k_rows + TC_BN * LDP, tid, nk1);
+    if (T > 2) split_row_item(sm + OFF_K + 6 * PART_K, PART_K, Kst, 0, tid);
+    split_row_item(Vp, PART_K, Vst, 0, tid);
+    if (T > 1) stage_row_item(Vst, 0, tid, vp, a.v_ss, TC_BN, S);
+    if (T > 3) stage_row_item(Kst, 0, tid, kp, a.k_ss, 3 * TC_BN, S);
+    cp_async_commit();
 #pragma unroll
     for (int c4 = 0; c4 < CW / 4; ++c4) {
       const float4 u = row < nq ? reinterpret_cast<const float4*>(q_rows + row * LDP + CW * cq)[c4]
@@ -302,10 +309,11 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
       bar_sync(2, TC_BLOCK);
       tc::fence_after_sync();
       const int j = n & 1;
-      issue_split_mma<true>(t_o, tbase + T_P, sV, idesc);
+      issue_split_mma<true>(t_o, tbase + T_P, sV + 3 * PART_K * j, idesc);
       tc::commit_warp(bar_o);
       if (n + 2 < T) {
-        issue_split_mma<false>(tbase + T_S + 64 * j, tbase + T_Q, sK0 + 3 * PART_K * j, idesc);
+        issue_split_mma<false>(tbase + T_S + 64 * j, tbase + T_Q, sK0 + 3 * PART_K * ((n + 2) % 3),
+                               idesc);
         tc::commit_warp(bar_s + j);
       }
     }
@@ -385,8 +393,7 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
     }
     lpart = fmaf(lpart, alpha, psum);
     m = m_new;
-    // (b) O += P V(n - 1); V(n), K(n + 2) into the parts P V(n - 1) and S(n) have released.
-    cp_async_wait_all();
+    // (b) O += P V(n - 1).
     if (n > 0) {
       err |= !tc::mbar_wait(bar_o, (n - 1) & 1, WAIT_TIMEOUT_NS);
       tc::fence_after_sync();
@@ -395,8 +402,6 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
 #pragma unroll
       for (int c = 0; c < CW; ++c) acc[c] = fmaf(acc[c], alpha_prev, ob[c]);
     }
-    split_row_item(Vp, PART_K, Vst, 0, tid);
-    if (n + 2 < T) split_row_item(sm + OFF_K + 3 * PART_K * j, PART_K, Kst, 0, tid);
     // (c) p into P's parts in TMEM (K-step cq of P V's A operand; P V(n - 1) has read the last
     // ones); hand the tile to the MMA warp.
     {
@@ -411,9 +416,15 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
     bar_sync(2, TC_BLOCK);
     tc::fence_after_sync();
     if (n == 0) prefetch_next_wave();
-    // (e) Refill this thread's staging slots.
-    if (n + 1 < T) stage_row_item(Vst, 0, tid, vp, a.v_ss, (n + 1) * TC_BN, S);
-    if (n + 3 < T) stage_row_item(Kst, 0, tid, kp, a.k_ss, (n + 3) * TC_BN, S);
+    // (e) While S(n + 1) completes: V(n + 1) into V buffer (n + 1) % 2 (P V(n - 1) has read it) and
+    // K(n + 3) into K buffer n % 3 (S(n) has read it) -- both needed at the next hand-off -- then
+    // the tiles after them travel.
+    cp_async_wait_all();
+    if (n + 1 < T) split_row_item(Vp + 3 * PART_K * ((n + 1) & 1), PART_K, Vst, 0, tid);
+    if (n + 3 < T) split_row_item(sm + OFF_K + 3 * PART_K * (n % 3), PART_K, Kst, 0, tid);
+    tc::fence_async_smem();
+    if (n + 2 < T) stage_row_item(Vst, 0, tid, vp, a.v_ss, (n + 2) * TC_BN, S);
+    if (n + 4 < T) stage_row_item(Kst, 0, tid, kp, a.k_ss, (n + 4) * TC_BN, S);
     cp_async_commit();
     alpha_prev = alpha;
   }
@@ -438,7 +449,7 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
     // rows of LDP floats (a 16-byte rotation per row keeps both passes conflict-free); then every
     // 16 threads store one whole row of O [b, s, h, 64].
     float* o_rows = reinterpret_cast<float*>(sm + OFF_K);
-    static_assert(TC_BM * LDP * 4 <= 9 * PART_K, "O rows fit the part buffers");
+    static_assert(TC_BM * LDP * 4 <= 15 * PART_K, "O rows fit the part buffers");
     if (!mma_warp) {
       float l = red[NQ * row];
 #pragma unroll
