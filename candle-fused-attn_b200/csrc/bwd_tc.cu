@@ -300,6 +300,10 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
                 "prologue staging");
   const int nk = min(KB, S - k0), nq = min(QT, S - t_begin * QT);
   __syncthreads();  // the mbarriers' initialisation
+  if (mma_warp) {  // TMEM, by the warp that is idle while the rows travel (it also frees it)
+    tc::tmem_alloc(tbase_p, TMEM_COLS);
+    tc::tmem_relinquish();
+  }
   float vx[16];
   if (!mma_warp) {
     if (tid < 2 * KB + 2 * QT) {
@@ -314,11 +318,6 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
       } else if (r < nq) {
         tc::bulk_load(o_rows + r * LDP, gp + static_cast<int64_t>(t_begin * QT + r) * a.do_ss, 256, bar_ld);
       }
-    }
-    if (w == 0) {  // TMEM while the rows travel
-      __syncwarp();
-      tc::tmem_alloc(tbase_p, TMEM_COLS);
-      tc::tmem_relinquish();
     }
     griddep_wait();  // L, D, the cleared counters: the prep kernel's writes
     stage_ld(0);
@@ -655,7 +654,7 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  if (w == 0) tc::tmem_dealloc(tbase, TMEM_COLS);
+  if (mma_warp) tc::tmem_dealloc(tbase, TMEM_COLS);
 }
 
 }  // namespace

@@ -238,6 +238,10 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
   float* k_rows = q_rows + TC_BM * LDP;
   const int nq = min(TC_BM, S - q0), nk0 = min(TC_BN, S), nk1 = T > 1 ? min(TC_BN, S - TC_BN) : 0;
   __syncthreads();  // the mbarriers' initialisation
+  if (mma_warp) {  // TMEM, by the warp that is idle while the rows travel (it also frees it)
+    tc::tmem_alloc(tbase_p, TMEM_COLS);
+    tc::tmem_relinquish();
+  }
   float qx[CW];
   if (!mma_warp) {
     if (tid < TC_BM) {
@@ -251,11 +255,6 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
     if (T > 2) stage_row_item(Kst, 0, tid, kp, a.k_ss, 2 * TC_BN, S);
     stage_row_item(Vst, 0, tid, vp, a.v_ss, 0, S);
     cp_async_commit();
-    if (w == 0) {  // TMEM while the rows travel
-      __syncwarp();
-      tc::tmem_alloc(tbase_p, TMEM_COLS);
-      tc::tmem_relinquish();
-    }
     err0 = !tc::mbar_wait(bar_ld, 0, WAIT_TIMEOUT_NS);
     cp_async_wait_all();
     split_staged_row(sm + OFF_K, k_rows, tid, nk0);
@@ -472,7 +471,7 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  if (w == 0) tc::tmem_dealloc(tbase, TMEM_COLS);
+  if (mma_warp) tc::tmem_dealloc(tbase, TMEM_COLS);
 }
 
 }  // namespace
