@@ -2,10 +2,10 @@
 //
 // cfa_bwd_f32_d64_noalloc: the backward for callers that cannot allocate device memory.
 //
-// Who needs it: code that runs where cudaMalloc is off limits -- inside a CUDA-graph-captured
-// region that must not allocate, under a framework whose allocator owns all device memory and
-// gives plugins no scratch, in a real-time or embedded loop where an allocation's latency or
-// failure is not acceptable, or behind an FFI that only passes tensors it was given. Such a caller
+// Who needs it: code that runs where cudaMalloc is off limits -- under a framework whose
+// allocator owns all device memory and gives plugins no scratch, in a real-time or embedded loop
+// where an allocation's latency or failure is not acceptable, or behind an FFI that only passes
+// the tensors it was given. Such a caller
 // can still supply the inputs and outputs of the backward, but not the scratch that
 // cfa_bwd_f32_d64 asks for (D = rowsum(dO o O), the dQ turn counters, the work ticket and the
 // error flag). This entry point keeps that scratch in a file-scope static device array instead.

@@ -130,8 +130,9 @@ int cfa_bwd_f32(const float* q, const int64_t q_strides[3],
 /* Size of the static scratch of cfa_bwd_f32_d64_noalloc (4 MiB per GPU that loads the library). */
 #define CFA_NOALLOC_SCRATCH_BYTES (4u << 20)
 
-/* The backward without any allocation, for callers that cannot call cudaMalloc (a captured graph
- * region that must not allocate, a host framework that owns all device memory, a real-time loop).
+/* The backward without any allocation, for callers that cannot call cudaMalloc (a host framework
+ * whose allocator owns all device memory, a real-time loop that cannot risk an allocation, an FFI
+ * that passes only the tensors it was given).
  * Same arguments and results as cfa_bwd_f32_d64 minus the workspace: the scratch is a file-scope
  * static device array of CFA_NOALLOC_SCRATCH_BYTES, held by every GPU that loads the library
  * until exit. Has no counterpart in the reference (its launch layer always allocates,

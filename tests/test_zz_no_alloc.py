@@ -1,10 +1,10 @@
 # SPDX-License-Identifier: MIT OR Apache-2.0
 """cfa_bwd_f32_d64_noalloc: the backward for callers that cannot call cudaMalloc.
 
-Some callers cannot allocate device memory (inside a graph-captured region that must not allocate,
-under a host framework that owns every device byte, in a real-time loop), yet they can hand over
-inputs and outputs. This entry point takes no workspace: its scratch is a static device array in the
-library (4 MiB per GPU). These tests call it through the C ABI and compare it with the ordinary
+Some callers cannot allocate device memory (under a host framework that owns every device byte, in
+a real-time loop that cannot risk an allocation, behind an FFI that passes only given tensors), yet
+they can hand over inputs and outputs. This entry point takes no workspace: its scratch is a static
+device array in the library (4 MiB per GPU). These tests call it through the C ABI and compare it with the ordinary
 backward (cfa_bwd_f32_d64 with a caller-allocated workspace): the same kernels on the same inputs,
 so the results must agree bit for bit (well inside the 5e-6 band the other tests use), on two calls
 in a row -- the second call reuses the array the first one left behind.
