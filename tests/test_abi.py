@@ -52,7 +52,7 @@ def test_workspace_formula():
     dsum = (b * h * s * 4 + 255) // 256 * 256
     assert _abi.bwd_workspace_bytes(b, h, s) == 256 + turn + dsum
     assert _abi.bwd_workspace_bytes(0, 6, 240) == 256
-    # the no-wait dQ path adds one partial per key block (s <= 512 only)
+    # the no-wait dQ path adds one partial per key block of 64 (s <= 1024 only)
     nkb = (s + 63) // 64
     assert _abi.bwd_workspace_bytes_fast(b, h, s) == 256 + turn + dsum + nkb * b * h * s * 64 * 4
     assert _abi.bwd_workspace_bytes_fast(4, 16, 8192) == _abi.bwd_workspace_bytes(4, 16, 8192)
@@ -135,3 +135,21 @@ def test_bwd_rejects_small_or_misaligned_workspace():
 
 def test_null_status_query():
     assert _abi.bwd_status(None, None) == _abi.CFA_ERR_NULL
+
+
+def test_kernel_pair_selection():
+    """cfa_fwd_select: the tensor-core pair (1) is the default; the call returns the previous choice,
+    and any value but 0 and 1 returns -1 and changes nothing (the Python wrapper raises)."""
+    lib = _abi.load()
+    prev = _abi.fwd_select(_abi.FWD_TC)
+    try:
+        assert prev == _abi.FWD_TC
+        assert _abi.fwd_select(_abi.FWD_FFMA) == _abi.FWD_TC
+        assert lib.cfa_fwd_select(7) == -1
+        assert _abi.fwd_select(_abi.FWD_TC) == _abi.FWD_FFMA
+        assert lib.cfa_fwd_select(-3) == -1
+        with pytest.raises(ValueError):
+            _abi.fwd_select(2)
+        assert _abi.fwd_select(_abi.FWD_TC) == _abi.FWD_TC
+    finally:
+        _abi.fwd_select(prev)
