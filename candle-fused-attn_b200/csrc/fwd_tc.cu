@@ -159,7 +159,8 @@ __device__ __forceinline__ void issue_split_mma(uint32_t d, uint32_t a_tmem, uin
     tc::mma_bf16_tmem_a_warp(d, a_tmem + 8 * ks, blo + ((STEP * ks) >> 4), bd.hi, id, 1);
 }
 
-// Named barriers: 1 = the softmax threads (TC_THREADS), 2 = those plus the MMA warp (TC_BLOCK).
+// Named barriers: 2 = the softmax threads plus the MMA warp (TC_BLOCK); 3 + q = the four softmax
+// warps of TMEM lane quarter q (w & 3 == q), which hold the same rows and exchange their row maxima.
 // Every participant syncs (none only arrives), so no group can run a phase ahead of another even
 // when a bounded wait has expired.
 __device__ __forceinline__ void bar_sync(int id, int count) {
@@ -377,7 +378,7 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
       tmax = fmaxf(tmax, x);
     }
     red[NQ * row + cq] = tmax;
-    bar_sync(1, TC_THREADS);
+    bar_sync(3 + (w & 3), 32 * NQ);
     tmax = red[NQ * row];
 #pragma unroll
     for (int g = 1; g < NQ; ++g) tmax = fmaxf(tmax, red[NQ * row + g]);
