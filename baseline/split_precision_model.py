@@ -7,7 +7,8 @@ Schemes: bf16 x3 split with 6 or 9 products, tf32 x2 (3 products) / x3 (6 produc
 accumulation modelled as round-to-nearest or truncating, into one accumulator or separate
 high/low-order accumulators; and "promoted" variants, in which the (truncating) TMEM accumulators
 start fresh every W MMA steps and each window's sums are added into fp32 registers with
-round-to-nearest (the scheme csrc/fwd_tc.cu uses, W = 4 steps of 16 = 64 elements).
+round-to-nearest (W = 4 steps of 16 = 64 elements); and the one-accumulator window with the small
+products first and the high-order ones last, the scheme csrc/fwd_tc.cu and csrc/bwd_tc.cu use.
 
     python baseline/split_precision_model.py
 """
@@ -88,6 +89,26 @@ def tc_promoted(A, B, kind='bf16', n=3, K=16, W=4, sep=True, tmem_rnd=None):
     return rn32(rb + rs) if sep else rb
 
 
+def tc_small_first(A, B, K=16, W=4):
+    """The tensor-core pair's scheme (csrc/fwd_tc.cu, csrc/bwd_tc.cu): bf16 x3, 6 products, ONE
+    truncating TMEM accumulator per window of W steps; within a window the five small products of
+    every step are issued first and the W high-order A0 B0 steps last; each window is added into
+    fp32 registers round-to-nearest."""
+    As, Bs = split_bf16(A, 3), split_bf16(B, 3)
+    m, kk = A.shape; nn = B.shape[1]
+    r = torch.zeros(m, nn, dtype=torch.float64)
+    for w0 in range(0, kk, K * W):
+        steps = range(w0, min(kk, w0 + K * W), K)
+        t = torch.zeros_like(r)
+        for c in steps:
+            for (i, j) in PAIRS6[1:]:
+                t = rz32(t + As[i][:, c:c+K] @ Bs[j][c:c+K, :])
+        for c in steps:
+            t = rz32(t + As[0][:, c:c+K] @ Bs[0][c:c+K, :])
+        r = rn32(r + t)
+    return r
+
+
 def ffma_gemm(A, B):  # sequential fp32 fma over k: emulate with float64 product + rn32 each step
     m, kk = A.shape; nn = B.shape[1]; acc = torch.zeros(m, nn, dtype=torch.float64)
     for c in range(kk):
@@ -129,7 +150,7 @@ for bh in range(4):
     for name, gemm in [('ffma', ffma_gemm),
                        ('bf16x3(6) RN sep', lambda A,B: tc_gemm(A,B,('bf16',3),rn32)),
                        ('bf16x3(6) RZ sep', lambda A,B: tc_gemm(A,B,('bf16',3),rz32)),
-                       ('bf16x3(6) RZ onеacc', lambda A,B: tc_gemm(A,B,('bf16',3),rz32,sep=False)),
+                       ('bf16x3(6) RZ one acc', lambda A,B: tc_gemm(A,B,('bf16',3),rz32,sep=False)),
                        ('bf16x9 RZ sep', lambda A,B: tc_gemm(A,B,('bf16',9),rz32)),
                        ('tf32x2(3) RN sep', lambda A,B: tc_gemm(A,B,('tf32',2),rn32,K=8)),
                        ('tf32x3(6) RZ sep', lambda A,B: tc_gemm(A,B,('tf32',3),rz32,K=8)),
@@ -138,6 +159,7 @@ for bh in range(4):
                        ('bf16x3(6) RZ one, promoted W=4', lambda A,B: tc_promoted(A,B,W=4,sep=False)),
                        ('bf16x3(6) RZ sep, no promotion', lambda A,B: tc_promoted(A,B,W=10**9)),
                        ('tf32x2(3) RZ sep, promoted W=2', lambda A,B: tc_promoted(A,B,'tf32',2,8,W=2)),
+                       ('bf16x3(6) RZ one, small first, W=4', tc_small_first),
                        ]:
         out = attention(q, k, v, do, 0.125, gemm)
         acc = res.setdefault(name, [[0,0] for _ in range(4)])
