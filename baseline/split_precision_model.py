@@ -134,36 +134,43 @@ def attention(q, k, v, do, scale, gemm):
     dK = rn32(gemm(dS.T.contiguous(), q) * scale)
     return O, dQ, dK, dV
 
-qkv, dout = oracle.seeded_inputs(2, 2, 240, 0, 0.5)
-q4, k4, v4 = oracle.qkv_views(qkv, 2); g4 = oracle.heads_view(dout, 2)
-res = {}
-for bh in range(4):
-    b, h = divmod(bh, 2)
-    q, k, v, do = (t[b, h].double() for t in (q4, k4, v4, g4))
-    ref = attention(q, k, v, do, 0.125, lambda A, B: A @ B)   # fp64 reference (rn32 elementwise though)
-    # true fp64 everything:
-    def f64(A,B): return A@B
-    import math
-    S = (q@k.T)*0.125; m=S.max(1,keepdim=True).values; P=torch.exp(S-m); l=P.sum(1,keepdim=True); P=P/l; O=P@v; L=m+torch.log(l)
-    dV=P.T@do; dP=do@v.T; D=(do*O).sum(1,keepdim=True); dS=P*(dP-D); dQ=dS@k*0.125; dK=dS.T@q*0.125
-    truth=(O,dQ,dK,dV)
-    for name, gemm in [('ffma', ffma_gemm),
-                       ('bf16x3(6) RN sep', lambda A,B: tc_gemm(A,B,('bf16',3),rn32)),
-                       ('bf16x3(6) RZ sep', lambda A,B: tc_gemm(A,B,('bf16',3),rz32)),
-                       ('bf16x3(6) RZ one acc', lambda A,B: tc_gemm(A,B,('bf16',3),rz32,sep=False)),
-                       ('bf16x9 RZ sep', lambda A,B: tc_gemm(A,B,('bf16',9),rz32)),
-                       ('tf32x2(3) RN sep', lambda A,B: tc_gemm(A,B,('tf32',2),rn32,K=8)),
-                       ('tf32x3(6) RZ sep', lambda A,B: tc_gemm(A,B,('tf32',3),rz32,K=8)),
-                       ('bf16x3(6) RZ sep, promoted W=1', lambda A,B: tc_promoted(A,B,W=1)),
-                       ('bf16x3(6) RZ sep, promoted W=4', lambda A,B: tc_promoted(A,B,W=4)),
-                       ('bf16x3(6) RZ one, promoted W=4', lambda A,B: tc_promoted(A,B,W=4,sep=False)),
-                       ('bf16x3(6) RZ sep, no promotion', lambda A,B: tc_promoted(A,B,W=10**9)),
-                       ('tf32x2(3) RZ sep, promoted W=2', lambda A,B: tc_promoted(A,B,'tf32',2,8,W=2)),
-                       ('bf16x3(6) RZ one, small first, W=4', tc_small_first),
-                       ]:
-        out = attention(q, k, v, do, 0.125, gemm)
-        acc = res.setdefault(name, [[0,0] for _ in range(4)])
-        for i in range(4):
-            acc[i][0] += float(((out[i]-truth[i])**2).sum()); acc[i][1] += float((truth[i]**2).sum())
-for name, acc in res.items():
-    print(f"{name:22s} " + " ".join(f"{p}={ (a/b)**0.5:.2e}" for p,(a,b) in zip("O dQ dK dV".split(), acc)))
+SCHEMES = [
+    ('ffma', ffma_gemm),
+    ('bf16x3(6) RN sep', lambda A,B: tc_gemm(A,B,('bf16',3),rn32)),
+    ('bf16x3(6) RZ sep', lambda A,B: tc_gemm(A,B,('bf16',3),rz32)),
+    ('bf16x3(6) RZ one acc', lambda A,B: tc_gemm(A,B,('bf16',3),rz32,sep=False)),
+    ('bf16x9 RZ sep', lambda A,B: tc_gemm(A,B,('bf16',9),rz32)),
+    ('tf32x2(3) RN sep', lambda A,B: tc_gemm(A,B,('tf32',2),rn32,K=8)),
+    ('tf32x3(6) RZ sep', lambda A,B: tc_gemm(A,B,('tf32',3),rz32,K=8)),
+    ('bf16x3(6) RZ sep, promoted W=1', lambda A,B: tc_promoted(A,B,W=1)),
+    ('bf16x3(6) RZ sep, promoted W=4', lambda A,B: tc_promoted(A,B,W=4)),
+    ('bf16x3(6) RZ one, promoted W=4', lambda A,B: tc_promoted(A,B,W=4,sep=False)),
+    ('bf16x3(6) RZ sep, no promotion', lambda A,B: tc_promoted(A,B,W=10**9)),
+    ('tf32x2(3) RZ sep, promoted W=2', lambda A,B: tc_promoted(A,B,'tf32',2,8,W=2)),
+    ('bf16x3(6) RZ one, small first, W=4', tc_small_first),
+]
+
+
+def normwise_errors(schemes=SCHEMES, n_slices=4):
+    """Normwise error against fp64 of O, dQ, dK, dV per scheme, over the first n_slices (b, h)
+    slices of the seeded canvas-shaped input (s = 240, d = 64)."""
+    qkv, dout = oracle.seeded_inputs(2, 2, 240, 0, 0.5)
+    q4, k4, v4 = oracle.qkv_views(qkv, 2); g4 = oracle.heads_view(dout, 2)
+    res = {}
+    for bh in range(n_slices):
+        b, h = divmod(bh, 2)
+        q, k, v, do = (t[b, h].double() for t in (q4, k4, v4, g4))
+        S = (q@k.T)*0.125; m=S.max(1,keepdim=True).values; P=torch.exp(S-m); l=P.sum(1,keepdim=True); P=P/l; O=P@v
+        dV=P.T@do; dP=do@v.T; D=(do*O).sum(1,keepdim=True); dS=P*(dP-D); dQ=dS@k*0.125; dK=dS.T@q*0.125
+        truth=(O,dQ,dK,dV)
+        for name, gemm in schemes:
+            out = attention(q, k, v, do, 0.125, gemm)
+            acc = res.setdefault(name, [[0,0] for _ in range(4)])
+            for i in range(4):
+                acc[i][0] += float(((out[i]-truth[i])**2).sum()); acc[i][1] += float((truth[i]**2).sum())
+    return {name: [(a/b)**0.5 for a, b in acc] for name, acc in res.items()}
+
+
+if __name__ == "__main__":
+    for name, errs in normwise_errors().items():
+        print(f"{name:22s} " + " ".join(f"{p}={e:.2e}" for p, e in zip("O dQ dK dV".split(), errs)))
