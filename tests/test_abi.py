@@ -2,7 +2,6 @@
 """The C ABI on the CPU: libcfa.so loads, exports every symbol include/cfa.h declares, and rejects
 bad arguments before touching a device (so these run without a GPU)."""
 
-import ctypes
 import re
 import subprocess
 from pathlib import Path
