@@ -168,7 +168,8 @@ int cfa_fwd_select(int impl);
 
 /* The forward for callers that run no backward on its outputs (inference, evaluation): as
  * cfa_fwd_f32 (head dims 32, 64, 128), with the tensor-core kernel at head dim 64 -- 1.4-2.3x
- * faster than the FFMA kernel on the BASELINE configs and closer to fp64 (O 9.4e-8 vs 2.9e-7 at
+ * faster than the FFMA kernel on the benchmark shapes (general, canvas, strided causal, long
+ * causal) and closer to fp64 (O 9.4e-8 vs 2.9e-7 at
  * the canvas shape). L is written too; a backward fed with it recomputes the same scores when it
  * runs the tensor-core backward (cfa_fwd_select(1)) -- the FFMA backward rounds them differently
  * and drifts from the reference's CPU gradients by up to 1.4x its 5e-6 band. No counterpart in
