@@ -16,7 +16,8 @@
 //    4 MiB, i.e. b*h*s above about one million rows) is rejected with CFA_ERR_WORKSPACE before
 //    anything runs; use cfa_bwd_f32_d64 with your own workspace for those.
 //  - The first call on each device looks up the array's device address (cudaGetSymbolAddress)
-//    with that device current and caches it; make that first call before any stream capture.
+//    with that device current and caches it; a failed lookup is returned as CFA_ERR_CUDA, on
+//    that call and every later one on that device.
 //  - Every call on a device shares the one array, which keeps the last call's contents. The
 //    backward's first kernel clears the ticket, error flag and turn counters itself, and writes
 //    all of D, so no state carries over between calls. Calls whose kernels can overlap on the

@@ -139,8 +139,8 @@ int cfa_bwd_f32(const float* q, const int64_t q_strides[3],
  * src/cuda.rs:203-209).
  *  - Problems needing more scratch than that (cfa_bwd_workspace_bytes > 4 MiB) return
  *    CFA_ERR_WORKSPACE before anything runs.
- *  - The first call on a device looks up the array's device address; make it before any stream
- *    capture.
+ *  - The first call on a device looks up the array's device address and caches it; a failed
+ *    lookup returns CFA_ERR_CUDA, then and on every later call on that device.
  *  - All calls on a device share the array (each call resets what must start at zero); calls
  *    that can overlap on the GPU race and must be ordered by the caller.
  *  - The device error flag is not exposed: use cfa_bwd_f32_d64 to query cfa_bwd_status. */
