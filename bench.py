@@ -331,6 +331,61 @@ def cpu_baseline(b: int, seconds: float = 10.0, max_reps: int = 50):
                       f"oracle/oracle.cpp on {threads} threads"}
 
 
+def waves(args):
+    """Wave quantisation at the canvas shape: the head-dim-64 forward and backward (prep + main, the
+    fast workspace) at s = 240, 6 heads, over batches around the canvas's 64. Both kernels run one
+    block per SM, 12 blocks per batch row, so a batch of b fills 12 b / 148 waves; the times show
+    what the canvas's partial last wave (5.19 waves) costs. CUDA events per call, L2 flushed
+    between steps, median of `steps`; one JSON line per batch."""
+    from candle_fused_attn import _abi
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    sh = torch.cuda.current_stream(dev).cuda_stream
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
+    gen = torch.Generator().manual_seed(0)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    for b in (49, 56, 61, 62, 64, 74):
+        x = (torch.randn(b, S, 3 * H * D, generator=gen) * 0.5).to(dev)
+        g = torch.randn(b, S, H, D, generator=gen).to(dev)
+        st, gst = (x.stride(0), D, x.stride(1)), (g.stride(0), D, g.stride(1))
+        p = [x.data_ptr() + 4 * i * H * D for i in range(3)]
+        o = torch.empty(b, S, H, D, device=dev)
+        lse = torch.empty(b, H, S, device=dev)
+        nb = _abi.bwd_workspace_bytes_fast(b, H, S)
+        ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+        dqkv = torch.empty(b, S, 3, H, D, device=dev)
+
+        def fwd():
+            _abi.check(_abi.fwd(p[0], st, p[1], st, p[2], st, o.data_ptr(), lse.data_ptr(), b, H,
+                                S, D, SCALE, CAUSAL, sh), "fwd")
+
+        def bwd():
+            _abi.check(_abi.bwd(p[0], st, p[1], st, p[2], st, o.data_ptr(), lse.data_ptr(),
+                                g.data_ptr(), gst, dqkv.data_ptr(), ws.data_ptr(), nb, b, H, S, D,
+                                SCALE, CAUSAL, sh), "bwd")
+
+        for _ in range(args.warmup):
+            fwd()
+            bwd()
+        tf, tb = [], []
+        for _ in range(args.steps):
+            flush.zero_()
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            e[0].record()
+            fwd()
+            e[1].record()
+            bwd()
+            e[2].record()
+            torch.cuda.synchronize()
+            tf.append(e[0].elapsed_time(e[1]))
+            tb.append(e[1].elapsed_time(e[2]))
+        _abi.check(_abi.bwd_status(ws.data_ptr(), sh), "bwd_status")
+        print(json.dumps({"mode": "waves", "batch": b, "heads": H, "seq_len": S, "blocks": 12 * b,
+                          "waves": round(12 * b / sms, 3),
+                          "fwd_us": round(1000 * statistics.median(tf), 1),
+                          "bwd_us": round(1000 * statistics.median(tb), 1)}), flush=True)
+
+
 def run_reference_arm(args, rank, world):
     if rank != 0:
         return
@@ -365,9 +420,10 @@ def main():
     ap.add_argument("--pair", choices=["tc", "ffma"], default="tc",
                     help="kernels mode: the head-dim-64 kernel pair of the fwd+bwd step (tc: the "
                          "tensor-core pair, the default; ffma: the CUDA-core pair)")
-    ap.add_argument("--mode", choices=["full", "kernels", "suite"], default="full",
+    ap.add_argument("--mode", choices=["full", "kernels", "suite", "waves"], default="full",
                     help="kernels: warm-up + `steps` plain steps, no timing (for ncu); "
-                         "suite: every BASELINE config, ours vs the reference kernel")
+                         "suite: every BASELINE config, ours vs the reference kernel; "
+                         "waves: canvas-shaped fwd / bwd times over batches around 64")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -378,6 +434,8 @@ def main():
         return run_reference_arm(args, rank, world)
     if args.mode == "suite":
         return suite(args)
+    if args.mode == "waves":
+        return waves(args)
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
