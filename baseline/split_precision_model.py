@@ -171,6 +171,65 @@ def normwise_errors(schemes=SCHEMES, n_slices=4):
     return {name: [(a/b)**0.5 for a, b in acc] for name, acc in res.items()}
 
 
+
+def online_forward(q, k, v, scale, gemm, halves=False, tile=64):
+    """O of the online-softmax forward in fp32 (the tensor-core forward's order: per 64-key tile,
+    m and l updated, O rescaled and P V added). halves=True runs the key tiles as two independent
+    online passes (first half, second half of the tiles) merged by one log-sum-exp combine -- the
+    planned tail split, which every block would run so that a tile's bits do not depend on where
+    it lands in the grid."""
+    def run(t0, t1):
+        m = torch.full((q.shape[0], 1), -float("inf"), dtype=torch.float64)
+        l = torch.zeros_like(m)
+        o = torch.zeros(q.shape[0], v.shape[1], dtype=torch.float64)
+        for t in range(t0, t1):
+            kt, vt = k[t * tile:(t + 1) * tile], v[t * tile:(t + 1) * tile]
+            s_ = rn32(gemm(q, kt.T.contiguous()) * scale)
+            m_new = torch.maximum(m, s_.max(1, keepdim=True).values)
+            alpha = rn32(torch.exp(rn32(m - m_new)))
+            p_ = rn32(torch.exp(rn32(s_ - m_new)))
+            l = rn32(rn32(l * alpha) + rn32(p_.sum(1, keepdim=True)))
+            o = rn32(rn32(o * alpha) + gemm(p_, vt))
+            m = m_new
+        return m, l, o
+    nt = (k.shape[0] + tile - 1) // tile
+    if not halves:
+        m, l, o = run(0, nt)
+        return rn32(o / l)
+    h = (nt + 1) // 2
+    m1, l1, o1 = run(0, h)
+    m2, l2, o2 = run(h, nt)
+    m = torch.maximum(m1, m2)
+    a1, a2 = rn32(torch.exp(rn32(m1 - m))), rn32(torch.exp(rn32(m2 - m)))
+    l = rn32(rn32(l1 * a1) + rn32(l2 * a2))
+    o = rn32(rn32(o1 * a1) + rn32(o2 * a2))
+    return rn32(o / l)
+
+
+def halves_errors(n_slices=4):
+    """Normwise O error against fp64: the online forward on the pair's product scheme, whole vs
+    two halves combined (and plain FFMA for scale), over the seeded canvas-shaped slices."""
+    qkv, _ = oracle.seeded_inputs(2, 2, 240, 0, 0.5)
+    q4, k4, v4 = oracle.qkv_views(qkv, 2)
+    acc = {"ffma whole": [0.0, 0.0], "pair whole": [0.0, 0.0], "pair halves": [0.0, 0.0]}
+    for bh in range(n_slices):
+        b, h = divmod(bh, 2)
+        q, k, v = (t[b, h].double() for t in (q4, k4, v4))
+        S = (q @ k.T) * 0.125
+        P = torch.softmax(S, 1)
+        truth = P @ v
+        for name, gemm, halves in (("ffma whole", ffma_gemm, False),
+                                   ("pair whole", tc_small_first, False),
+                                   ("pair halves", tc_small_first, True)):
+            out = online_forward(q, k, v, 0.125, gemm, halves)
+            acc[name][0] += float(((out - truth) ** 2).sum())
+            acc[name][1] += float((truth ** 2).sum())
+    return {n: (a / b) ** 0.5 for n, (a, b) in acc.items()}
+
 if __name__ == "__main__":
+    if "--halves" in sys.argv:
+        for name, e in halves_errors().items():
+            print(f"{name:12s} O={e:.3e}")
+        sys.exit(0)
     for name, errs in normwise_errors().items():
         print(f"{name:22s} " + " ".join(f"{p}={e:.2e}" for p, e in zip("O dQ dK dV".split(), errs)))

@@ -39,3 +39,12 @@ def test_small_first_window_at_or_below_ffma(model):
     for i, out in enumerate("O dQ dK dV".split()):
         assert err["small first"][i] <= err["ffma"][i], (out, err)
         assert err["step order"][i] > err["ffma"][i], (out, err)
+
+
+def test_forward_in_two_halves_keeps_its_accuracy(model):
+    # The planned wave-tail split: every forward tile as two online-softmax halves merged by one
+    # log-sum-exp combine. Modelled on the pair's product scheme, O's error against fp64 must stay
+    # where the single pass has it (and below plain FFMA).
+    err = model.halves_errors(n_slices=2)
+    assert err["pair halves"] <= 1.05 * err["pair whole"], err
+    assert err["pair halves"] < err["ffma whole"], err
