@@ -13,6 +13,9 @@ on one seeded canvas-shaped (b, h) slice:
   dK and dV;
 - the same accumulator fed in plain step order: above FFMA (the order is what makes it work).
 
+It also checks, on the same model, that a forward run as two online-softmax halves merged by one
+log-sum-exp combine (a way to split the last wave's tiles over two SMs) keeps O's accuracy.
+
 The measured counterpart on the GPU is tests/test_fwd_tc_gpu.py::test_pair_accuracy_vs_ffma."""
 
 import importlib.util
