@@ -135,11 +135,14 @@ def make_inputs(rank: int, b: int):
 
 
 class OursStep:
-    """One forward + backward through the C ABI on preallocated device buffers."""
+    """One forward + backward through the C ABI on preallocated device buffers. pair: "tc" (the
+    head-dim-64 entry points, the tensor-core pair) or "ffma" (the CUDA-core pair's entry points)."""
 
-    def __init__(self, qkv, dout):
+    def __init__(self, qkv, dout, pair="tc"):
         from candle_fused_attn import _abi
         self.abi = _abi
+        self.fwd_fn = _abi.fwd if pair == "tc" else _abi.fwd_ffma
+        self.bwd_fn = _abi.bwd if pair == "tc" else _abi.bwd_ffma
         b = qkv.shape[0]
         self.b = b
         dev = qkv.device
@@ -155,25 +158,17 @@ class OursStep:
         self.gst = (dout.stride(0), D, dout.stride(1))
 
     def fwd(self, stream):
-        rc = self.abi.fwd(self.ptr[0], self.st, self.ptr[1], self.st, self.ptr[2], self.st,
-                          self.o.data_ptr(), self.lse.data_ptr(), self.b, H, S, D, SCALE, CAUSAL,
-                          stream)
-        if rc:
-            raise RuntimeError(self.abi.strerror(rc))
-
-    def fwd_infer(self, stream):
-        """The forward-only entry point (tensor cores at head dim 64)."""
-        rc = self.abi.fwd_infer(self.ptr[0], self.st, self.ptr[1], self.st, self.ptr[2], self.st,
-                                self.o.data_ptr(), self.lse.data_ptr(), self.b, H, S, D, SCALE,
-                                CAUSAL, stream)
+        rc = self.fwd_fn(self.ptr[0], self.st, self.ptr[1], self.st, self.ptr[2], self.st,
+                         self.o.data_ptr(), self.lse.data_ptr(), self.b, H, S, D, SCALE, CAUSAL,
+                         stream)
         if rc:
             raise RuntimeError(self.abi.strerror(rc))
 
     def bwd(self, stream):
-        rc = self.abi.bwd(self.ptr[0], self.st, self.ptr[1], self.st, self.ptr[2], self.st,
-                          self.o.data_ptr(), self.lse.data_ptr(), self.dout.data_ptr(), self.gst,
-                          self.dqkv.data_ptr(), self.ws.data_ptr(), self.ws_bytes, self.b, H, S,
-                          D, SCALE, CAUSAL, stream)
+        rc = self.bwd_fn(self.ptr[0], self.st, self.ptr[1], self.st, self.ptr[2], self.st,
+                         self.o.data_ptr(), self.lse.data_ptr(), self.dout.data_ptr(), self.gst,
+                         self.dqkv.data_ptr(), self.ws.data_ptr(), self.ws_bytes, self.b, H, S,
+                         D, SCALE, CAUSAL, stream)
         if rc:
             raise RuntimeError(self.abi.strerror(rc))
 
@@ -386,6 +381,13 @@ def waves(args):
                           "bwd_us": round(1000 * statistics.median(tb), 1)}), flush=True)
 
 
+def config_of(world: int) -> dict:
+    """The `config` of both arms' JSON lines (the same workload, the same keys)."""
+    return {"workload": WORKLOAD, "global_batch": B_PER_GPU * world, "seq_len": S, "heads": H,
+            "head_dim": D, "causal": CAUSAL, "parallelism": f"batch-shard x{world}",
+            "l2": f"inputs rotate over {N_SETS} sets of ~190 MB (> 126 MB L2)"}
+
+
 def run_reference_arm(args, rank, world):
     if rank != 0:
         return
@@ -395,8 +397,7 @@ def run_reference_arm(args, rank, world):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1)*0.5)",
-        "config": {"workload": WORKLOAD, "global_batch": B_PER_GPU, "seq_len": S, "heads": H,
-                   "head_dim": D, "causal": CAUSAL},
+        "config": config_of(world),
         "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": res["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -473,7 +474,8 @@ def main():
     sets = []
     for i in range(N_SETS):
         qkv, dout = make_inputs(rank * N_SETS + i, b)
-        sets.append(OursStep(qkv.to(dev), dout.to(dev)))
+        sets.append(OursStep(qkv.to(dev), dout.to(dev),
+                             args.pair if args.mode == "kernels" else "tc"))
     torch.cuda.synchronize()
 
     def step(i):
@@ -486,8 +488,6 @@ def main():
     torch.cuda.synchronize()
 
     if args.mode == "kernels":  # a fixed, short launch sequence for ncu
-        from candle_fused_attn import _abi
-        _abi.fwd_select(_abi.FWD_TC if args.pair == "tc" else _abi.FWD_FFMA)
         for i in range(args.steps):
             step(i)
         torch.cuda.synchronize()
@@ -516,8 +516,6 @@ def main():
     # per-kernel split: forward alone, backward alone (prep + main), same rotation
     fwd_ms = timed(lambda i: sets[i % N_SETS].fwd(sh), args.steps, stream)
     bwd_ms = timed(lambda i: sets[i % N_SETS].bwd(sh), args.steps, stream)
-    # the forward-only entry point (tensor-core kernel), which inference calls take
-    infer_ms = timed(lambda i: sets[i % N_SETS].fwd_infer(sh), args.steps, stream)
     if sets[0].abi.fwd_status(sh) != sets[0].abi.CFA_OK:
         raise RuntimeError("tensor-core forward: a bounded wait expired")
 
@@ -637,20 +635,10 @@ def main():
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1)*0.5 qkv, N(0,1) dO)",
-        "config": {"workload": WORKLOAD, "global_batch": b * world, "seq_len": S, "heads": H,
-                   "head_dim": D, "causal": CAUSAL, "parallelism": f"batch-shard x{world}",
-                   "l2": f"inputs rotate over {N_SETS} sets of ~190 MB (> 126 MB L2)"},
+        "config": config_of(world),
         "tflops_per_gpu": value / world,
         "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
         "fwd_tflops": flops(b, H, S, D, CAUSAL, "fwd") / (fwd_ms * 1e-3) / 1e12,
-        "forward_only": {
-            "ms": infer_ms, "tflops": flops(b, H, S, D, CAUSAL, "fwd") / (infer_ms * 1e-3) / 1e12,
-            "kernel": "fwd_tc_kernel (cfa_fwd_f32_infer): tcgen05, fp32 from 6 bf16 split products",
-            "tensor_frac": 6 * flops(b, H, S, D, CAUSAL, "fwd") / (infer_ms * 1e-3) / 1e12
-            / pk["bf16_tflops"],
-            "tensor_peak": pk["bf16_tflops"],
-            "note": "the forward-only entry point (inference); the fwd+bwd step runs the same "
-                    "kernel as the forward of the tensor-core pair"},
         "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": (sets[0].qkv.numel() + sets[0].dout.numel()) * 4,

@@ -23,15 +23,23 @@ recomputes P from it.
 Device only: the CUDA kernels are the product; the reference's CPU composed path lives in the
 test oracle (oracle/), never here. A CPU tensor, a dtype other than float32, a head_dim not in
 `HEAD_DIMS`, or a missing libcfa.so raise `FusedAttentionError` / `ImportError`.
+
+Failure detection: every device-side wait of the kernels is bounded. An expired wait (results
+invalid) is written by the kernel into a page-locked host flag this module registers with the C
+ABI (`cfa_error_sink`), so the next call of any function here raises `FusedAttentionError`
+without synchronising; `check_status()` synchronises first and raises for the calls before it.
 """
 
 from __future__ import annotations
+
+import ctypes
 
 import torch
 
 from . import _abi
 
 __all__ = [
+    "check_status",
     "CUDA_HEAD_DIM",
     "HEAD_DIMS",
     "FusedAttentionError",
@@ -135,19 +143,54 @@ def _stream(dev: torch.device) -> int:
 
 
 # ---------------------------------------------------------------------------------------------
+# Failure detection: the host-visible error flag (cfa_error_sink)
+# ---------------------------------------------------------------------------------------------
+
+_sink_tensor: torch.Tensor | None = None
+
+
+def _sink_flag() -> ctypes.c_int32:
+    """The registered page-locked flag (created and registered on first use, with CUDA up)."""
+    global _sink_tensor
+    if _sink_tensor is None:
+        t = torch.zeros(1, dtype=torch.int32).pin_memory()
+        st = _abi.error_sink(t.data_ptr())
+        if st != _abi.CFA_OK:
+            raise FusedAttentionError(_abi.strerror(st))
+        _sink_tensor = t
+    return ctypes.c_int32.from_address(_sink_tensor.data_ptr())
+
+
+def _raise_if_expired() -> None:
+    """Raise (once) for a bounded wait that expired in a kernel launched earlier: the flag is read
+    as it stands, with no synchronisation, so kernels still running are not covered."""
+    flag = _sink_flag()
+    code = flag.value
+    if code != 0:
+        flag.value = 0
+        raise FusedAttentionError(_abi.strerror(code))
+
+
+def check_status(device: torch.device | int | None = None) -> None:
+    """Synchronise `device` (default: the current one) and raise `FusedAttentionError` if a bounded
+    device-side wait of any earlier call expired (their results are then invalid)."""
+    torch.cuda.synchronize(device)
+    _raise_if_expired()
+
+
+# ---------------------------------------------------------------------------------------------
 # Launch wrappers (the src/cuda.rs role, over the C ABI)
 # ---------------------------------------------------------------------------------------------
 
-def attention_forward(q_ptr, qs, k_ptr, ks, v_ptr, vs, dims, scale, causal, device,
-                      infer: bool = False):
+def attention_forward(q_ptr, qs, k_ptr, ks, v_ptr, vs, dims, scale, causal, device):
     """One forward over device operands given as (pointer, (sb, sh, ss)): returns (O [b, s, h, d],
-    L [b, h, s]) as fresh tensors (the role of src/cuda.rs:140-185). `infer`: no backward will run
-    on these outputs -- the forward-only entry point (tensor cores at head dim 64)."""
+    L [b, h, s]) as fresh tensors (the role of src/cuda.rs:140-185)."""
     b, h, s, d = dims
     _check_head_dim(d)
+    _raise_if_expired()
     o = torch.empty((b, s, h, d), dtype=torch.float32, device=device)
     lse = torch.empty((b, h, s), dtype=torch.float32, device=device)
-    fwd = _abi.fwd_infer if infer else (_abi.fwd if d == CUDA_HEAD_DIM else _abi.fwd_hd)
+    fwd = _abi.fwd if d == CUDA_HEAD_DIM else _abi.fwd_hd
     with torch.cuda.device(device):
         st = fwd(q_ptr, qs, k_ptr, ks, v_ptr, vs, o.data_ptr(), lse.data_ptr(),
                  b, h, s, d, float(scale), causal, _stream(device))
@@ -162,6 +205,7 @@ def attention_backward(q_ptr, qs, k_ptr, ks, v_ptr, vs, o, lse, do_ptr, dos, dim
     from torch's caching allocator; `check_status` synchronises and reads the device error flag."""
     b, h, s, d = dims
     _check_head_dim(d)
+    _raise_if_expired()
     if not (o.is_contiguous() and lse.is_contiguous()):
         raise FusedAttentionError("fused_attention: O and L must be contiguous")
     dqkv = torch.empty((b, s, 3, h, d), dtype=torch.float32, device=device)
@@ -190,13 +234,13 @@ class _FusedAttention(torch.autograd.Function):
     """CustomOp3 `FusedAttention` (src/lib.rs:383-491): [b, h, s, d] in, [b, s, h, d] out."""
 
     @staticmethod
-    def forward(ctx, q, k, v, scale, causal, infer):
+    def forward(ctx, q, k, v, scale, causal):
         dims = _check_shapes(q, k, v)
         dev = _check_device(q, k, v, who="fused_attention")
         if not all(float4_aligned(t) for t in (q, k, v)):
             raise FusedAttentionError("fused_attention: rows must be 16-byte aligned")
         o, lse = attention_forward(q.data_ptr(), _bhs_strides(q), k.data_ptr(), _bhs_strides(k),
-                                   v.data_ptr(), _bhs_strides(v), dims, scale, causal, dev, infer)
+                                   v.data_ptr(), _bhs_strides(v), dims, scale, causal, dev)
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.scale, ctx.causal, ctx.dims = scale, causal, dims
         return o
@@ -211,22 +255,21 @@ class _FusedAttention(torch.autograd.Function):
             _bhs_strides(v), o, lse, grad.data_ptr(), (gb, gh, gs), ctx.dims, ctx.scale,
             ctx.causal, q.device)
         part = lambda i: dqkv[:, :, i].transpose(1, 2)  # noqa: E731  (src/lib.rs:484)
-        return part(0), part(1), part(2), None, None, None
+        return part(0), part(1), part(2), None, None
 
 
 class _FusedAttentionQkv(torch.autograd.Function):
     """CustomOp1 `FusedAttentionQkv` (src/lib.rs:494-590): qkv in, merged [b, s, h*d] out."""
 
     @staticmethod
-    def forward(ctx, qkv, heads, scale, causal, infer):
+    def forward(ctx, qkv, heads, scale, causal):
         _check_device(qkv, who="fused_attention_qkv")
         dims, strides, offs = qkv_geometry(tuple(qkv.shape), qkv.stride(), heads)
         if qkv.storage_offset() % 4 != 0 or any(x % 4 != 0 for x in strides):
             raise FusedAttentionError("fused_attention_qkv: rows must be 16-byte aligned")
         base = qkv.data_ptr()
         o, lse = attention_forward(base + 4 * offs[0], strides, base + 4 * offs[1], strides,
-                                   base + 4 * offs[2], strides, dims, scale, causal, qkv.device,
-                                   infer)
+                                   base + 4 * offs[2], strides, dims, scale, causal, qkv.device)
         ctx.save_for_backward(qkv, o, lse)
         ctx.heads, ctx.scale, ctx.causal = heads, scale, causal
         b, h, s, d = dims
@@ -245,14 +288,7 @@ class _FusedAttentionQkv(torch.autograd.Function):
         dqkv = attention_backward(
             base + 4 * offs[0], strides, base + 4 * offs[1], strides, base + 4 * offs[2], strides,
             o, lse, grad.data_ptr(), (gb, d, gs), dims, ctx.scale, ctx.causal, qkv.device)
-        return dqkv.view(b, s, 3 * h * d), None, None, None, None
-
-
-def _records_backward(*inputs: torch.Tensor) -> bool:
-    """Whether autograd records this call (grad mode on and an input requiring a gradient). When it
-    does not -- inference, torch.no_grad -- no backward will consume the forward's L, and the
-    forward-only entry point (tensor cores at head dim 64) runs."""
-    return torch.is_grad_enabled() and any(t.requires_grad for t in inputs)
+        return dqkv.view(b, s, 3 * h * d), None, None, None
 
 
 def fused_attention_qkv(qkv: torch.Tensor, heads: int, scale: float, causal: bool) -> torch.Tensor:
@@ -263,8 +299,7 @@ def fused_attention_qkv(qkv: torch.Tensor, heads: int, scale: float, causal: boo
                and st[0] % 4 == 0 and st[1] % 4 == 0)
     if not aligned:
         qkv = qkv.contiguous()
-    return _FusedAttentionQkv.apply(qkv, int(heads), float(scale), bool(causal),
-                                    not _records_backward(qkv))
+    return _FusedAttentionQkv.apply(qkv, int(heads), float(scale), bool(causal))
 
 
 def fused_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
@@ -272,8 +307,7 @@ def fused_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
     """src/lib.rs:143-161. q, k, v [batch, heads, seq, d] f32 on CUDA (d in HEAD_DIMS), any
     strides -> [batch, heads, seq, d] (a transposed view of a dense [batch, seq, heads, d] buffer)."""
     q, k, v = _float4_rows(q), _float4_rows(k), _float4_rows(v)
-    return _FusedAttention.apply(q, k, v, float(scale), bool(causal),
-                                 not _records_backward(q, k, v)).transpose(1, 2)
+    return _FusedAttention.apply(q, k, v, float(scale), bool(causal)).transpose(1, 2)
 
 
 from .host_pipeline import HostPipeline  # noqa: E402  (uses _abi; public host-buffer API)

@@ -42,14 +42,12 @@ EXPORTS = (
     "cfa_bwd_workspace_bytes_hd",
     "cfa_bwd_workspace_bytes_fast_hd",
     "cfa_bwd_f32",
-    "cfa_fwd_select",
     "cfa_fwd_status",
-    "cfa_fwd_f32_infer",
+    "cfa_fwd_f32_d64_ffma",
+    "cfa_bwd_f32_d64_ffma",
+    "cfa_bwd_noalloc_status",
+    "cfa_error_sink",
 )
-
-# Head-dim-64 forward implementations (cfa_fwd_select).
-FWD_FFMA = 0
-FWD_TC = 1
 
 # Head dims the generic entry points (cfa_fwd_f32, cfa_bwd_f32) take; the _d64 ones take 64 only,
 # as the reference's CUDA path does (src/lib.rs:91).
@@ -105,10 +103,14 @@ def load() -> ctypes.CDLL:
     lib.cfa_fwd_f32.argtypes = lib.cfa_fwd_f32_d64.argtypes
     lib.cfa_bwd_f32.restype = ctypes.c_int
     lib.cfa_bwd_f32.argtypes = lib.cfa_bwd_f32_d64.argtypes
-    lib.cfa_fwd_f32_infer.restype = ctypes.c_int
-    lib.cfa_fwd_f32_infer.argtypes = lib.cfa_fwd_f32_d64.argtypes
-    lib.cfa_fwd_select.restype = ctypes.c_int
-    lib.cfa_fwd_select.argtypes = [ctypes.c_int]
+    lib.cfa_fwd_f32_d64_ffma.restype = ctypes.c_int
+    lib.cfa_fwd_f32_d64_ffma.argtypes = lib.cfa_fwd_f32_d64.argtypes
+    lib.cfa_bwd_f32_d64_ffma.restype = ctypes.c_int
+    lib.cfa_bwd_f32_d64_ffma.argtypes = lib.cfa_bwd_f32_d64.argtypes
+    lib.cfa_bwd_noalloc_status.restype = ctypes.c_int
+    lib.cfa_bwd_noalloc_status.argtypes = [_p]
+    lib.cfa_error_sink.restype = ctypes.c_int
+    lib.cfa_error_sink.argtypes = [_p]
     lib.cfa_fwd_status.restype = ctypes.c_int
     lib.cfa_fwd_status.argtypes = [_p]
     for name in ("cfa_bwd_workspace_bytes_hd", "cfa_bwd_workspace_bytes_fast_hd"):
@@ -165,12 +167,21 @@ def fwd_hd(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, b, h, s, d, scale, c
         b, h, s, d, ctypes.c_float(scale), int(bool(causal)), stream)
 
 
-def fwd_infer(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, b, h, s, d, scale, causal,
-              stream) -> int:
-    """cfa_fwd_f32_infer (forward only: the tensor-core kernel at head dim 64); the status."""
-    return load().cfa_fwd_f32_infer(
+def fwd_ffma(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, b, h, s, d, scale, causal,
+             stream) -> int:
+    """cfa_fwd_f32_d64_ffma (the CUDA-core pair's forward); returns the status."""
+    return load().cfa_fwd_f32_d64_ffma(
         q_ptr, strides3(qs), k_ptr, strides3(ks), v_ptr, strides3(vs), o_ptr, lse_ptr,
         b, h, s, d, ctypes.c_float(scale), int(bool(causal)), stream)
+
+
+def bwd_ffma(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, do_ptr, dos, dqkv_ptr, ws_ptr,
+             ws_bytes, b, h, s, d, scale, causal, stream) -> int:
+    """cfa_bwd_f32_d64_ffma (the CUDA-core pair's backward; L from fwd_ffma); the status."""
+    return load().cfa_bwd_f32_d64_ffma(
+        q_ptr, strides3(qs), k_ptr, strides3(ks), v_ptr, strides3(vs), o_ptr, lse_ptr,
+        do_ptr, strides3(dos), dqkv_ptr, ws_ptr, ws_bytes, b, h, s, d,
+        ctypes.c_float(scale), int(bool(causal)), stream)
 
 
 def bwd_workspace_bytes_hd(b, h, s, d) -> int:
@@ -194,12 +205,16 @@ def bwd_status(ws_ptr, stream) -> int:
     return load().cfa_bwd_status(ws_ptr, stream)
 
 
-def fwd_select(impl: int) -> int:
-    """Head-dim-64 forward for this process (FWD_FFMA or FWD_TC); returns the previous choice."""
-    prev = load().cfa_fwd_select(int(impl))
-    if prev < 0:
-        raise ValueError(f"candle_fused_attn: unknown forward implementation {impl}")
-    return prev
+def error_sink(host_ptr) -> int:
+    """cfa_error_sink: register a page-locked host int (its address; None unregisters) that every
+    bounded-wait expiry reaches without a synchronisation. Returns the status."""
+    return load().cfa_error_sink(host_ptr)
+
+
+def bwd_noalloc_status(stream) -> int:
+    """cfa_bwd_noalloc_status: synchronises `stream`; CFA_ERR_TIMEOUT if the last no-allocation
+    backward on the current device had a bounded wait expire."""
+    return load().cfa_bwd_noalloc_status(stream)
 
 
 def fwd_status(stream) -> int:

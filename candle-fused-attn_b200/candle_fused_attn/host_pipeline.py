@@ -64,6 +64,8 @@ class HostPipeline:
         self.next_slot = 0  # slots rotate across chunks and across steps
 
     def _kernels(self, slot: int, b: int) -> None:
+        from . import _raise_if_expired  # an earlier call's expired bounded wait raises here
+        _raise_if_expired()
         h, s = self.h, self.s
         x, g = self.qkv[slot], self.dout[slot]
         st = (x.stride(0), 64, x.stride(1))

@@ -349,7 +349,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 2) bwd_ffma_kernel(const BwdArgs 
     bool go = true;
     if (kb > 0) {
       if (tid == 0) {
-        s_int[1] = wait_turn_bounded(turn + t, kb, a.err, a.timeout_ns) ? 1 : 0;
+        s_int[1] = wait_turn_bounded(turn + t, kb, a.err, a.timeout_ns, a.sink) ? 1 : 0;
         // ORDER: with the barrier below, extends thread 0's acquire to the whole block.
         __threadfence();
       }
@@ -493,19 +493,20 @@ namespace {
 // bounded routine the dQ turn chain uses, for a flag that nothing ever sets. Block 0 gives up after
 // `short_ns`; the others would wait 100x longer but bail out as soon as block 0 has flagged the
 // error. The kernel always ends: with CFA_ERR_TIMEOUT in ws[1] after about `short_ns`.
-__global__ void selftest_wait_kernel(int* ws, uint64_t short_ns) {
+__global__ void selftest_wait_kernel(int* ws, uint64_t short_ns, int* sink) {
   if (threadIdx.x != 0) return;
   const int* never = ws + 2;  // cleared by the host-side memset; nothing writes it afterwards
   const uint64_t limit = blockIdx.x == 0 ? short_ns : 100 * short_ns;
-  wait_turn_bounded(never, 1, ws + 1, limit);
+  wait_turn_bounded(never, 1, ws + 1, limit, sink);
 }
 
 }  // namespace
 
-cudaError_t launch_selftest_wait(int* ws, uint64_t short_ns, int blocks, cudaStream_t stream) {
+cudaError_t launch_selftest_wait(int* ws, uint64_t short_ns, int blocks, int* sink,
+                                 cudaStream_t stream) {
   cudaError_t e = cudaMemsetAsync(ws, 0, 16, stream);
   if (e != cudaSuccess) return e;
-  selftest_wait_kernel<<<blocks, 32, 0, stream>>>(ws, short_ns);
+  selftest_wait_kernel<<<blocks, 32, 0, stream>>>(ws, short_ns, sink);
   return cudaGetLastError();
 }
 

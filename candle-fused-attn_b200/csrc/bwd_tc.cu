@@ -502,7 +502,7 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
         if (kb > 0) {
           if (tid == 0) {
             // (slot by tile parity: a thread may still read the last tile's flag)
-            s_int[2 + (n & 1)] = wait_turn_bounded(turn + t, kb, a.err, a.timeout_ns) ? 1 : 0;
+            s_int[2 + (n & 1)] = wait_turn_bounded(turn + t, kb, a.err, a.timeout_ns, a.sink) ? 1 : 0;
             // ORDER: with the barrier below, extends thread 0's acquire to the compute warps.
             __threadfence();
           }
@@ -537,7 +537,7 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
   cp_async_wait_all();
   err = __syncthreads_or(err);  // any expired wait in the block: nothing is written
   if (err) {
-    if (tid == 0) atomicExch(a.err, CFA_ERR_TIMEOUT);
+    if (tid == 0) flag_timeout(a.err, a.sink);
     tc::mbar_wait(bar_t2, (N - 1) & 1, WAIT_TIMEOUT_NS);  // no MMA left in flight
   } else {
     // The dQ partials' hand-off: after the barrier above, thread 0's acquire-release count
@@ -589,7 +589,7 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
         reinterpret_cast<float4*>(dq_base + i * row_stride)[c4] =
             make_float4(v.x * a.scale, v.y * a.scale, v.z * a.scale, v.w * a.scale);
       }
-      if (!ok && tid == 0) atomicExch(a.err, CFA_ERR_TIMEOUT);
+      if (!ok && tid == 0) flag_timeout(a.err, a.sink);
     } else if (s_int[0] == nkb - 1) {
       const float* part = a.dq_part + static_cast<int64_t>(bh) * nkb * S * 64;
       const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * 64;

@@ -28,11 +28,12 @@ DeviceOnce g_bwd_once[kMaxDevices];
 DeviceOnce g_hd_once[kMaxDevices];  // head dims 32 and 128
 DeviceOnce g_fwd_tc_once[kMaxDevices];
 DeviceOnce g_bwd_tc_once[kMaxDevices];
-// Head-dim-64 kernels (cfa_fwd_select): 1 (the default) = the tensor-core pair -- forward and
-// backward both on tcgen05, their scores bit-identical; the backward's dQ takes the no-wait
-// partials where the workspace holds them (cfa_bwd_workspace_bytes_fast, s <= 1024), else the
-// turn chain; 0 = the FFMA pair. cfa_fwd_f32_infer takes the tensor-core forward either way.
-std::atomic<int> g_fwd_impl{1};
+// The head-dim-64 kernel pair of a call, chosen by the entry point (no process-wide state): the
+// tensor-core pair (the _d64 and head-dim-generic entry points) or the FFMA pair (the _ffma ones).
+// A backward recomputes its forward's scores bit for bit only within one pair.
+enum class Pair { kTensorCore, kFfma };
+// The host-visible error flag of cfa_error_sink, as the device addresses it (nullptr: none).
+std::atomic<int*> g_sink{nullptr};
 
 int setup(DeviceOnce* table, cudaError_t (*fn)()) {
   int dev = 0;
@@ -74,7 +75,7 @@ int check_dims(int64_t B, int64_t H, int64_t S, int64_t D, bool any_dim, bool* e
 int fwd_impl(const float* q, const int64_t q_strides[3], const float* k,
              const int64_t k_strides[3], const float* v, const int64_t v_strides[3], float* o,
              float* lse, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, float scale,
-             int causal, void* stream, bool any_dim, int impl) {
+             int causal, void* stream, bool any_dim, Pair pair) {
   bool empty = false;
   int st = check_dims(batch, heads, seq, head_dim, any_dim, &empty);
   if (st != CFA_OK || empty) return st;
@@ -83,7 +84,7 @@ int fwd_impl(const float* q, const int64_t q_strides[3], const float* k,
   if (!strides_ok(q_strides) || !strides_ok(k_strides) || !strides_ok(v_strides))
     return CFA_ERR_ALIGNMENT;
   const bool d64 = head_dim == 64;
-  const bool tc = d64 && (impl == 1 || (impl < 0 && g_fwd_impl.load(std::memory_order_relaxed) == 1));
+  const bool tc = d64 && pair == Pair::kTensorCore;
   st = tc    ? setup(g_fwd_tc_once, cfa::setup_fwd_tc_attributes)
        : d64 ? setup(g_fwd_once, cfa::setup_fwd_attributes)
              : setup(g_hd_once, cfa::setup_hd_attributes);
@@ -108,6 +109,7 @@ int fwd_impl(const float* q, const int64_t q_strides[3], const float* k,
   a.H = static_cast<int>(heads);
   a.S = static_cast<int>(seq);
   a.scale = scale;
+  a.sink = g_sink.load(std::memory_order_relaxed);
   const int bm = d64 ? cfa::fwd_tile_rows(seq) : cfa::hd_fwd_rows(static_cast<int>(head_dim), seq);
   a.n_qtiles = static_cast<int>((seq + bm - 1) / bm);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -121,7 +123,8 @@ int bwd_impl(const float* q, const int64_t q_strides[3], const float* k,
              const int64_t k_strides[3], const float* v, const int64_t v_strides[3],
              const float* o, const float* lse, const float* d_o, const int64_t do_strides[3],
              float* dqkv, void* workspace, size_t workspace_bytes, int64_t batch, int64_t heads,
-             int64_t seq, int64_t head_dim, float scale, int causal, void* stream, bool any_dim) {
+             int64_t seq, int64_t head_dim, float scale, int causal, void* stream, bool any_dim,
+             Pair pair) {
   bool empty = false;
   int st = check_dims(batch, heads, seq, head_dim, any_dim, &empty);
   if (st != CFA_OK || empty) return st;
@@ -138,10 +141,10 @@ int bwd_impl(const float* q, const int64_t q_strides[3], const float* k,
   if (workspace_bytes < lay.total || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return CFA_ERR_WORKSPACE;
   const bool d64 = head_dim == 64;
-  // The tensor-core backward pairs with the tensor-core forward (cfa_fwd_select(1): the scores it
-  // recomputes are the forward's, bit for bit), at every length: its dQ takes the no-wait
-  // partials when the workspace holds them, else the turn chain (the same sums, bit for bit).
-  const bool tc = d64 && g_fwd_impl.load(std::memory_order_relaxed) == 1;
+  // The tensor-core backward pairs with the tensor-core forward (the scores it recomputes are the
+  // forward's, bit for bit), at every length: its dQ takes the no-wait partials when the
+  // workspace holds them, else the turn chain (the same sums, bit for bit).
+  const bool tc = d64 && pair == Pair::kTensorCore;
   st = tc    ? setup(g_bwd_tc_once, cfa::setup_bwd_tc_attributes)
        : d64 ? setup(g_bwd_once, cfa::setup_bwd_attributes)
              : setup(g_hd_once, cfa::setup_hd_attributes);
@@ -203,6 +206,7 @@ int bwd_impl(const float* q, const int64_t q_strides[3], const float* k,
   a.n_qtiles = nqt;
   a.n_kblocks = nkb;
   a.timeout_ns = cfa::WAIT_TIMEOUT_NS;
+  a.sink = g_sink.load(std::memory_order_relaxed);
   // The no-wait dQ path when the workspace holds the partials (same results, bit for bit).
   a.dq_part = (lay.total_fast > lay.total && workspace_bytes >= lay.total_fast)
                   ? reinterpret_cast<float*>(ws + lay.part_off)
@@ -215,9 +219,13 @@ int bwd_impl(const float* q, const int64_t q_strides[3], const float* k,
 
 }  // namespace
 
+namespace cfa {
+int* error_sink() { return g_sink.load(std::memory_order_relaxed); }
+}  // namespace cfa
+
 extern "C" {
 
-int cfa_abi_version(void) { return (1 << 16) | 1; }
+int cfa_abi_version(void) { return (2 << 16) | 0; }
 
 const char* cfa_strerror(int status) {
   switch (status) {
@@ -241,7 +249,15 @@ int cfa_fwd_f32_d64(const float* q, const int64_t q_strides[3], const float* k,
                     float* o, float* lse, int64_t batch, int64_t heads, int64_t seq,
                     int64_t head_dim, float scale, int causal, void* stream) {
   return fwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, batch, heads, seq, head_dim,
-                  scale, causal, stream, false, -1);
+                  scale, causal, stream, false, Pair::kTensorCore);
+}
+
+int cfa_fwd_f32_d64_ffma(const float* q, const int64_t q_strides[3], const float* k,
+                         const int64_t k_strides[3], const float* v, const int64_t v_strides[3],
+                         float* o, float* lse, int64_t batch, int64_t heads, int64_t seq,
+                         int64_t head_dim, float scale, int causal, void* stream) {
+  return fwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, batch, heads, seq, head_dim,
+                  scale, causal, stream, false, Pair::kFfma);
 }
 
 int cfa_fwd_f32(const float* q, const int64_t q_strides[3], const float* k,
@@ -249,15 +265,7 @@ int cfa_fwd_f32(const float* q, const int64_t q_strides[3], const float* k,
                 float* lse, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                 float scale, int causal, void* stream) {
   return fwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, batch, heads, seq, head_dim,
-                  scale, causal, stream, true, -1);
-}
-
-int cfa_fwd_f32_infer(const float* q, const int64_t q_strides[3], const float* k,
-                      const int64_t k_strides[3], const float* v, const int64_t v_strides[3],
-                      float* o, float* lse, int64_t batch, int64_t heads, int64_t seq,
-                      int64_t head_dim, float scale, int causal, void* stream) {
-  return fwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, batch, heads, seq, head_dim,
-                  scale, causal, stream, true, 1);
+                  scale, causal, stream, true, Pair::kTensorCore);
 }
 
 size_t cfa_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq) {
@@ -289,7 +297,18 @@ int cfa_bwd_f32_d64(const float* q, const int64_t q_strides[3], const float* k,
                     int64_t head_dim, float scale, int causal, void* stream) {
   return bwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, d_o, do_strides, dqkv,
                   workspace, workspace_bytes, batch, heads, seq, head_dim, scale, causal, stream,
-                  false);
+                  false, Pair::kTensorCore);
+}
+
+int cfa_bwd_f32_d64_ffma(const float* q, const int64_t q_strides[3], const float* k,
+                         const int64_t k_strides[3], const float* v, const int64_t v_strides[3],
+                         const float* o, const float* lse, const float* d_o,
+                         const int64_t do_strides[3], float* dqkv, void* workspace,
+                         size_t workspace_bytes, int64_t batch, int64_t heads, int64_t seq,
+                         int64_t head_dim, float scale, int causal, void* stream) {
+  return bwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, d_o, do_strides, dqkv,
+                  workspace, workspace_bytes, batch, heads, seq, head_dim, scale, causal, stream,
+                  false, Pair::kFfma);
 }
 
 int cfa_bwd_f32(const float* q, const int64_t q_strides[3], const float* k,
@@ -300,7 +319,7 @@ int cfa_bwd_f32(const float* q, const int64_t q_strides[3], const float* k,
                 void* stream) {
   return bwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, d_o, do_strides, dqkv,
                   workspace, workspace_bytes, batch, heads, seq, head_dim, scale, causal, stream,
-                  true);
+                  true, Pair::kTensorCore);
 }
 
 int cfa_selftest_bounded_wait(void* workspace, int64_t timeout_ns, int blocks, void* stream) {
@@ -310,13 +329,27 @@ int cfa_selftest_bounded_wait(void* workspace, int64_t timeout_ns, int blocks, v
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return CFA_ERR_WORKSPACE;
   const cudaError_t e = cfa::launch_selftest_wait(static_cast<int*>(workspace),
                                                   static_cast<uint64_t>(timeout_ns), blocks,
+                                                  g_sink.load(std::memory_order_relaxed),
                                                   static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? CFA_OK : CFA_ERR_LAUNCH;
 }
 
-int cfa_fwd_select(int impl) {
-  if (impl != 0 && impl != 1) return -1;
-  return g_fwd_impl.exchange(impl);
+int cfa_error_sink(int* host_flag) {
+  if (host_flag == nullptr) {
+    g_sink.store(nullptr);
+    return CFA_OK;
+  }
+  if ((reinterpret_cast<uintptr_t>(host_flag) & 3u) != 0) return CFA_ERR_ALIGNMENT;
+  // Only page-locked host memory the device can address is accepted: a kernel's store to anything
+  // else would fault.
+  cudaPointerAttributes attr{};
+  if (cudaPointerGetAttributes(&attr, host_flag) != cudaSuccess) return CFA_ERR_CUDA;
+  if (attr.type != cudaMemoryTypeHost) return CFA_ERR_CUDA;
+  void* dev_ptr = nullptr;
+  if (cudaHostGetDevicePointer(&dev_ptr, host_flag, 0) != cudaSuccess || dev_ptr == nullptr)
+    return CFA_ERR_CUDA;
+  g_sink.store(static_cast<int*>(dev_ptr));
+  return CFA_OK;
 }
 
 int cfa_fwd_status(void* stream) {

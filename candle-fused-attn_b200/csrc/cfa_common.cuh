@@ -202,15 +202,28 @@ __device__ __forceinline__ void st_release_gpu(int* p, int v) {
   asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Records that a bounded wait expired: CFA_ERR_TIMEOUT into the device flag `err` (the first
+// writer wins) and, when the caller registered one with cfa_error_sink, into that host-visible
+// flag -- a plain system-scope store (no atomic on host memory), so the host reads it without a
+// synchronisation and without the kernel depending on host atomics.
+__device__ __forceinline__ void flag_timeout(int* err, int* sink) {
+  if (err != nullptr) atomicCAS(err, 0, CFA_ERR_TIMEOUT);
+  if (sink != nullptr) {
+    asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(sink), "r"(int(CFA_ERR_TIMEOUT))
+                 : "memory");
+    __threadfence_system();
+  }
+}
+
 // Wait (one thread) until *turn == want, at most `timeout_ns` of GPU time. Returns true when the
-// turn came. On expiry it records CFA_ERR_TIMEOUT in *err and returns false; it also returns
-// false as soon as any other waiter has recorded an error, so one expired wait ends every chain
-// quickly instead of each waiter spending its own full limit.
+// turn came. On expiry it records CFA_ERR_TIMEOUT (flag_timeout) and returns false; it also
+// returns false as soon as any other waiter has recorded an error, so one expired wait ends every
+// chain quickly instead of each waiter spending its own full limit.
 // ORDER: the acquire pairs with the release in pass_turn by the previous contributor: once this
 // returns true, that block's dQ stores are visible to the caller (extended to the whole block by
 // the caller's fence + barrier).
 __device__ __forceinline__ bool wait_turn_bounded(const int* turn, int want, int* err,
-                                                  uint64_t timeout_ns) {
+                                                  uint64_t timeout_ns, int* sink) {
   if (ld_acquire_gpu(turn) == want) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t spin = 1;; ++spin) {
@@ -219,7 +232,7 @@ __device__ __forceinline__ bool wait_turn_bounded(const int* turn, int want, int
     if ((spin & 15u) == 0u) {
       if (ld_relaxed_gpu(err) != 0) return false;
       if (global_timer_ns() - t0 > timeout_ns) {
-        atomicCAS(err, 0, CFA_ERR_TIMEOUT);
+        flag_timeout(err, sink);
         return false;
       }
     }

@@ -47,6 +47,7 @@ struct FwdArgs {
   float scale;
   int n_qtiles;
   int wave_ctas;  // tensor-core forward: blocks resident at once (one per SM); 0: none
+  int* sink;      // host-visible error flag (cfa_error_sink) or nullptr
 };
 
 struct BwdArgs {
@@ -71,6 +72,7 @@ struct BwdArgs {
   int n_kblocks; // ceil(S / BWD_BN)
   int wave_ctas;  // tensor-core backward: blocks resident at once (one per SM); 0: none
   uint64_t timeout_ns;
+  int* sink;      // host-visible error flag (cfa_error_sink) or nullptr
 };
 
 struct PrepArgs {
@@ -135,7 +137,11 @@ cudaError_t launch_hd_bwd_prep(const PrepArgs& a, int head_dim, cudaStream_t str
 cudaError_t launch_hd_bwd(const BwdArgs& a, int head_dim, int causal, cudaStream_t stream);
 
 // The failure-detection self-test (cfa_selftest_bounded_wait).
-cudaError_t launch_selftest_wait(int* ws, uint64_t short_ns, int blocks, cudaStream_t stream);
+cudaError_t launch_selftest_wait(int* ws, uint64_t short_ns, int blocks, int* sink,
+                                 cudaStream_t stream);
+
+// The host-visible error flag registered with cfa_error_sink (its device address), or nullptr.
+int* error_sink();
 
 // One-time per-device attribute set-up (dynamic shared memory limits).
 cudaError_t setup_fwd_attributes();

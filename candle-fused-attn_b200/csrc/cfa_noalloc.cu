@@ -17,7 +17,10 @@
 //    anything runs; use cfa_bwd_f32_d64 with your own workspace for those.
 //  - The first call on each device looks up the array's device address (cudaGetSymbolAddress)
 //    with that device current and caches it; a failed lookup is returned as CFA_ERR_CUDA, on
-//    that call and every later one on that device.
+//    that call and every later one on that device. The cache lives as long as the process: a
+//    caller that resets the device (cudaDeviceReset, or anything else that destroys the primary
+//    context) must not call this entry point on that device afterwards, since the array may then
+//    sit at another address.
 //  - Every call on a device shares the one array, which keeps the last call's contents. The
 //    backward's first kernel clears the ticket, error flag and turn counters itself, and writes
 //    all of D, so no state carries over between calls. Calls whose kernels can overlap on the
@@ -44,6 +47,40 @@ struct ScratchAddress {
 };
 ScratchAddress g_addr[kMaxDevices];
 
+// The checks of cfa_bwd_f32_d64 that do not need the workspace, in its order, so that a bad head
+// dim, an empty or oversized problem or a null pointer is reported as such and not as a
+// workspace shortage. The size bound keeps cfa_bwd_workspace_bytes's arithmetic in range.
+int precheck(const float* q, const float* k, const float* v, const float* o, const float* lse,
+             const float* d_o, float* dqkv, const int64_t* qs, const int64_t* ks,
+             const int64_t* vs, const int64_t* dos, int64_t batch, int64_t heads, int64_t seq,
+             int64_t head_dim, bool* empty) {
+  *empty = false;
+  if (batch < 0 || heads < 0 || seq < 0 || head_dim < 0) return CFA_ERR_SHAPE;
+  if (head_dim != CFA_HEAD_DIM) return CFA_ERR_HEAD_DIM;
+  if (batch == 0 || heads == 0 || seq == 0) {
+    *empty = true;
+    return CFA_OK;
+  }
+  const int64_t lim = (int64_t(1) << 31) - 1;
+  if (batch > lim || heads > lim || seq > lim || batch > lim / heads || batch * heads > lim / seq)
+    return CFA_ERR_OVERFLOW;
+  if (!q || !k || !v || !o || !lse || !d_o || !dqkv || !qs || !ks || !vs || !dos)
+    return CFA_ERR_NULL;
+  return CFA_OK;
+}
+
+int scratch_address(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CFA_ERR_CUDA;
+  ScratchAddress& a = g_addr[dev];
+  std::call_once(a.once, [&a] {
+    a.err = cudaGetSymbolAddress(&a.ptr, g_noalloc_scratch);
+  });
+  if (a.err != cudaSuccess || a.ptr == nullptr) return CFA_ERR_CUDA;
+  *out = a.ptr;
+  return CFA_OK;
+}
+
 }  // namespace
 
 extern "C" int cfa_bwd_f32_d64_noalloc(const float* q, const int64_t q_strides[3],
@@ -53,17 +90,23 @@ extern "C" int cfa_bwd_f32_d64_noalloc(const float* q, const int64_t q_strides[3
                                        const int64_t do_strides[3], float* dqkv, int64_t batch,
                                        int64_t heads, int64_t seq, int64_t head_dim, float scale,
                                        int causal, void* stream) {
-  if (batch > 0 && heads > 0 && seq > 0 &&
-      cfa_bwd_workspace_bytes(batch, heads, seq) > CFA_NOALLOC_SCRATCH_BYTES)
+  bool empty = false;
+  const int st = precheck(q, k, v, o, lse, d_o, dqkv, q_strides, k_strides, v_strides,
+                          do_strides, batch, heads, seq, head_dim, &empty);
+  if (st != CFA_OK || empty) return st;
+  if (cfa_bwd_workspace_bytes(batch, heads, seq) > CFA_NOALLOC_SCRATCH_BYTES)
     return CFA_ERR_WORKSPACE;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CFA_ERR_CUDA;
-  ScratchAddress& a = g_addr[dev];
-  std::call_once(a.once, [&a] {
-    a.err = cudaGetSymbolAddress(&a.ptr, g_noalloc_scratch);
-  });
-  if (a.err != cudaSuccess || a.ptr == nullptr) return CFA_ERR_CUDA;
+  void* scratch = nullptr;
+  const int sa = scratch_address(&scratch);
+  if (sa != CFA_OK) return sa;
   return cfa_bwd_f32_d64(q, q_strides, k, k_strides, v, v_strides, o, lse, d_o, do_strides, dqkv,
-                         a.ptr, CFA_NOALLOC_SCRATCH_BYTES, batch, heads, seq, head_dim, scale,
+                         scratch, CFA_NOALLOC_SCRATCH_BYTES, batch, heads, seq, head_dim, scale,
                          causal, stream);
+}
+
+extern "C" int cfa_bwd_noalloc_status(void* stream) {
+  void* scratch = nullptr;
+  const int sa = scratch_address(&scratch);
+  if (sa != CFA_OK) return sa;
+  return cfa_bwd_status(scratch, stream);
 }

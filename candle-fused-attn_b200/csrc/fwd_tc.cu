@@ -441,7 +441,10 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
   if (__syncthreads_or(err)) {
     // A commit did not arrive in time: flag it, give the tensor core one more bounded wait for
     // the last commits, free TMEM, write nothing.
-    if (tid == 0) atomicExch(&g_fwd_tc_err, 1);
+    if (tid == 0) {
+      atomicExch(&g_fwd_tc_err, 1);
+      flag_timeout(nullptr, a.sink);
+    }
     tc::mbar_wait(bar_o, (T - 1) & 1, WAIT_TIMEOUT_NS);
     tc::mbar_wait(bar_s + ((T - 1) & 1), ((T - 1) >> 1) & 1, WAIT_TIMEOUT_NS);
   } else {

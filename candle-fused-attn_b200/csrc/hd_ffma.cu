@@ -595,7 +595,7 @@ __global__ void __launch_bounds__(Bwd<D>::NT, 256 / (Bwd<D>::NT / 2)) hd_bwd_ker
     bool go = true;
     if (kb > 0) {
       if (tid == 0) {
-        s_int[1] = wait_turn_bounded(turn + t, kb, a.err, a.timeout_ns) ? 1 : 0;
+        s_int[1] = wait_turn_bounded(turn + t, kb, a.err, a.timeout_ns, a.sink) ? 1 : 0;
         __threadfence();  // ORDER: with the barrier, extends thread 0's acquire to the block
       }
       __syncthreads();

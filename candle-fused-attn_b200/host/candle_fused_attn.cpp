@@ -27,6 +27,31 @@ void check_status(int st) {
   if (st != CFA_OK) throw Error(cfa_strerror(st));
 }
 
+// The host-visible error flag (cfa_error_sink): page-locked, registered once per process, never
+// freed (kernels of any later call may write it).
+volatile int* error_flag() {
+  static volatile int* flag = [] {
+    void* p = nullptr;
+    check_cuda(cudaHostAlloc(&p, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable),
+               "cudaHostAlloc");
+    *static_cast<volatile int*>(p) = 0;
+    check_status(cfa_error_sink(static_cast<int*>(p)));
+    return static_cast<volatile int*>(p);
+  }();
+  return flag;
+}
+
+// Throws (once) for a bounded wait that expired in a kernel launched earlier; no synchronisation,
+// so kernels still running are not covered.
+void raise_if_expired() {
+  volatile int* flag = error_flag();
+  const int code = *flag;
+  if (code != 0) {
+    *flag = 0;
+    throw Error(cfa_strerror(code));
+  }
+}
+
 // src/lib.rs:302-315: the forward's L, kept for the backward.
 void save(std::mutex& mu, std::optional<Tensor>& slot, const Tensor& l) {
   std::lock_guard<std::mutex> g(mu);
@@ -52,6 +77,7 @@ std::pair<Tensor, Tensor> forward(float scale, bool causal, const Dims& dims,
   if (!head_dim_ok(d))
     throw Error("fused_attention: the CUDA kernels take head_dim 64 (and 32 or 128), got " +
                 std::to_string(d));
+  raise_if_expired();
   Tensor o = Tensor::empty({b, s, h, d});
   Tensor l = Tensor::empty({b, h, s});
   check_status(cfa_fwd_f32(ptr[0], st[0].data(), ptr[1], st[1].data(), ptr[2], st[2].data(),
@@ -70,6 +96,7 @@ Tensor cuda_backward(float scale, bool causal, const Dims& dims,
   if (!o.layout().is_contiguous() || !l.layout().is_contiguous())
     throw Error("fused_attention: O and L must be contiguous");
   const auto [b, h, s, d] = dims;
+  raise_if_expired();
   Tensor dqkv = Tensor::empty({b, s, 3, h, d});
   const size_t ws_bytes = cfa_bwd_workspace_bytes_fast_hd(
       static_cast<int64_t>(b), static_cast<int64_t>(h), static_cast<int64_t>(s),
@@ -96,6 +123,11 @@ std::array<int64_t, 3> i64(const std::array<size_t, 3>& a) {
 }
 
 }  // namespace
+
+void check_status() {
+  check_cuda(cudaStreamSynchronize(current_stream()), "cudaStreamSynchronize");
+  raise_if_expired();
+}
 
 bool float4_aligned(const Layout& l) {
   return l.rank() == 4 && l.start_offset % 4 == 0 && l.stride[3] == 1 && l.stride[0] % 4 == 0 &&

@@ -4,7 +4,13 @@
 // compiled caller links (libcfa_host.so), mirroring src/lib.rs name for name -- the two public
 // functions, the layout predicates and geometry, the two custom ops with their saved L, and the
 // `fused_attention:` error messages. The Rust crate itself keeps src/lib.rs and swaps only its
-// launch layer; this file is the same contract for C++ hosts.
+// launch layer (src/cuda.rs) for an `extern "C"` binding of include/cfa.h; this file is the same
+// contract for C++ hosts.
+//
+// Failure detection: the kernels' device-side waits are bounded. An expired wait (results
+// invalid) reaches a page-locked host flag this layer registers with the C ABI (cfa_error_sink)
+// on its first call, so the next call of any function here throws Error without synchronising;
+// check_status() synchronises the current stream first.
 //
 // What differs from candle, by necessity: there is no autograd graph, so the public functions
 // return the output together with the op that made it, and `backward(grad)` runs the op's `bwd`
@@ -115,6 +121,10 @@ struct Attention {
 QkvAttention fused_attention_qkv(const Tensor& qkv, size_t heads, float scale, bool causal);
 
 // src/lib.rs:143-161.
+// Synchronises the current stream and throws Error if a bounded device-side wait of any earlier
+// call expired (their results are then invalid). Has no counterpart in the reference.
+void check_status();
+
 Attention fused_attention(const Tensor& q, const Tensor& k, const Tensor& v, float scale,
                           bool causal);
 

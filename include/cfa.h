@@ -22,6 +22,14 @@
  *   cfa_bwd_workspace_bytes*_hd            reference's CUDA path rejects (src/cuda.rs:85-93) and
  *                                          lists as later work (ROADMAP.md "head_dim 32 and 128");
  *                                          its CPU path (src/lib.rs:241-299) takes any head dim
+ *   cfa_error_sink             has no counterpart: a host-visible flag that every bounded-wait
+ *                                          expiry reaches without a synchronisation
+ *
+ * Head dim 64 runs one kernel pair, as the reference does (src/cuda.rs:140-260): the tensor-core
+ * pair (csrc/fwd_tc.cu, csrc/bwd_tc.cu). A backward must run on the forward's L of the same pair
+ * (it recomputes the forward's scores bit for bit); the entry points fix the pair, so there is
+ * no process-wide setting two users could disagree on. The CUDA-core pair stays available under
+ * its own names (cfa_fwd_f32_d64_ffma, cfa_bwd_f32_d64_ffma) for comparison.
  *
  * Conventions (the reference's, src/cuda.rs:60-67 and src/lib.rs:165-188):
  *  - Every pointer is a device pointer at the operand's first element, on the current device.
@@ -31,8 +39,9 @@
  *  - Outputs are dense: O [b, s, h, 64] (merge-heads layout), L [b, h, s],
  *    dqkv [b, s, 3, h, 64] (dQ, dK, dV interleaved: a fused qkv projection's gradient).
  *  - Everything is asynchronous on `stream` (a cudaStream_t; NULL = the legacy default stream).
- *    No entry point allocates memory, synchronises, or keeps state besides a once-per-device
- *    kernel attribute set-up. Calls on different streams may run concurrently.
+ *    No entry point allocates memory or keeps state besides a once-per-device kernel attribute
+ *    set-up and the registered error sink; only the *_status queries synchronise. Calls on
+ *    different streams may run concurrently.
  *  - Zero batch, heads or seq is a valid empty problem: CFA_OK and nothing is launched (the
  *    reference panics there, its audit item B2).
  *  - Results are bit-identical across reruns and independent of the GPU's SM count and of how
@@ -59,7 +68,7 @@ enum cfa_status {
   CFA_ERR_NULL = 5,       /* a null pointer for a non-empty problem */
   CFA_ERR_WORKSPACE = 6,  /* workspace smaller than cfa_bwd_workspace_bytes or misaligned */
   CFA_ERR_LAUNCH = 7,     /* the CUDA launch failed */
-  CFA_ERR_TIMEOUT = 8,    /* a bounded device-side wait of the backward expired */
+  CFA_ERR_TIMEOUT = 8,    /* a bounded device-side wait of a kernel expired */
   CFA_ERR_CUDA = 9        /* another CUDA runtime error (device query, copy, sync) */
 };
 
@@ -127,6 +136,28 @@ int cfa_bwd_f32(const float* q, const int64_t q_strides[3],
                 int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                 float scale, int causal, void* stream);
 
+/* The CUDA-core (FFMA) pair at head dim 64: the same arguments, layouts and contract as
+ * cfa_fwd_f32_d64 / cfa_bwd_f32_d64, computed with packed fp32 FMAs (csrc/fwd_ffma.cu,
+ * csrc/bwd_ffma.cu). Pair cfa_bwd_f32_d64_ffma only with the L of cfa_fwd_f32_d64_ffma (and the
+ * tensor-core backward only with the tensor-core forward's L): across pairs the recomputed scores
+ * round differently and the gradients drift up to 1.4x past the reference's 5e-6 band. No
+ * counterpart in the reference (one kernel pair). */
+int cfa_fwd_f32_d64_ffma(const float* q, const int64_t q_strides[3],
+                         const float* k, const int64_t k_strides[3],
+                         const float* v, const int64_t v_strides[3],
+                         float* o, float* lse,
+                         int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                         float scale, int causal, void* stream);
+
+int cfa_bwd_f32_d64_ffma(const float* q, const int64_t q_strides[3],
+                         const float* k, const int64_t k_strides[3],
+                         const float* v, const int64_t v_strides[3],
+                         const float* o, const float* lse,
+                         const float* d_o, const int64_t do_strides[3],
+                         float* dqkv, void* workspace, size_t workspace_bytes,
+                         int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                         float scale, int causal, void* stream);
+
 /* Size of the static scratch of cfa_bwd_f32_d64_noalloc (4 MiB per GPU that loads the library). */
 #define CFA_NOALLOC_SCRATCH_BYTES (4u << 20)
 
@@ -139,11 +170,15 @@ int cfa_bwd_f32(const float* q, const int64_t q_strides[3],
  * src/cuda.rs:203-209).
  *  - Problems needing more scratch than that (cfa_bwd_workspace_bytes > 4 MiB) return
  *    CFA_ERR_WORKSPACE before anything runs.
+ *  - Other bad arguments (head dim, negative or oversized dimensions, null pointers) return the
+ *    codes cfa_bwd_f32_d64 returns for them, checked before the scratch size.
  *  - The first call on a device looks up the array's device address and caches it; a failed
- *    lookup returns CFA_ERR_CUDA, then and on every later call on that device.
+ *    lookup returns CFA_ERR_CUDA, then and on every later call on that device. The cached
+ *    address stays valid until the device's primary context is destroyed: do not call this
+ *    entry point on a device after cudaDeviceReset.
  *  - All calls on a device share the array (each call resets what must start at zero); calls
  *    that can overlap on the GPU race and must be ordered by the caller.
- *  - The device error flag is not exposed: use cfa_bwd_f32_d64 to query cfa_bwd_status. */
+ *  - cfa_bwd_noalloc_status reads the array's error flag. */
 int cfa_bwd_f32_d64_noalloc(const float* q, const int64_t q_strides[3],
                             const float* k, const int64_t k_strides[3],
                             const float* v, const int64_t v_strides[3],
@@ -153,33 +188,15 @@ int cfa_bwd_f32_d64_noalloc(const float* q, const int64_t q_strides[3],
                             int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                             float scale, int causal, void* stream);
 
+/* cfa_bwd_status for the static scratch of cfa_bwd_f32_d64_noalloc on the current device:
+ * synchronises `stream` and returns CFA_ERR_TIMEOUT if a bounded wait of the last no-allocation
+ * backward on this device expired, else CFA_OK (CFA_ERR_CUDA if the array cannot be addressed).
+ * Has no counterpart in the reference. */
+int cfa_bwd_noalloc_status(void* stream);
+
 /* Synchronises `stream` and returns CFA_ERR_TIMEOUT if a bounded wait of the last backward that
  * used `workspace` expired (its results are then invalid), else CFA_OK (or CFA_ERR_CUDA). */
 int cfa_bwd_status(const void* workspace, void* stream);
-
-/* Head-dim-64 kernels for this process. 1 (the default): the tensor-core pair (fp32 from split
- * bf16 products with fp32 promotion: csrc/fwd_tc.cu, csrc/bwd_tc.cu) at every length -- the
- * backward recomputes the forward's scores bit for bit; its dQ takes the no-wait partials where
- * the workspace holds them (cfa_bwd_workspace_bytes_fast, seq <= 1024), else the key-block turn
- * chain, the same sums bit for bit. 0: the FFMA pair (csrc/fwd_ffma.cu, csrc/bwd_ffma.cu). The
- * choice must not change between a forward and its backward. Returns the previous choice, -1 for
- * any other value. No counterpart in the reference (one kernel pair). */
-int cfa_fwd_select(int impl);
-
-/* The forward for callers that run no backward on its outputs (inference, evaluation): as
- * cfa_fwd_f32 (head dims 32, 64, 128), with the tensor-core kernel at head dim 64 -- 1.4-2.3x
- * faster than the FFMA kernel on the benchmark shapes (general, canvas, strided causal, long
- * causal) and closer to fp64 (O 9.4e-8 vs 2.9e-7 at
- * the canvas shape). L is written too; a backward fed with it recomputes the same scores when it
- * runs the tensor-core backward (cfa_fwd_select(1)) -- the FFMA backward rounds them differently
- * and drifts from the reference's CPU gradients by up to 1.4x its 5e-6 band. No counterpart in
- * the reference. */
-int cfa_fwd_f32_infer(const float* q, const int64_t q_strides[3],
-                      const float* k, const int64_t k_strides[3],
-                      const float* v, const int64_t v_strides[3],
-                      float* o, float* lse,
-                      int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
-                      float scale, int causal, void* stream);
 
 /* Synchronises `stream` and returns CFA_ERR_TIMEOUT if a bounded wait of a tensor-core forward
  * since the last call expired (its outputs are then invalid), else CFA_OK; clears the flag. */
@@ -192,10 +209,21 @@ int cfa_fwd_status(void* stream);
  * 256-byte, 256-aligned `workspace` for cfa_bwd_status to read. No GPU fault, no hang. */
 int cfa_selftest_bounded_wait(void* workspace, int64_t timeout_ns, int blocks, void* stream);
 
+/* Registers a host-visible error flag (NULL unregisters; the default is none). `host_flag` must
+ * be page-locked host memory the GPUs can address (cudaHostAlloc, cudaMallocHost, or a pinned
+ * tensor), 4-byte aligned; anything else returns CFA_ERR_CUDA (CFA_ERR_ALIGNMENT if misaligned)
+ * and leaves the registration unchanged. Every kernel launched afterwards (any device, any
+ * stream) writes CFA_ERR_TIMEOUT there when one of its bounded waits expires -- as well as into
+ * the flags cfa_fwd_status / cfa_bwd_status read -- so the caller learns of an expiry by reading
+ * one int, without synchronising; the library never clears it. Process-wide: one flag for all
+ * callers, which each see every expiry. The memory must stay valid while kernels launched with
+ * it registered can run. Has no counterpart in the reference, whose waits have no bound. */
+int cfa_error_sink(int* host_flag);
+
 /* A static description of a status code. */
 const char* cfa_strerror(int status);
 
-/* ABI version: (major << 16) | minor (1.1: the head-dim-generic entry points). */
+/* ABI version: (major << 16) | minor (2.0: one kernel pair per entry point, the error sink). */
 int cfa_abi_version(void);
 
 #ifdef __cplusplus

@@ -35,7 +35,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_version_and_strerror():
     lib = _abi.load()
-    assert lib.cfa_abi_version() >> 16 == 1
+    assert lib.cfa_abi_version() >> 16 == 2
     for code in range(10):
         msg = _abi.strerror(code)
         assert msg.startswith("fused_attention:")
@@ -136,19 +136,49 @@ def test_null_status_query():
     assert _abi.bwd_status(None, None) == _abi.CFA_ERR_NULL
 
 
-def test_kernel_pair_selection():
-    """cfa_fwd_select: the tensor-core pair (1) is the default; the call returns the previous choice,
-    and any value but 0 and 1 returns -1 and changes nothing (the Python wrapper raises)."""
+def test_ffma_pair_entry_points_check_arguments():
+    """The CUDA-core pair's entry points apply the head-dim-64 checks of the default ones before
+    touching a device."""
+    st = (1024, 256, 64)
     lib = _abi.load()
-    prev = _abi.fwd_select(_abi.FWD_TC)
-    try:
-        assert prev == _abi.FWD_TC
-        assert _abi.fwd_select(_abi.FWD_FFMA) == _abi.FWD_TC
-        assert lib.cfa_fwd_select(7) == -1
-        assert _abi.fwd_select(_abi.FWD_TC) == _abi.FWD_FFMA
-        assert lib.cfa_fwd_select(-3) == -1
-        with pytest.raises(ValueError):
-            _abi.fwd_select(2)
-        assert _abi.fwd_select(_abi.FWD_TC) == _abi.FWD_TC
-    finally:
-        _abi.fwd_select(prev)
+    for fwd in (_abi.fwd, _abi.fwd_ffma):
+        assert fwd(FAKE, st, FAKE, st, FAKE, st, FAKE, FAKE, 1, 1, 8, 32, 0.1, 0,
+                   None) == _abi.CFA_ERR_HEAD_DIM
+        assert fwd(FAKE, st, FAKE, st, FAKE, st, FAKE, FAKE, 0, 1, 8, 64, 0.1, 0,
+                   None) == _abi.CFA_OK
+        assert fwd(None, st, FAKE, st, FAKE, st, FAKE, FAKE, 1, 1, 8, 64, 0.1, 0,
+                   None) == _abi.CFA_ERR_NULL
+        assert fwd(FAKE + 4, st, FAKE, st, FAKE, st, FAKE, FAKE, 1, 1, 8, 64, 0.1, 0,
+                   None) == _abi.CFA_ERR_ALIGNMENT
+    for bwd in (_abi.bwd, _abi.bwd_ffma):
+        assert bwd(FAKE, st, FAKE, st, FAKE, st, FAKE, FAKE, FAKE, st, FAKE, FAKE, 1 << 20,
+                   1, 1, 8, 128, 0.1, 0, None) == _abi.CFA_ERR_HEAD_DIM
+        assert bwd(FAKE, st, FAKE, st, FAKE, st, FAKE, FAKE, FAKE, st, FAKE, FAKE, 16,
+                   1, 1, 8, 64, 0.1, 0, None) == _abi.CFA_ERR_WORKSPACE
+    assert not hasattr(_abi, "fwd_select")
+    with pytest.raises(AttributeError):
+        lib.cfa_fwd_select  # one pair per entry point: no process-wide switch
+
+
+def test_error_sink_host_checks():
+    """cfa_error_sink: NULL unregisters (always OK); a misaligned address is refused before any
+    CUDA call."""
+    assert _abi.error_sink(None) == _abi.CFA_OK
+    assert _abi.error_sink(FAKE + 2) == _abi.CFA_ERR_ALIGNMENT
+    assert _abi.error_sink(None) == _abi.CFA_OK
+
+
+def test_noalloc_checks_before_scratch_size():
+    """The no-allocation backward reports a bad head dim, an empty problem and a null pointer as
+    such -- checked before the scratch size, so a huge problem with head dim 32 is a head-dim
+    error, not a workspace one -- and an oversized problem as CFA_ERR_WORKSPACE."""
+    st = (1024, 256, 64)
+    args = lambda q, b, h, s, d: (q, st, FAKE, st, FAKE, st, FAKE, FAKE, FAKE, st, FAKE,  # noqa
+                                  b, h, s, d, 0.125, 0, None)
+    assert _abi.bwd_noalloc(*args(FAKE, 64, 6, 240, 32)) == _abi.CFA_ERR_HEAD_DIM
+    assert _abi.bwd_noalloc(*args(FAKE, 1 << 20, 64, 1 << 12, 32)) == _abi.CFA_ERR_HEAD_DIM
+    assert _abi.bwd_noalloc(*args(None, 64, 6, 240, 64)) == _abi.CFA_ERR_NULL
+    assert _abi.bwd_noalloc(*args(FAKE, 0, 6, 240, 64)) == _abi.CFA_OK
+    assert _abi.bwd_noalloc(*args(FAKE, -1, 6, 240, 64)) == _abi.CFA_ERR_SHAPE
+    assert _abi.bwd_noalloc(*args(FAKE, 1 << 30, 1 << 30, 1 << 30, 64)) == _abi.CFA_ERR_OVERFLOW
+    assert _abi.bwd_noalloc(*args(FAKE, 64, 64, 1024, 64)) == _abi.CFA_ERR_WORKSPACE

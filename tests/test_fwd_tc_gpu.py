@@ -1,7 +1,6 @@
 # SPDX-License-Identifier: MIT OR Apache-2.0
-"""The tensor-core forward (csrc/fwd_tc.cu) against the CPU oracle. It runs for forward-only calls
-(cfa_fwd_f32_infer; the Python API takes it when no input needs a gradient) and, selected with
-cfa_fwd_select(1), for every head-dim-64 forward.
+"""The tensor-core forward (csrc/fwd_tc.cu) against the CPU oracle: the forward of every head-dim-64
+call through cfa_fwd_f32_d64 / cfa_fwd_f32 and the Python API.
 
 Same bar as the FFMA forward (tests/parity.rs:161-167, :210-221 and the north star): 1e-5
 normwise and a 5e-6 max-abs band (scaled by the output magnitude) against the fp32 composed path
@@ -17,6 +16,7 @@ import torch
 import candle_fused_attn as cfa
 from candle_fused_attn import _abi
 from oracle import oracle
+from pairs import run_pair
 
 pytestmark = pytest.mark.gpu
 
@@ -25,9 +25,7 @@ BAND_NORMWISE = 1e-5
 
 @pytest.fixture
 def tc(cuda):
-    prev = _abi.fwd_select(_abi.FWD_TC)
-    yield cuda
-    _abi.fwd_select(prev)
+    return cuda
 
 
 def status_ok():
@@ -106,9 +104,7 @@ def test_accuracy_vs_fp64(tc):
     x = qkv.to(tc)
     o_tc = cfa.fused_attention_qkv(x, h, 0.125, False).cpu().double()
     status_ok()
-    _abi.fwd_select(_abi.FWD_FFMA)
-    o_ff = cfa.fused_attention_qkv(x.requires_grad_(True), h, 0.125, False).detach().cpu().double()
-    _abi.fwd_select(_abi.FWD_TC)
+    o_ff = run_pair("ffma", qkv, None, h, 0.125, False, tc)[0].cpu().double()
     e_tc, e_ff = oracle.normwise(o_tc, o64), oracle.normwise(o_ff, o64)
     print(f"O vs fp64: tensor cores {e_tc:.3e}, FFMA {e_ff:.3e}")
     assert e_tc <= e_ff, (e_tc, e_ff)
@@ -125,24 +121,44 @@ def test_long_causal_slice(tc):
     check(out.cpu(), o_ref.reshape(b, s, -1), "O")
 
 
-def test_kernel_selection(cuda):
-    """The default (cfa_fwd_select(1)) runs the tensor-core pair at head dim 64 for s <= 1024:
-    the training forward equals the forward-only one bit for bit. With the FFMA pair selected,
-    training takes the FFMA forward while forward-only calls keep the tensor cores."""
-    assert _abi.fwd_select(_abi.FWD_TC) == _abi.FWD_TC  # the default
-    qkv, _ = oracle.seeded_inputs(2, 6, 240, 9, 0.5)
+def test_one_pair_per_entry_point(cuda):
+    """Head dim 64 has one kernel pair per entry point and no process-wide switch: the Python API
+    (with or without autograd) runs the tensor-core pair, bit for bit the C ABI's default entry
+    points; the CUDA-core pair is reached only through its own entry points and differs."""
+    qkv, dout = oracle.seeded_inputs(2, 6, 240, 9, 0.5)
     x = qkv.to(cuda)
-    o_infer = cfa.fused_attention_qkv(x, 6, 0.125, False)
+    o_abi, _, g_abi = run_pair("tc", qkv, dout, 6, 0.125, False, cuda)
+    o_ffma, _, _ = run_pair("ffma", qkv, dout, 6, 0.125, False, cuda)
     with torch.no_grad():
-        o_nograd = cfa.fused_attention_qkv(x.clone().requires_grad_(True), 6, 0.125, False)
-    o_train = cfa.fused_attention_qkv(x.clone().requires_grad_(True), 6, 0.125, False).detach()
-    _abi.fwd_select(_abi.FWD_FFMA)
-    o_ffma = cfa.fused_attention_qkv(x.clone().requires_grad_(True), 6, 0.125, False).detach()
-    o_infer2 = cfa.fused_attention_qkv(x, 6, 0.125, False)
-    _abi.fwd_select(_abi.FWD_TC)
+        o_nograd = cfa.fused_attention_qkv(x, 6, 0.125, False)
+    xg = x.clone().requires_grad_(True)
+    o_train = cfa.fused_attention_qkv(xg, 6, 0.125, False)
+    o_train.backward(dout.to(cuda))
     status_ok()
-    assert torch.equal(o_infer, o_train) and torch.equal(o_nograd, o_train)
-    assert torch.equal(o_infer2, o_train) and not torch.equal(o_ffma, o_train)
+    assert torch.equal(o_nograd, o_abi) and torch.equal(o_train.detach(), o_abi)
+    assert torch.equal(xg.grad, g_abi)
+    assert not torch.equal(o_ffma, o_abi)
+
+
+def test_two_users_mixing_pairs(cuda):
+    """Two users in one process, one on each pair, their forwards and backwards interleaved: each
+    gets its own pair's results bit for bit (nothing one does changes the other's kernels), and
+    both stay within the band of the CPU composed path."""
+    b, s, h = 2, 200, 3
+    qkv, dout = oracle.seeded_inputs(b, h, s, 21, 0.5)
+    o_ref, _, g_ref = oracle.qkv_forward_backward(qkv, dout, h, 0.125, True)
+    alone = {p: run_pair(p, qkv, dout, h, 0.125, True, cuda) for p in ("tc", "ffma")}
+    # interleaved: user A (tensor cores, through the public API) and user B (the CUDA-core pair)
+    xa = qkv.to(cuda).requires_grad_(True)
+    oa = cfa.fused_attention_qkv(xa, h, 0.125, True)
+    ob, _, gb = run_pair("ffma", qkv, dout, h, 0.125, True, cuda)
+    oa.backward(dout.to(cuda))
+    status_ok()
+    assert torch.equal(oa.detach(), alone["tc"][0]) and torch.equal(xa.grad, alone["tc"][2])
+    assert torch.equal(ob, alone["ffma"][0]) and torch.equal(gb, alone["ffma"][2])
+    for o, g in ((oa.detach(), xa.grad), (ob, gb)):
+        assert oracle.normwise(o.cpu(), o_ref.reshape(b, s, -1)) < BAND_NORMWISE
+        assert oracle.normwise(g.cpu(), g_ref.reshape(b, s, -1)) < BAND_NORMWISE
 
 
 def test_pair_accuracy_vs_ffma(cuda):
@@ -154,17 +170,13 @@ def test_pair_accuracy_vs_ffma(cuda):
     o64, _, g64 = oracle.qkv_forward_backward(qkv, dout, h, 0.125, False, dtype=torch.float64)
     g64 = g64.reshape(b, s, 3, h * 64)
 
-    def errors(impl):
-        prev = _abi.fwd_select(impl)
-        x = qkv.to(cuda).requires_grad_(True)
-        out = cfa.fused_attention_qkv(x, h, 0.125, False)
-        out.backward(dout.to(cuda))
-        _abi.fwd_select(prev)
-        g = x.grad.cpu().double().reshape(b, s, 3, h * 64)
-        return {"O": oracle.normwise(out.detach().cpu().double(), o64),
+    def errors(pair):
+        out, _, g = run_pair(pair, qkv, dout, h, 0.125, False, cuda)
+        g = g.cpu().double().reshape(b, s, 3, h * 64)
+        return {"O": oracle.normwise(out.cpu().double(), o64),
                 **{n: oracle.normwise(g[:, :, i], g64[:, :, i]) for i, n in enumerate(("dQ", "dK", "dV"))}}
 
-    e_tc, e_ff = errors(_abi.FWD_TC), errors(_abi.FWD_FFMA)
+    e_tc, e_ff = errors("tc"), errors("ffma")
     status_ok()
     print("tensor cores vs fp64:", {k: f"{v:.3e}" for k, v in e_tc.items()})
     print("FFMA         vs fp64:", {k: f"{v:.3e}" for k, v in e_ff.items()})

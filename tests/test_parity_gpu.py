@@ -209,12 +209,8 @@ def test_c_abi_direct(cuda):
 def test_no_wait_dq_path_equals_turn_chain(cuda, b, h, s, causal):
     """The FFMA backward's two dQ orderings (the key-block turn chain with the minimal workspace,
     the store-then-last-block-sums path with cfa_bwd_workspace_bytes_fast) give the same bits (the
-    FFMA pair selected: by default the larger workspace takes the tensor-core backward)."""
-    prev = _abi.fwd_select(_abi.FWD_FFMA)
-    try:
-        _no_wait_vs_turn_chain(cuda, b, h, s, causal)
-    finally:
-        _abi.fwd_select(prev)
+    CUDA-core pair's entry points)."""
+    _no_wait_vs_turn_chain(cuda, b, h, s, causal, "ffma")
 
 
 @pytest.mark.parametrize("b,h,s,causal", [(64, 6, 240, False), (3, 2, 200, True),
@@ -224,11 +220,7 @@ def test_tc_no_wait_dq_path_equals_turn_chain(cuda, b, h, s, causal):
     """The tensor-core backward's two dQ orderings -- the key-block turn chain (the minimal
     workspace; the only one past s = 1024) and the partials summed by the last block
     (cfa_bwd_workspace_bytes_fast) -- give the same bits."""
-    prev = _abi.fwd_select(_abi.FWD_TC)
-    try:
-        _no_wait_vs_turn_chain(cuda, b, h, s, causal)
-    finally:
-        _abi.fwd_select(prev)
+    _no_wait_vs_turn_chain(cuda, b, h, s, causal, "tc")
 
 
 @pytest.mark.parametrize("s,causal", [(2048, True), (1536, False)])
@@ -250,7 +242,9 @@ def test_tc_pair_long_sequences(cuda, s, causal):
     assert torch.equal(o, o2) and torch.equal(g, g2)
 
 
-def _no_wait_vs_turn_chain(cuda, b, h, s, causal):
+def _no_wait_vs_turn_chain(cuda, b, h, s, causal, pair):
+    fwd = {"tc": _abi.fwd, "ffma": _abi.fwd_ffma}[pair]
+    bwd = {"tc": _abi.bwd, "ffma": _abi.bwd_ffma}[pair]
     qkv, dout = oracle.seeded_inputs(b, h, s, 4)
     x, g = qkv.to(cuda), dout.to(cuda)
     st, gst = (x.stride(0), 64, x.stride(1)), (g.stride(0), 64, g.stride(1))
@@ -259,15 +253,15 @@ def _no_wait_vs_turn_chain(cuda, b, h, s, causal):
     o = torch.empty(b, s, h, 64, device=cuda)
     lse = torch.empty(b, h, s, device=cuda)
     stream = torch.cuda.current_stream().cuda_stream
-    assert _abi.fwd(ptrs[0], st, ptrs[1], st, ptrs[2], st, o.data_ptr(), lse.data_ptr(), b, h, s,
-                    64, 0.125, causal, stream) == _abi.CFA_OK
+    assert fwd(ptrs[0], st, ptrs[1], st, ptrs[2], st, o.data_ptr(), lse.data_ptr(), b, h, s,
+               64, 0.125, causal, stream) == _abi.CFA_OK
     out = []
     for nbytes in (_abi.bwd_workspace_bytes(b, h, s), _abi.bwd_workspace_bytes_fast(b, h, s)):
         ws = torch.empty(nbytes, dtype=torch.uint8, device=cuda)
         dqkv = torch.full((b, s, 3, h, 64), float("nan"), device=cuda)
-        assert _abi.bwd(ptrs[0], st, ptrs[1], st, ptrs[2], st, o.data_ptr(), lse.data_ptr(),
-                        g.data_ptr(), gst, dqkv.data_ptr(), ws.data_ptr(), nbytes, b, h, s, 64,
-                        0.125, causal, stream) == _abi.CFA_OK
+        assert bwd(ptrs[0], st, ptrs[1], st, ptrs[2], st, o.data_ptr(), lse.data_ptr(),
+                   g.data_ptr(), gst, dqkv.data_ptr(), ws.data_ptr(), nbytes, b, h, s, 64,
+                   0.125, causal, stream) == _abi.CFA_OK
         assert _abi.bwd_status(ws.data_ptr(), stream) == _abi.CFA_OK
         out.append(dqkv)
     assert _abi.bwd_workspace_bytes_fast(b, h, s) > _abi.bwd_workspace_bytes(b, h, s)

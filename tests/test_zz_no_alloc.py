@@ -62,14 +62,17 @@ def _noalloc_backward(b, h, s, causal, g, st, gst, ptrs, o, lse, stream, dev):
     return dqkv
 
 
+# (3, 2, 150) and (2, 3, 257) fit their dQ partials into the static scratch (the no-wait dQ path);
+# (64, 6, 240) and (32, 6, 240, causal) do not, and run the key-block turn chain through it.
 @pytest.mark.parametrize("shape,causal", [((3, 2, 150), False), ((2, 3, 257), True),
-                                          ((64, 6, 240), False)])
+                                          ((64, 6, 240), False), ((32, 6, 240), True)])
 def test_noalloc_matches_workspace_backward_twice(cuda, shape, causal):
     b, h, s = shape
     x, g, st, gst, ptrs, o, lse, stream = _setup(b, h, s, causal, 5, cuda)
     want = _reference_backward(b, h, s, causal, x, g, st, gst, ptrs, o, lse, stream, cuda)
     for call in range(2):
         got = _noalloc_backward(b, h, s, causal, g, st, gst, ptrs, o, lse, stream, cuda)
+        assert _abi.bwd_noalloc_status(stream) == _abi.CFA_OK, f"call {call}"
         assert torch.isfinite(got).all(), f"call {call}"
         assert (got - want).abs().max().item() < BAND, f"call {call}"
         assert torch.equal(got.view(torch.int32), want.view(torch.int32)), f"call {call}"
@@ -83,3 +86,8 @@ def test_noalloc_rejects_problems_past_the_static_scratch(cuda):
     rc = _abi.bwd_noalloc(fake, s3, fake, s3, fake, s3, fake, fake, fake, s3, fake, b, h, s, 64,
                           0.125, 0, None)
     assert rc == _abi.CFA_ERR_WORKSPACE
+    # the other argument errors keep their own codes
+    assert _abi.bwd_noalloc(fake, s3, fake, s3, fake, s3, fake, fake, fake, s3, fake, b, h, s, 32,
+                            0.125, 0, None) == _abi.CFA_ERR_HEAD_DIM
+    assert _abi.bwd_noalloc(None, s3, fake, s3, fake, s3, fake, fake, fake, s3, fake, 1, 1, 64, 64,
+                            0.125, 0, None) == _abi.CFA_ERR_NULL
