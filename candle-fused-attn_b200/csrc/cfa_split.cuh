@@ -25,21 +25,45 @@ __device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// x[0..7] -> three 16-byte rows of bf16 parts (packed pairs, the even element low).
+// Packed fp32 pairs (a 64-bit register pair, the first value low) and the sm_100 packed
+// arithmetic on them: one instruction per pair where a scalar form takes two.
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// The round-to-nearest bf16 pair of a float pair (the low value in the low half).
+__device__ __forceinline__ uint32_t to_bf2(uint64_t v) {
+  float lo, hi;
+  unpack2(v, lo, hi);
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+// The float pair a bf16 pair stands for (exact: a bf16 is the high half of its float).
+__device__ __forceinline__ uint64_t from_bf2(uint32_t h) {
+  return pack2(__uint_as_float(h << 16), __uint_as_float(h & 0xffff0000u));
+}
+
+// x[0..7] -> three 16-byte rows of bf16 parts (packed pairs, the even element low). Per pair:
+// x0 = RN(x), x1 = RN(x - x0), x2 = RN(x - x0 - x1); both subtractions are exact.
 __device__ __forceinline__ void split8(const float (&x)[8], uint4& p0, uint4& p1, uint4& p2) {
   uint32_t a[4], b[4], c[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float x0 = x[2 * i], x1 = x[2 * i + 1];
-    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-    const float2 hf = __bfloat1622float2(h);
-    const float r0 = x0 - hf.x, r1 = x1 - hf.y;  // exact
-    const __nv_bfloat162 m = __floats2bfloat162_rn(r0, r1);
-    const float2 mf = __bfloat1622float2(m);
-    const __nv_bfloat162 l = __floats2bfloat162_rn(r0 - mf.x, r1 - mf.y);  // exact differences
-    a[i] = bf2_bits(h);
-    b[i] = bf2_bits(m);
-    c[i] = bf2_bits(l);
+    const uint64_t v = pack2(x[2 * i], x[2 * i + 1]);
+    a[i] = to_bf2(v);
+    const uint64_t r = sub2(v, from_bf2(a[i]));
+    b[i] = to_bf2(r);
+    c[i] = to_bf2(sub2(r, from_bf2(b[i])));
   }
   p0 = make_uint4(a[0], a[1], a[2], a[3]);
   p1 = make_uint4(b[0], b[1], b[2], b[3]);

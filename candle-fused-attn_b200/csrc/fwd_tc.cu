@@ -17,26 +17,40 @@
 // sequential-FFMA fp32 on every output of the forward and backward, level with separate
 // accumulators for A0B0 and the small products at half the TMEM.
 //
-// Block: 16 softmax warps and one MMA warp own TC_BM = 128 queries of one (batch, head). Softmax
-// thread (warp w < 16, lane l) owns query row 32 (w % 4) + l -- its TMEM lane -- and the 16
-// columns (keys of S, dims of O) of group w / 4; warp 16 issues every MMA. The A operands live in
-// TMEM -- Q's parts (stored once) for S = Q K^T, P's parts for O = P V -- so an MMA reads only its
-// B operand (2 KB) from shared memory and runs at the tensor rate (with both operands in shared
-// memory, 6 KB per M128 N64 K16 MMA at 128 B per clock made it 1.5x slower). Per key tile of 64
-// the softmax threads read S from TMEM, run the online softmax (row max of the four column groups
-// through shared memory), put P's parts into TMEM and split their items of V (transposed: the P V
-// product reads V's rows as an MN-major B operand) and K into shared memory; the MMA warp then issues P V(n) and
-// S(n + 2). S is issued two tiles ahead (two S buffers in TMEM, two K part buffers) and P V(n - 1)
-// is folded into the fp32 O registers one tile late, so the tensor core works while the softmax
-// runs. Every thread copies (cp.async) the fp32 chunks it splits itself, a tile ahead of use.
+// Block: 256 queries of one (batch, head) as two query tiles of 128 (tile t: rows 128 t ..
+// 128 t + 127), 16 softmax warps and one MMA warp. Both tiles read the same K and V parts, so
+// every key tile is split into bf16 parts once per 256 queries. The softmax warps work the tiles
+// in turn -- softmax of tile 0, then of tile 1, per key tile -- and the tensor core computes one
+// tile's P V and next S while the warps run the other tile's softmax (ping-pong): per key tile n,
+//   softmax warps:  S0(n) -> P0(n) | split K(n + 2) | S1(n) -> P1(n) | split V(n + 1)
+//   MMA warp:       P V0(n), then S0(n + 1) | P V1(n), then S1(n + 1)
+// Softmax thread (warp w < 16, lane l) owns query row 32 (w % 4) + l of each tile -- its TMEM lane
+// -- and the 16 columns (keys of S, dims of O) of group w / 4; warp 16 issues every MMA.
+//
+// TMEM (512 columns, lane = query row of the tile). Tile t: Q's parts (the A operand of S = Q K^T,
+// written once; part i, K-step ks at T_Q(t) + 32 i + 8 ks), the S / P region (S in its first 64
+// columns; after the row's softmax, P's parts over it: part i, K-step ks at T_SP(t) + 32 i +
+// 8 ks, the A operand of O = P V) and O (one key tile's P V, folded into registers by the next
+// softmax). S(n + 1) overwrites P(n), so it is issued once P V(n) has completed; the other tile's
+// work keeps the tensor core busy meanwhile. B operands from shared memory: K's parts K-major,
+// V's parts (the same row layout) read MN-major.
+//
+// Staging. Every thread copies (cp.async) exactly the fp32 chunks of K and V it later splits,
+// into slots of its own, so no barrier separates a copy from its split; K(n + 3) and V(n + 2) travel
+// while key tile n runs. Three K part buffers, two V part buffers; mbarriers carry every hand-off
+// (MMA commits; one arrival per softmax warp for P, K and V parts).
 //
 // Every mbarrier wait is bounded (WAIT_TIMEOUT_NS); on expiry the block sets the device error flag
-// (cfa_fwd_status reads it), waits once more, frees its TMEM and returns without writing.
+// (cfa_fwd_status reads it) and the caller's host-visible flag (cfa_error_sink), waits once more
+// for the last commits, frees its TMEM and returns without writing.
 //
 // DETERMINISM: the MMA order is fixed by the code; every register sum has one order: the row
 // max over each group's 16 keys in order, then the groups 0..3; p summed over the group's keys in
-// order, per tile; l = ((l0 + l1) + l2) + l3; O over key tiles in index order.
+// order, per tile; l = ((l0 + l1) + l2) + l3; O over key tiles in index order. A row's arithmetic
+// does not depend on the other rows of its block, so results do not depend on the grid.
 #include <cuda_bf16.h>
+
+#include <type_traits>
 
 #include "cfa_common.cuh"
 #include "cfa_split.cuh"
@@ -54,80 +68,74 @@ __device__ int g_fwd_tc_err = 0;
 
 namespace {
 
-constexpr int TC_BM = 128;      // query rows per block = MMA M = TMEM lanes
-constexpr int TC_BN = 64;       // keys per tile = MMA N of S = MMA K of P V
-constexpr int TC_THREADS = 512;  // the softmax / split threads; one more warp issues the MMAs
-constexpr int TC_BLOCK = TC_THREADS + 32;
-constexpr int NQ = TC_THREADS / 128;  // threads per query row
-constexpr int CW = 64 / NQ;           // columns (keys of S, dims of O) per thread
-constexpr int PART_K = TC_BN * 64 * 2;  // bytes of one bf16 part of a [64][64] operand
-constexpr int TILE_F32 = TC_BN * 64 * 4;  // bytes of one fp32 [64][64] tile
-constexpr int OFF_K = 0;                       // three buffers of K parts, [64 keys][64 d]
-constexpr int OFF_V = OFF_K + 9 * PART_K;      // two buffers of V parts, [64 keys][64 d], rows as K's
-constexpr int OFF_KST = OFF_V + 6 * PART_K;    // fp32 K tile in flight, [64][64]
-constexpr int OFF_VST = OFF_KST + TILE_F32;    // fp32 V tile in flight, [64][64]
-constexpr int LDP = 68;                        // prologue staging: rows of 64 floats, 68 apart
-constexpr int OFF_ROWS = OFF_VST + TILE_F32;   // prologue: fp32 rows of Q, K(0), K(1)
-constexpr int OFF_RED = OFF_ROWS + (TC_BM + 2 * TC_BN) * LDP * 4;  // float [128][NQ]: row max, l
-constexpr int OFF_BAR = OFF_RED + TC_BM * NQ * 4;  // mbarriers S0, S1, O, rows; the TMEM base
-constexpr int TC_SMEM = OFF_BAR + 40;
-constexpr int TC_SMEM_ALLOC = TC_SMEM + 1024;  // room to align the base to 1024 bytes
-// TMEM columns (lane = query row). Q's parts, the A operand of S: part i, K-step ks (16 dims) in
-// the 8 columns T_Q + 32 i + 8 ks. S of two key tiles (T_S, T_S + 64). O. P's parts, the A operand
-// of P V: part i, K-step ks (16 keys) at T_P + 32 i + 8 ks. One block per SM.
-constexpr uint32_t T_Q = 0, T_S = 96, T_O = 224, T_P = 288;
-constexpr uint32_t TMEM_COLS = 512;
+constexpr int QT = 128;          // query rows per tile = MMA M = TMEM lanes
+constexpr int NTILE = 2;         // query tiles per block
+constexpr int BQ = QT * NTILE;   // queries per block
+constexpr int KT = 64;           // keys per key tile = MMA N of S = MMA K of P V
+constexpr int NSM = 512;         // softmax / split threads; one more warp issues the MMAs
+constexpr int NBLK = NSM + 32;
+constexpr int NQ = NSM / QT;     // threads per query row
+constexpr int CW = 64 / NQ;      // columns (keys of S, dims of O) per thread
+constexpr int PART = KT * 64 * 2;   // bytes of one bf16 part of a [64][64] operand
+constexpr int PARTS = 3 * PART;     // the three parts of one operand tile
+constexpr int STG = NSM * 32;       // one staging set: two 16-byte slots per thread
+constexpr int OFF_K = 0;                          // three buffers of K parts, [64 keys][64 d]
+constexpr int OFF_V = OFF_K + 3 * PARTS;          // two buffers of V parts, rows as K's
+constexpr int OFF_KST = OFF_V + 2 * PARTS;        // fp32 K items in flight
+constexpr int OFF_VST = OFF_KST + STG;            // fp32 V items in flight
+constexpr int OFF_RED = OFF_VST + STG;            // float [2][128][NQ]: row maxima per tile
+constexpr int OFF_LRED = OFF_RED + NTILE * QT * NQ * 4;  // float [2][128][NQ]: row sums
+constexpr int OFF_BAR = OFF_LRED + NTILE * QT * NQ * 4;  // mbarriers; the TMEM base
+constexpr int NBAR = 10;  // s[2], o[2], p[2], k[2], v[2]
+constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;
+constexpr int SMEM_ALLOC = SMEM + 1024;  // room to align the base to 1024 bytes
+constexpr int LDO = 68;  // epilogue: O rows of 64 floats, 68 apart (in the K part buffers)
+static_assert(BQ * LDO * 4 <= 3 * PARTS, "the epilogue's O rows fit the K part buffers");
+static_assert(STG <= PARTS, "a K part buffer holds one staging set");
+static_assert(KT * 8 == NSM, "one K (or V) row item per thread per key tile");
+static_assert(SMEM_ALLOC <= 232448, "shared memory per block");
 
-// Staging. Every thread copies (cp.async) exactly the fp32 chunks it later splits, into slots of
-// its own, so no barrier separates a copy from its split: a row item (r, kc) -- row r, elements
-// 8 kc .. 8 kc + 7 of K or V -- as two 16-byte copies. Slot j of thread t sits at
-// (j * TC_THREADS + t) * 16 bytes: a warp's copies and reads of one slot are consecutive.
-// Row items: item c takes row 8 (c / 64) + c % 8 and chunk (c / 8) % 8, so a quarter-warp's parts
-// land in 8 different bank groups of the core-matrix layout and a warp reads 4 x 32 bytes of each
-// of 8 rows.
+__host__ __device__ constexpr uint32_t T_Q(int t) { return 96u * t; }
+__host__ __device__ constexpr uint32_t T_SP(int t) { return 192u + 96u * t; }
+__host__ __device__ constexpr uint32_t T_O(int t) { return 384u + 64u * t; }
+constexpr uint32_t TMEM_COLS = 512;
+static_assert(T_O(1) + 64 == TMEM_COLS, "TMEM budget");
+
+// Row items: item c takes row 8 (c / 64) + c % 8 and chunk (c / 8) % 8 (elements 8 chunk ..
+// 8 chunk + 7), so a quarter-warp's parts land in 8 different bank groups of the core-matrix
+// layout and a warp reads 4 x 32 bytes of each of 8 rows. Slot j of thread t sits at
+// (j * NSM + t) * 16 bytes: a warp's copies and reads of one slot are consecutive.
 __device__ __forceinline__ void row_item(int c, int& r, int& kc) {
   r = 8 * (c >> 6) + (c & 7);
   kc = (c >> 3) & 7;
 }
 
-// Row item c of the prologue's row-major staging (rows LDP floats apart; rows >= valid read as
-// zeros) into K-major parts.
-__device__ __forceinline__ void split_staged_row(unsigned char* parts, const float* rows, int c,
-                                                 int valid) {
+// Copy this thread's row item of a strided [seq, 64] operand, rows from r0 (rows past the end
+// are zero-filled: source size 0, address clamped to row 0).
+__device__ __forceinline__ void stage_item(unsigned char* st, const float* src, int64_t stride,
+                                           int r0, int seq) {
   int r, kc;
-  row_item(c, r, kc);
-  float x[8];
-  if (r < valid) {
-    const float4 u = reinterpret_cast<const float4*>(rows + r * LDP + 8 * kc)[0];
-    const float4 v = reinterpret_cast<const float4*>(rows + r * LDP + 8 * kc)[1];
-    x[0] = u.x, x[1] = u.y, x[2] = u.z, x[3] = u.w, x[4] = v.x, x[5] = v.y, x[6] = v.z, x[7] = v.w;
-  } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) x[i] = 0.0f;
-  }
-  store_parts(parts, PART_K, kmaj_off(r, kc), x);
-}
-
-// Copy row item c (slot base `slot`, two 16-byte slots) of a strided operand, rows from r0.
-__device__ __forceinline__ void stage_row_item(unsigned char* st, int slot, int c, const float* src,
-                                               int64_t stride, int r0, int seq) {
-  int r, kc;
-  row_item(c, r, kc);
+  row_item(threadIdx.x, r, kc);
   const bool ok = r0 + r < seq;
   const float* g = src + static_cast<int64_t>(ok ? r0 + r : 0) * stride + 8 * kc;
-  cp_async16(st + 16 * ((2 * slot) * TC_THREADS + threadIdx.x), g, ok ? 16 : 0);
-  cp_async16(st + 16 * ((2 * slot + 1) * TC_THREADS + threadIdx.x), g + 4, ok ? 16 : 0);
+  cp_async16(st + 16 * threadIdx.x, g, ok ? 16 : 0);
+  cp_async16(st + 16 * (NSM + threadIdx.x), g + 4, ok ? 16 : 0);
 }
 
-__device__ __forceinline__ void split_row_item(unsigned char* parts, int part_bytes,
-                                               const unsigned char* st, int slot, int c) {
+// This thread's staged row item into the K-major parts of one operand tile.
+__device__ __forceinline__ void split_item(unsigned char* parts, const unsigned char* st) {
   int r, kc;
-  row_item(c, r, kc);
-  const float4 u = *reinterpret_cast<const float4*>(st + 16 * ((2 * slot) * TC_THREADS + threadIdx.x));
-  const float4 v =
-      *reinterpret_cast<const float4*>(st + 16 * ((2 * slot + 1) * TC_THREADS + threadIdx.x));
+  row_item(threadIdx.x, r, kc);
+  const float4 u = *reinterpret_cast<const float4*>(st + 16 * threadIdx.x);
+  const float4 v = *reinterpret_cast<const float4*>(st + 16 * (NSM + threadIdx.x));
   const float x[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
-  store_parts(parts, part_bytes, kmaj_off(r, kc), x);
+  store_parts(parts, PART, kmaj_off(r, kc), x);
+}
+
+// cp.async.wait_group N: every group but the N most recent is complete.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
 // The six (A part, B part) products of K = 64 (four K-steps of 16 bf16) into one accumulator `d`,
@@ -152,291 +160,385 @@ __device__ __forceinline__ void issue_split_mma(uint32_t d, uint32_t a_tmem, uin
 #pragma unroll
     for (int p = 1; p < 6; ++p)
       tc::mma_bf16_tmem_a_warp(d, a_tmem + 32 * PA[p] + 8 * ks,
-                               blo + ((PB[p] * PART_K + STEP * ks) >> 4), bd.hi, id,
+                               blo + ((PB[p] * PART + STEP * ks) >> 4), bd.hi, id,
                                ks > 0 || p > 1);
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks)
     tc::mma_bf16_tmem_a_warp(d, a_tmem + 8 * ks, blo + ((STEP * ks) >> 4), bd.hi, id, 1);
 }
 
-// Named barriers: 2 = the softmax threads plus the MMA warp (TC_BLOCK); 3 + q = the four softmax
-// warps of TMEM lane quarter q (w & 3 == q), which hold the same rows and exchange their row maxima.
-// Every participant syncs (none only arrives), so no group can run a phase ahead of another even
-// when a bounded wait has expired.
+// Named barriers 3 + q: the four softmax warps of TMEM lane quarter q (w % 4 == q), which hold
+// the same rows and exchange their row maxima. Every participant syncs, so no warp can run a
+// phase ahead of another even when a bounded wait has expired.
 __device__ __forceinline__ void bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-// CW = 16 consecutive fp32 columns of this thread's TMEM lane.
+// The limit of a thread's next mbarrier wait: WAIT_TIMEOUT_NS, or 1 ms once one of its waits has
+// expired (the results are invalid by then; the block only has to reach its end quickly, every
+// thread still keeping to the same arrivals and barriers).
+__device__ __forceinline__ uint64_t wait_ns(bool expired) {
+  return expired ? 1000000ull : WAIT_TIMEOUT_NS;
+}
+
+// Packed fp32 pairs (tc::pack2 / unpack2): products, sums and the O fold one instruction a pair.
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// (x, y) = (x, y) * a + b, one rounding per lane.
+__device__ __forceinline__ void fma2x(float& x, float& y, uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(tc::pack2(x, y)), "l"(a), "l"(b));
+  tc::unpack2(d, x, y);
+}
+constexpr float LOG2E = 1.4426950408889634f;  // log2(e), rounded to fp32
+
+// max(a, b, c) in one instruction (sm_100).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __device__ __forceinline__ void tmem_ld1(uint32_t taddr, float (&u)[CW]) {
   static_assert(CW == 16, "one 16-column load per accumulator");
   tc::tmem_ld16(taddr, u);
   tc::tmem_wait_ld();
 }
 
+// The online-softmax state of one thread for one query tile: its 16 columns of O (unnormalised),
+// the row maximum m of the scaled scores, its share of the row sum, and the last tile's rescale
+// factor.
+struct RowState {
+  float acc[CW];
+  float m, lpart, alpha_prev;
+};
+
 template <bool CAUSAL>
-__global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
+__global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = tc::smem_u32(smem_raw);
   unsigned char* sm = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  unsigned char* Kp = sm + OFF_K;
   unsigned char* Vp = sm + OFF_V;
   unsigned char* Kst = sm + OFF_KST;
   unsigned char* Vst = sm + OFF_VST;
   float* red = reinterpret_cast<float*>(sm + OFF_RED);
-  uint64_t* bar_s = reinterpret_cast<uint64_t*>(sm + OFF_BAR);  // [2]
-  uint64_t* bar_o = bar_s + 2;
-  uint64_t* bar_ld = bar_s + 3;  // the prologue's bulk row copies
-  uint32_t* tbase_p = reinterpret_cast<uint32_t*>(bar_s + 4);
+  float* lred = reinterpret_cast<float*>(sm + OFF_LRED);
+  uint64_t* bar_s = reinterpret_cast<uint64_t*>(sm + OFF_BAR);  // [2]: S(t) committed
+  uint64_t* bar_o = bar_s + 2;  // [2]: P V(t) committed
+  uint64_t* bar_p = bar_s + 4;  // [2]: P(t)'s parts in TMEM (one arrival per softmax warp)
+  uint64_t* bar_k = bar_s + 6;  // [2]: K(j)'s parts in place, j >= 2, by j % 2 (same)
+  uint64_t* bar_v = bar_s + 8;  // [2]: V(j)'s parts in place, j >= 1, by j % 2 (same)
+  uint32_t* tbase_p = reinterpret_cast<uint32_t*>(bar_s + NBAR);
 
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
-  const int row = 32 * (w & 3) + lane;  // TMEM lane
-  const int cq = w >> 2;                // columns (keys of S, dims of O) CW cq .. CW cq + CW - 1
+  const bool mma_warp = w == NSM / 32;  // warp 16: issues every MMA, nothing else
+  const int row = 32 * (w & 3) + lane;  // TMEM lane: query row of each tile
+  const int cq = w >> 2;                // columns CW cq .. CW cq + CW - 1
   const int BH = a.B * a.H;
-  int qt, bh;
+  int qb, bh;
   if (CAUSAL) {
-    qt = a.n_qtiles - 1 - static_cast<int>(blockIdx.x / BH);  // longest tiles first
+    qb = a.n_qtiles - 1 - static_cast<int>(blockIdx.x / BH);  // longest blocks first
     bh = static_cast<int>(blockIdx.x % BH);
   } else {
-    qt = static_cast<int>(blockIdx.x % a.n_qtiles);
+    qb = static_cast<int>(blockIdx.x % a.n_qtiles);
     bh = static_cast<int>(blockIdx.x / a.n_qtiles);
   }
   const int b = bh / a.H, h = bh % a.H;
-  const int q0 = qt * TC_BM;
+  const int q0 = qb * BQ;
   const int S = a.S;
   const float* qp = a.q + b * a.q_sb + h * a.q_sh;
   const float* kp = a.k + b * a.k_sb + h * a.k_sh;
   const float* vp = a.v + b * a.v_sb + h * a.v_sh;
-  const int k_end = CAUSAL ? min(S, q0 + TC_BM) : S;
-  const int T = (k_end + TC_BN - 1) / TC_BN;  // key tiles, >= 1
-  bool err0 = false;
+  // Key tiles of each query tile (0: the tile lies past the sequence), and of the block.
+  int Tt[NTILE];
+#pragma unroll
+  for (int t = 0; t < NTILE; ++t) {
+    const int r0 = q0 + QT * t;
+    const int k_end = CAUSAL ? min(S, r0 + QT) : S;
+    Tt[t] = r0 < S ? (k_end + KT - 1) / KT : 0;
+  }
+  const int T0 = Tt[0], T1 = Tt[1];
+  const int T = max(T0, T1);  // >= 1
 
   if (tid == 0) {
-    tc::mbar_init(bar_s, 1);
-    tc::mbar_init(bar_s + 1, 1);
-    tc::mbar_init(bar_o, 1);
-    tc::mbar_init(bar_ld, 1);
+#pragma unroll
+    for (int i = 0; i < NBAR; ++i) tc::mbar_init(bar_s + i, i < 4 ? 1 : NSM / 32);
     tc::fence_mbar_init();
-    tc::mbar_arrive_expect_tx(bar_ld, 256u * (min(TC_BM, S - q0) + min(TC_BN, S) +
-                                              (T > 1 ? min(TC_BN, S - TC_BN) : 0)));
   }
-
   griddep_wait();  // q, k, v may come from the previous kernel on the stream
   griddep_launch_dependents();
-
-  // Schedule. Tile n's softmax runs while the tensor core computes P V(n - 1) and S(n + 1): S is
-  // issued two tiles ahead (two S buffers in TMEM, three K part buffers), and P V(n - 1) is folded
-  // into O one tile late. Per tile n: (a) S(n) -> softmax -> p in registers; (b) P V(n - 1) -> O;
-  // (c) p into P's parts; barrier; (d) issue P V(n) and S(n + 2); (e) this thread's items of
-  // V(n + 1) and K(n + 3) into their parts (two V buffers, three K buffers: both released) while
-  // S(n + 1) completes, then stage V(n + 2), K(n + 4).
-  static_assert(TC_BM * 8 == 2 * TC_THREADS && TC_BN * 8 == TC_THREADS, "items per thread");
-  const bool mma_warp = w == TC_THREADS / 32;  // warp 16: issues every MMA, nothing else
-  // Prologue: the rows of Q, K(0), K(1) travel as one bulk copy each (threads 0-255, one row
-  // apiece) into row-major staging (rows past the sequence are not copied and read as zeros),
-  // K(2) and V(0) by cp.async; K(0..2), V(0) split into their parts; Q (this thread's row and 16
-  // dims: K-step cq of S's A operand) into TMEM; S(0), S(1) issued; V(1), K(3) in flight.
-  float* q_rows = reinterpret_cast<float*>(sm + OFF_ROWS);
-  float* k_rows = q_rows + TC_BM * LDP;
-  const int nq = min(TC_BM, S - q0), nk0 = min(TC_BN, S), nk1 = T > 1 ? min(TC_BN, S - TC_BN) : 0;
   __syncthreads();  // the mbarriers' initialisation
-  if (mma_warp) {  // TMEM, by the warp that is idle while the rows travel (it also frees it)
+  if (mma_warp) {  // TMEM, by the warp that issues the MMAs (it also frees it)
     tc::tmem_alloc(tbase_p, TMEM_COLS);
     tc::tmem_relinquish();
   }
-  float qx[CW];
+
+  // Prologue: K(0), K(1), V(0) into their parts (K(1) staged in K part buffer 2, free until the
+  // first loop step), Q of both tiles (this thread's row and 16 dims: K-step cq of S's A operand)
+  // into TMEM; K(2), V(1) left in flight. Then the MMA warp issues S0(0) and S1(0).
+  float qx[NTILE][CW];
   if (!mma_warp) {
-    if (tid < TC_BM) {
-      if (tid < nq)
-        tc::bulk_load(q_rows + tid * LDP, qp + static_cast<int64_t>(q0 + tid) * a.q_ss, 256, bar_ld);
-    } else if (tid < TC_BM + 2 * TC_BN) {
-      const int r = tid - TC_BM;  // key row 0 .. 127 of K(0), K(1)
-      if (r < (r < TC_BN ? nk0 : TC_BN + nk1))
-        tc::bulk_load(k_rows + r * LDP, kp + static_cast<int64_t>(r) * a.k_ss, 256, bar_ld);
-    }
-    if (T > 2) stage_row_item(Kst, 0, tid, kp, a.k_ss, 2 * TC_BN, S);
-    stage_row_item(Vst, 0, tid, vp, a.v_ss, 0, S);
-    cp_async_commit();
-    err0 = !tc::mbar_wait(bar_ld, 0, WAIT_TIMEOUT_NS);
-    cp_async_wait_all();
-    split_staged_row(sm + OFF_K, k_rows, tid, nk0);
-    if (T > 1) split_staged_row(sm + OFF_K + 3 * PART_K, k_rows + TC_BN * LDP, tid, nk1);
-    if (T > 2) split_row_item(sm + OFF_K + 6 * PART_K, PART_K, Kst, 0, tid);
-    split_row_item(Vp, PART_K, Vst, 0, tid);
-    if (T > 1) stage_row_item(Vst, 0, tid, vp, a.v_ss, TC_BN, S);
-    if (T > 3) stage_row_item(Kst, 0, tid, kp, a.k_ss, 3 * TC_BN, S);
+    stage_item(Kst, kp, a.k_ss, 0, S);
+    if (T > 1) stage_item(Kp + 2 * PARTS, kp, a.k_ss, KT, S);
+    stage_item(Vst, vp, a.v_ss, 0, S);
     cp_async_commit();
 #pragma unroll
-    for (int c4 = 0; c4 < CW / 4; ++c4) {
-      const float4 u = row < nq ? reinterpret_cast<const float4*>(q_rows + row * LDP + CW * cq)[c4]
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-      qx[4 * c4] = u.x;
-      qx[4 * c4 + 1] = u.y;
-      qx[4 * c4 + 2] = u.z;
-      qx[4 * c4 + 3] = u.w;
+    for (int t = 0; t < NTILE; ++t) {
+      const int qi = q0 + QT * t + row;
+      const float4* src = reinterpret_cast<const float4*>(qp + static_cast<int64_t>(qi) * a.q_ss + CW * cq);
+#pragma unroll
+      for (int c4 = 0; c4 < CW / 4; ++c4) {
+        const float4 u = qi < S ? __ldg(src + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        qx[t][4 * c4] = u.x;
+        qx[t][4 * c4 + 1] = u.y;
+        qx[t][4 * c4 + 2] = u.z;
+        qx[t][4 * c4 + 3] = u.w;
+      }
     }
-    tc::fence_async_smem();
   }
   tc::fence_before_sync();
-  __syncthreads();
+  __syncthreads();  // the TMEM base
   tc::fence_after_sync();
   const uint32_t tbase = *tbase_p;
   const uint32_t lane_sel = static_cast<uint32_t>(32 * (w & 3)) << 16;
-  const uint32_t t_o = tbase + T_O;
   if (!mma_warp) {
-    uint32_t qparts[3][8];
-    split16(qx, qparts);
 #pragma unroll
-    for (int i = 0; i < 3; ++i) tmem_st8(tbase + lane_sel + T_Q + 32 * i + 8 * cq, qparts[i]);
+    for (int t = 0; t < NTILE; ++t) {
+      uint32_t qparts[3][8];
+      split16(qx[t], qparts);
+#pragma unroll
+      for (int i = 0; i < 3; ++i) tmem_st8(tbase + lane_sel + T_Q(t) + 32 * i + 8 * cq, qparts[i]);
+    }
     tc::tmem_wait_st();
+    cp_async_wait_all();
+    split_item(Kp, Kst);
+    if (T > 1) split_item(Kp + PARTS, Kp + 2 * PARTS);
+    split_item(Vp, Vst);
+    tc::fence_async_smem();
+    // In flight during key tile 0: K(2), then V(1) (two cp.async groups, in that order).
+    if (T > 2) stage_item(Kst, kp, a.k_ss, 2 * KT, S);
+    cp_async_commit();
+    if (T > 1) stage_item(Vst, vp, a.v_ss, KT, S);
+    cp_async_commit();
   }
   tc::fence_before_sync();
-  __syncthreads();
+  __syncthreads();  // K(0), K(1), V(0) parts and Q in place; K part buffer 2 free
   tc::fence_after_sync();
-  bool err = err0;
+  bool err = false;
 
   if (mma_warp) {
-    // S(0), S(1); then per tile, once its P, V and K(n + 2) parts are in place: P V(n), S(n + 2).
-    const uint32_t idesc = tc::idesc_f32acc(1, TC_BM, TC_BN);
-    const uint32_t sV = tc::smem_u32(Vp), sK0 = tc::smem_u32(sm + OFF_K);
+    // Per key tile n and tile t: once P(t, n) is in TMEM (and V(n) in place), P V(t, n); once that
+    // has completed -- S(t, n + 1) overwrites P(t, n) -- and K(n + 1) is in place, S(t, n + 1).
     // The whole warp runs the issue code (warp-uniform operands); one elected lane issues.
-    issue_split_mma<false>(tbase + T_S, tbase + T_Q, sK0, idesc);
-    tc::commit_warp(bar_s);
-    if (T > 1) {
-      issue_split_mma<false>(tbase + T_S + 64, tbase + T_Q, sK0 + 3 * PART_K, idesc);
-      tc::commit_warp(bar_s + 1);
-    }
+    const uint32_t idesc = tc::idesc_f32acc(1, QT, KT);
+    const uint32_t sK = tc::smem_u32(Kp), sV = tc::smem_u32(Vp);
+#pragma unroll
+    for (int t = 0; t < NTILE; ++t)
+      if (Tt[t] > 0) {
+        issue_split_mma<false>(tbase + T_SP(t), tbase + T_Q(t), sK, idesc);
+        tc::commit_warp(bar_s + t);
+      }
     for (int n = 0; n < T; ++n) {
-      bar_sync(2, TC_BLOCK);
-      tc::fence_after_sync();
-      const int j = n & 1;
-      issue_split_mma<true>(t_o, tbase + T_P, sV + 3 * PART_K * j, idesc);
-      tc::commit_warp(bar_o);
-      if (n + 2 < T) {
-        issue_split_mma<false>(tbase + T_S + 64 * j, tbase + T_Q, sK0 + 3 * PART_K * ((n + 2) % 3),
-                               idesc);
-        tc::commit_warp(bar_s + j);
+      bool v_ready = n == 0, k_ready = n + 1 < 2;
+#pragma unroll
+      for (int t = 0; t < NTILE; ++t) {
+        if (n >= Tt[t]) continue;
+        err |= !tc::mbar_wait(bar_p + t, n & 1, wait_ns(err));
+        if (!v_ready) {  // V(n), n >= 1: completion (n - 1) / 2 of bar_v[n % 2]
+          err |= !tc::mbar_wait(bar_v + (n & 1), ((n - 1) >> 1) & 1, wait_ns(err));
+          v_ready = true;
+        }
+        tc::fence_after_sync();
+        issue_split_mma<true>(tbase + T_O(t), tbase + T_SP(t), sV + PARTS * (n & 1), idesc);
+        tc::commit_warp(bar_o + t);
+        if (n + 1 < Tt[t]) {
+          err |= !tc::mbar_wait(bar_o + t, n & 1, wait_ns(err));
+          if (!k_ready) {  // K(n + 1), n + 1 >= 2: completion (n - 1) / 2 of bar_k[(n + 1) % 2]
+            err |= !tc::mbar_wait(bar_k + ((n + 1) & 1), ((n - 1) >> 1) & 1, wait_ns(err));
+            k_ready = true;
+          }
+          tc::fence_after_sync();
+          issue_split_mma<false>(tbase + T_SP(t), tbase + T_Q(t), sK + PARTS * ((n + 1) % 3),
+                                 idesc);
+          tc::commit_warp(bar_s + t);
+        }
       }
     }
   }
 
-  // The block one wave later (blockIdx + a.wave_ctas) starts by reading its 128 Q rows and the
-  // first 128 K rows and 64 V rows of its (batch, head), all at once across the wave: pull them
-  // into L2 while this wave computes (one 256-byte row per thread).
+  // The block one wave later (blockIdx + a.wave_ctas) starts by reading its 256 Q rows and the
+  // first 128 K rows and 64 V rows of its (batch, head): pull them into L2 while this wave
+  // computes (one 256-byte row per thread).
   auto prefetch_next_wave = [&]() {
     const int nb = static_cast<int>(blockIdx.x) + a.wave_ctas;
-    if (a.wave_ctas <= 0 || nb >= static_cast<int>(gridDim.x) || tid >= 2 * TC_BM + TC_BN) return;
-    int nqt, nbh;
+    if (a.wave_ctas <= 0 || nb >= static_cast<int>(gridDim.x) || tid >= BQ + 2 * KT + KT) return;
+    int nqb, nbh;
     if (CAUSAL) {
-      nqt = a.n_qtiles - 1 - nb / BH;
+      nqb = a.n_qtiles - 1 - nb / BH;
       nbh = nb % BH;
     } else {
-      nqt = nb % a.n_qtiles;
+      nqb = nb % a.n_qtiles;
       nbh = nb / a.n_qtiles;
     }
     const int nb_b = nbh / a.H, nb_h = nbh % a.H;
     const float* src;
     int r;
-    if (tid < TC_BM) {
-      r = nqt * TC_BM + tid;
+    if (tid < BQ) {
+      r = nqb * BQ + tid;
       src = a.q + nb_b * a.q_sb + nb_h * a.q_sh + static_cast<int64_t>(r) * a.q_ss;
-    } else if (tid < 2 * TC_BM) {
-      r = tid - TC_BM;
+    } else if (tid < BQ + 2 * KT) {
+      r = tid - BQ;
       src = a.k + nb_b * a.k_sb + nb_h * a.k_sh + static_cast<int64_t>(r) * a.k_ss;
     } else {
-      r = tid - 2 * TC_BM;
+      r = tid - BQ - 2 * KT;
       src = a.v + nb_b * a.v_sb + nb_h * a.v_sh + static_cast<int64_t>(r) * a.v_ss;
     }
     if (r < S) asm volatile("cp.async.bulk.prefetch.L2.global [%0], 256;" ::"l"(src) : "memory");
   };
 
-  // Online-softmax state of this thread's columns: acc holds O[row][CW cq + c] (unnormalised).
-  float m = -INFINITY, lpart = 0.0f, alpha_prev = 1.0f;
-  float acc[CW];
+  const uint64_t sc2 = tc::pack2(a.scale, a.scale);
+  const uint64_t l2e2 = tc::pack2(LOG2E, LOG2E);
+  RowState st[NTILE];
 #pragma unroll
-  for (int c = 0; c < CW; ++c) acc[c] = 0.0f;
-  const int qi = q0 + row;
-  float sv[CW];
+  for (int t = 0; t < NTILE; ++t) {
+    st[t].m = -INFINITY;
+    st[t].lpart = 0.0f;
+    st[t].alpha_prev = 1.0f;
+#pragma unroll
+    for (int c = 0; c < CW; ++c) st[t].acc[c] = 0.0f;
+  }
 
-  // Every softmax thread waits for every commit itself; an expired wait is remembered (the outputs
-  // are then invalid) and the block runs on, so all threads keep to the same barriers.
-  for (int n = 0; n < T && !mma_warp; ++n) {
-    const int k0 = n * TC_BN, j = n & 1;
-    // (a) S(n) from TMEM; the online softmax.
-    err |= !tc::mbar_wait(bar_s + j, (n >> 1) & 1, WAIT_TIMEOUT_NS);
-    tc::fence_after_sync();
-    tmem_ld1(tbase + T_S + 64 * j + lane_sel + CW * cq, sv);
-    const bool edge = (k0 + TC_BN > S) || (CAUSAL && k0 + TC_BN - 1 > q0);
-    float tmax = -INFINITY;
-#pragma unroll
-    for (int c = 0; c < CW; ++c) {
-      float x = sv[c] * a.scale;
-      if (edge) {
-        const int jj = k0 + CW * cq + c;
-        if (!(jj < S && !(CAUSAL && jj > qi))) x = -INFINITY;
-      }
-      sv[c] = x;
-      tmax = fmaxf(tmax, x);
-    }
-    red[NQ * row + cq] = tmax;
-    bar_sync(3 + (w & 3), 32 * NQ);
-    tmax = red[NQ * row];
-#pragma unroll
-    for (int g = 1; g < NQ; ++g) tmax = fmaxf(tmax, red[NQ * row + g]);
-    const float m_new = fmaxf(m, tmax);
-    const float mu = m_new == -INFINITY ? 0.0f : m_new;  // a fully masked row keeps p = 0
-    const float alpha = expf(m - mu);
-    float psum = 0.0f;
-#pragma unroll
-    for (int c = 0; c < CW; ++c) {
-      sv[c] = expf(sv[c] - mu);
-      psum += sv[c];
-    }
-    lpart = fmaf(lpart, alpha, psum);
-    m = m_new;
-    // (b) O += P V(n - 1).
-    if (n > 0) {
-      err |= !tc::mbar_wait(bar_o, (n - 1) & 1, WAIT_TIMEOUT_NS);
+  // Key tile n of query tile t: fold P V(t, n - 1) into O (it uses the previous tile's rescale
+  // factor only, so it comes first and its TMEM values never share registers with S's), then the
+  // online softmax of S(t, n) into P(t, n)'s parts; for n == Tt[t], only that last fold. Every
+  // softmax thread waits for every commit itself; an expired wait is remembered (the outputs are
+  // then invalid) and the block runs on, so all threads keep to the same barriers.
+  auto softmax_step = [&](auto tile, int n) {
+    constexpr int t = decltype(tile)::value;
+    RowState& rs = st[t];
+    const int Tn = Tt[t];
+    if (n > Tn) return;
+    if (n > 0) {  // O = O * alpha(n - 1) + P V(t, n - 1)
+      err |= !tc::mbar_wait(bar_o + t, (n - 1) & 1, wait_ns(err));
       tc::fence_after_sync();
       float ob[CW];
-      tmem_ld1(t_o + lane_sel + CW * cq, ob);
+      tmem_ld1(tbase + lane_sel + T_O(t) + CW * cq, ob);
+      const uint64_t al2 = tc::pack2(rs.alpha_prev, rs.alpha_prev);
 #pragma unroll
-      for (int c = 0; c < CW; ++c) acc[c] = fmaf(acc[c], alpha_prev, ob[c]);
+      for (int c = 0; c < CW; c += 2)
+        fma2x(rs.acc[c], rs.acc[c + 1], al2, tc::pack2(ob[c], ob[c + 1]));
     }
-    // (c) p into P's parts in TMEM (K-step cq of P V's A operand; P V(n - 1) has read the last
-    // ones); hand the tile to the MMA warp.
-    {
-      uint32_t pparts[3][8];
-      split16(sv, pparts);
+    if (n == Tn) return;
+    const int k0 = n * KT;
+    const int qi = q0 + QT * t + row;
+    float sv[CW];
+    err |= !tc::mbar_wait(bar_s + t, n & 1, wait_ns(err));
+    tc::fence_after_sync();
+    tmem_ld1(tbase + lane_sel + T_SP(t) + CW * cq, sv);
+    // Scaled scores y = s * scale, masked to -inf past the end / diagonal.
 #pragma unroll
-      for (int i = 0; i < 3; ++i) tmem_st8(tbase + lane_sel + T_P + 32 * i + 8 * cq, pparts[i]);
-      tc::tmem_wait_st();
+    for (int c = 0; c < CW; c += 2) {
+      const uint64_t y = mul2(tc::pack2(sv[c], sv[c + 1]), sc2);
+      tc::unpack2(y, sv[c], sv[c + 1]);
     }
-    tc::fence_async_smem();
+    const bool edge = (k0 + KT > S) || (CAUSAL && k0 + KT - 1 > q0 + QT * t);
+    if (edge) {
+#pragma unroll
+      for (int c = 0; c < CW; ++c) {
+        const int jj = k0 + CW * cq + c;
+        if (!(jj < S && !(CAUSAL && jj > qi))) sv[c] = -INFINITY;
+      }
+    }
+    float tmax = max3f(sv[0], sv[1], sv[2]);
+#pragma unroll
+    for (int c = 3; c < CW - 1; c += 2) tmax = max3f(tmax, sv[c], sv[c + 1]);
+    tmax = fmaxf(tmax, sv[CW - 1]);
+    float* rr = red + (t * QT + row) * NQ;
+    rr[cq] = tmax;
+    tc::fence_before_sync();  // every S read of the row done before any thread stores P over it
+    bar_sync(3 + (w & 3), 32 * NQ);
+    tc::fence_after_sync();
+    tmax = max3f(max3f(rs.m, rr[0], rr[1]), rr[2], rr[3]);
+    const float mu = tmax == -INFINITY ? 0.0f : tmax;  // a fully masked row keeps p = 0
+    // e^(y - mu) = 2^((y - mu) log2 e): y - mu is exact where p matters (Sterbenz), one rounding
+    // of the product, then the SFU's 2^x (ex2.approx, max relative error about 2^-22).
+    const float alpha = ex2((rs.m - mu) * LOG2E);
+    const uint64_t mu2 = tc::pack2(mu, mu);
+    uint64_t ps2 = 0;  // (+0, +0)
+#pragma unroll
+    for (int c = 0; c < CW; c += 2) {
+      float lo, hi;
+      tc::unpack2(mul2(tc::sub2(tc::pack2(sv[c], sv[c + 1]), mu2), l2e2), lo, hi);
+      sv[c] = ex2(lo);
+      sv[c + 1] = ex2(hi);
+      ps2 = add2(ps2, tc::pack2(sv[c], sv[c + 1]));
+    }
+    float ps_lo, ps_hi;
+    tc::unpack2(ps2, ps_lo, ps_hi);
+    rs.lpart = fmaf(rs.lpart, alpha, ps_lo + ps_hi);
+    rs.m = tmax;
+    rs.alpha_prev = alpha;
+    // p into P's parts in TMEM (K-step cq of P V's A operand); hand the tile to the MMA warp.
+    uint32_t pparts[3][8];
+    split16(sv, pparts);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) tmem_st8(tbase + lane_sel + T_SP(t) + 32 * i + 8 * cq, pparts[i]);
+    tc::tmem_wait_st();
     tc::fence_before_sync();
-    bar_sync(2, TC_BLOCK);
-    tc::fence_after_sync();
-    if (n == 0) prefetch_next_wave();
-    // (e) While S(n + 1) completes: V(n + 1) into V buffer (n + 1) % 2 (P V(n - 1) has read it) and
-    // K(n + 3) into K buffer n % 3 (S(n) has read it) -- both needed at the next hand-off -- then
-    // the tiles after them travel.
-    cp_async_wait_all();
-    if (n + 1 < T) split_row_item(Vp + 3 * PART_K * ((n + 1) & 1), PART_K, Vst, 0, tid);
-    if (n + 3 < T) split_row_item(sm + OFF_K + 3 * PART_K * (n % 3), PART_K, Kst, 0, tid);
-    tc::fence_async_smem();
-    if (n + 2 < T) stage_row_item(Vst, 0, tid, vp, a.v_ss, (n + 2) * TC_BN, S);
-    if (n + 4 < T) stage_row_item(Kst, 0, tid, kp, a.k_ss, (n + 4) * TC_BN, S);
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(bar_p + t);
+  };
+
+  // K(n + 2) into K buffer (n + 2) % 3 (it held K(n - 1): S(0, n - 1), S(1, n - 1) have completed),
+  // then K(n + 3) travels. It runs after a softmax step that waited for S(t, n) of an active tile:
+  // the MMA warp issued that S after waiting for K(n), so bar_k[n % 2] never completes K(n + 2)
+  // before the MMA warp has seen K(n) complete.
+  auto split_k = [&](int n) {
+    cp_async_wait_group<1>();  // K(n + 2)'s group (V(n + 1)'s, committed after it, may remain)
+    if (n + 2 < T) {
+      split_item(Kp + PARTS * ((n + 2) % 3), Kst);
+      tc::fence_async_smem();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(bar_k + (n & 1));
+    }
+    if (n + 3 < T) stage_item(Kst, kp, a.k_ss, (n + 3) * KT, S);
     cp_async_commit();
-    alpha_prev = alpha;
-  }
+  };
+  // V(n + 1) into V buffer (n + 1) % 2 (it held V(n - 1): both P V(t, n - 1) have completed --
+  // each thread has waited for them in this step's folds), then V(n + 2) travels.
+  auto split_v = [&](int n) {
+    cp_async_wait_group<1>();
+    if (n + 1 < T) {
+      split_item(Vp + PARTS * ((n + 1) & 1), Vst);
+      tc::fence_async_smem();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(bar_v + ((n + 1) & 1));
+    }
+    if (n + 2 < T) stage_item(Vst, vp, a.v_ss, (n + 2) * KT, S);
+    cp_async_commit();
+  };
+
   if (!mma_warp) {
-    // The last tile's P V.
-    err |= !tc::mbar_wait(bar_o, (T - 1) & 1, WAIT_TIMEOUT_NS);
-    tc::fence_after_sync();
-    tmem_ld1(t_o + lane_sel + CW * cq, sv);
-#pragma unroll
-    for (int c = 0; c < CW; ++c) acc[c] = fmaf(acc[c], alpha_prev, sv[c]);
+    for (int n = 0; n <= T; ++n) {
+      softmax_step(std::integral_constant<int, 0>{}, n);
+      if (n == 0) prefetch_next_wave();
+      if (n < T0) split_k(n);  // tile 0 waited for S(0, n)
+      softmax_step(std::integral_constant<int, 1>{}, n);
+      if (n >= T0) split_k(n);  // tile 0 done (causal tail): tile 1 waited for S(1, n)
+      split_v(n);
+    }
     cp_async_wait_all();
-    red[NQ * row + cq] = lpart;
+#pragma unroll
+    for (int t = 0; t < NTILE; ++t) lred[(t * QT + row) * NQ + cq] = st[t].lpart;
   }
   if (__syncthreads_or(err)) {
     // A commit did not arrive in time: flag it, give the tensor core one more bounded wait for
@@ -445,31 +547,37 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
       atomicExch(&g_fwd_tc_err, 1);
       flag_timeout(nullptr, a.sink);
     }
-    tc::mbar_wait(bar_o, (T - 1) & 1, WAIT_TIMEOUT_NS);
-    tc::mbar_wait(bar_s + ((T - 1) & 1), ((T - 1) >> 1) & 1, WAIT_TIMEOUT_NS);
+#pragma unroll
+    for (int t = 0; t < NTILE; ++t)
+      if (Tt[t] > 0) tc::mbar_wait(bar_o + t, (Tt[t] - 1) & 1, WAIT_TIMEOUT_NS);
   } else {
-    // O = acc / l through shared memory (the K and V part buffers: no MMA is left to read them),
-    // rows of LDP floats (a 16-byte rotation per row keeps both passes conflict-free); then every
-    // 16 threads store one whole row of O [b, s, h, 64].
+    // O = acc / l through shared memory (the K part buffers: every MMA has completed), rows of
+    // LDO floats (a 16-byte rotation per row keeps both passes conflict-free); then every 16
+    // threads store one whole row of O [b, s, h, 64].
     float* o_rows = reinterpret_cast<float*>(sm + OFF_K);
-    static_assert(TC_BM * LDP * 4 <= 15 * PART_K, "O rows fit the part buffers");
     if (!mma_warp) {
-      float l = red[NQ * row];
 #pragma unroll
-      for (int g = 1; g < NQ; ++g) l += red[NQ * row + g];
+      for (int t = 0; t < NTILE; ++t) {
+        const float* lr = lred + (t * QT + row) * NQ;
+        float l = lr[0];
 #pragma unroll
-      for (int c4 = 0; c4 < CW / 4; ++c4)
-        reinterpret_cast<float4*>(o_rows + row * LDP + CW * cq)[c4] =
-            make_float4(__fdiv_rn(acc[4 * c4], l), __fdiv_rn(acc[4 * c4 + 1], l),
-                        __fdiv_rn(acc[4 * c4 + 2], l), __fdiv_rn(acc[4 * c4 + 3], l));
-      if (cq == 0 && qi < S) a.lse[static_cast<int64_t>(bh) * S + qi] = m + logf(l);
+        for (int g = 1; g < NQ; ++g) l += lr[g];
+        float* orow = o_rows + (t * QT + row) * LDO + CW * cq;
+#pragma unroll
+        for (int c4 = 0; c4 < CW / 4; ++c4)
+          reinterpret_cast<float4*>(orow)[c4] =
+              make_float4(__fdiv_rn(st[t].acc[4 * c4], l), __fdiv_rn(st[t].acc[4 * c4 + 1], l),
+                          __fdiv_rn(st[t].acc[4 * c4 + 2], l), __fdiv_rn(st[t].acc[4 * c4 + 3], l));
+        const int qi = q0 + QT * t + row;
+        if (cq == 0 && qi < S) a.lse[static_cast<int64_t>(bh) * S + qi] = st[t].m + logf(l);
+      }
     }
     __syncthreads();
-    for (int f = tid; f < TC_BM * 16; f += TC_BLOCK) {
+    for (int f = tid; f < BQ * 16; f += NBLK) {
       const int r = f >> 4, c4 = f & 15;
       if (q0 + r < S)
         reinterpret_cast<float4*>(a.o + ((static_cast<int64_t>(b) * S + q0 + r) * a.H + h) * 64)[c4] =
-            reinterpret_cast<const float4*>(o_rows + r * LDP)[c4];
+            reinterpret_cast<const float4*>(o_rows + r * LDO)[c4];
     }
   }
   tc::fence_before_sync();
@@ -480,19 +588,17 @@ __global__ void __launch_bounds__(TC_BLOCK, 1) fwd_tc_kernel(const FwdArgs a) {
 
 }  // namespace
 
-int fwd_tc_tile_rows() { return TC_BM; }
-
 cudaError_t setup_fwd_tc_attributes() {
   cudaError_t e = cudaFuncSetAttribute(fwd_tc_kernel<false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_ALLOC);
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC);
   if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(fwd_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              TC_SMEM_ALLOC);
+                              SMEM_ALLOC);
 }
 
 cudaError_t launch_fwd_tc(const FwdArgs& args, int causal, cudaStream_t stream) {
   FwdArgs a = args;
-  a.n_qtiles = (a.S + TC_BM - 1) / TC_BM;
+  a.n_qtiles = (a.S + BQ - 1) / BQ;  // blocks of 256 queries per (batch, head)
   int dev = 0, sms = 0;  // one block per SM: a wave is the SM count
   if (cudaGetDevice(&dev) == cudaSuccess &&
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
@@ -500,9 +606,8 @@ cudaError_t launch_fwd_tc(const FwdArgs& args, int causal, cudaStream_t stream) 
   else
     a.wave_ctas = 0;
   const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(a.n_qtiles) * a.B * a.H));
-  if (causal)
-    return launch_pdl(fwd_tc_kernel<true>, grid, dim3(TC_BLOCK), TC_SMEM_ALLOC, stream, a);
-  return launch_pdl(fwd_tc_kernel<false>, grid, dim3(TC_BLOCK), TC_SMEM_ALLOC, stream, a);
+  if (causal) return launch_pdl(fwd_tc_kernel<true>, grid, dim3(NBLK), SMEM_ALLOC, stream, a);
+  return launch_pdl(fwd_tc_kernel<false>, grid, dim3(NBLK), SMEM_ALLOC, stream, a);
 }
 
 cudaError_t fwd_tc_status(int* flag) {
