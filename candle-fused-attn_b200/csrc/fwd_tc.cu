@@ -142,30 +142,89 @@ __device__ __forceinline__ void cp_async_wait_group() {
 // A in TMEM (part i, K-step ks at column a_tmem + 32 i + 8 ks), B in shared memory from b_base:
 // the small pairs (0, 1), (1, 0), (0, 2), (1, 1), (2, 0) of every step, then the (0, 0) of every
 // step. With A in TMEM an MMA reads only B's 2 KB from shared memory, so it runs at the tensor
-// rate. Called by the whole MMA warp (one elected lane issues).
-// B is K's parts read K-major (S = Q K^T: K-steps 256 bytes apart) or, B_MN, V's parts -- the same
-// row layout -- read MN-major (O = P V, N = d: K-steps of 16 keys 2048 bytes apart).
+// rate. B is K's parts read K-major (S = Q K^T: K-steps 256 bytes apart) or, B_MN, V's parts --
+// the same row layout -- read MN-major (O = P V, N = d: K-steps of 16 keys 2048 bytes apart).
+// Called by the whole MMA warp. The 24 MMAs are one asm block: one elect.sync for all of them,
+// constant accumulate predicates, and the operand offsets (A: TMEM columns; B: the descriptor's
+// start address in 16-byte units, parts PART bytes apart) as immediates -- three instructions an
+// MMA, so the issue keeps ahead of the tensor core while the softmax warps share the scheduler.
+#define MMA6(AO, BO, P)                                                   \
+  "add.u32 at, %1, " #AO ";\n\t"                                          \
+  "add.u32 bl, %2, " #BO ";\n\t"                                          \
+  "mov.b64 bd, {bl, %3};\n\t"                                             \
+  "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [at], bd, %4, " #P ";\n\t"
+#define MMA_BLOCK_BEGIN                                                   \
+  "{\n\t.reg .pred e, pf, pt;\n\t.reg .b32 at, bl;\n\t.reg .b64 bd;\n\t"  \
+  "elect.sync _|e, 0xffffffff;\n\t"                                       \
+  "setp.ne.b32 pf, %1, %1;\n\tsetp.eq.b32 pt, %1, %1;\n\t"
+static_assert(PART >> 4 == 512, "part stride in descriptor units");
+
 template <bool B_MN>
 __device__ __forceinline__ void issue_split_mma(uint32_t d, uint32_t a_tmem, uint32_t b_base,
                                                 uint32_t idesc) {
-  constexpr int PA[6] = {0, 0, 1, 0, 1, 2};
-  constexpr int PB[6] = {0, 1, 0, 2, 1, 0};
-  constexpr int STEP = B_MN ? 2048 : 256;
   const tc::Desc bd = tc::split_desc(B_MN ? tc::desc_kmajor(b_base, 1024, 128)
                                           : tc::desc_kmajor(b_base, 128, 1024));
   const uint32_t id = B_MN ? idesc | (1u << 16) : idesc;
-  const uint32_t blo = tc::opaque(bd.lo);
-#pragma unroll
-  for (int ks = 0; ks < 4; ++ks)
-#pragma unroll
-    for (int p = 1; p < 6; ++p)
-      tc::mma_bf16_tmem_a_warp(d, a_tmem + 32 * PA[p] + 8 * ks,
-                               blo + ((PB[p] * PART + STEP * ks) >> 4), bd.hi, id,
-                               ks > 0 || p > 1);
-#pragma unroll
-  for (int ks = 0; ks < 4; ++ks)
-    tc::mma_bf16_tmem_a_warp(d, a_tmem + 8 * ks, blo + ((STEP * ks) >> 4), bd.hi, id, 1);
+  if constexpr (!B_MN) {
+    asm volatile(MMA_BLOCK_BEGIN
+        MMA6(0, 512, pf)
+        MMA6(32, 0, pt)
+        MMA6(0, 1024, pt)
+        MMA6(32, 512, pt)
+        MMA6(64, 0, pt)
+        MMA6(8, 528, pt)
+        MMA6(40, 16, pt)
+        MMA6(8, 1040, pt)
+        MMA6(40, 528, pt)
+        MMA6(72, 16, pt)
+        MMA6(16, 544, pt)
+        MMA6(48, 32, pt)
+        MMA6(16, 1056, pt)
+        MMA6(48, 544, pt)
+        MMA6(80, 32, pt)
+        MMA6(24, 560, pt)
+        MMA6(56, 48, pt)
+        MMA6(24, 1072, pt)
+        MMA6(56, 560, pt)
+        MMA6(88, 48, pt)
+        MMA6(0, 0, pt)
+        MMA6(8, 16, pt)
+        MMA6(16, 32, pt)
+        MMA6(24, 48, pt)
+        "}\n" ::"r"(d), "r"(a_tmem), "r"(bd.lo), "r"(bd.hi), "r"(id)
+        : "memory");
+  } else {
+    asm volatile(MMA_BLOCK_BEGIN
+        MMA6(0, 512, pf)
+        MMA6(32, 0, pt)
+        MMA6(0, 1024, pt)
+        MMA6(32, 512, pt)
+        MMA6(64, 0, pt)
+        MMA6(8, 640, pt)
+        MMA6(40, 128, pt)
+        MMA6(8, 1152, pt)
+        MMA6(40, 640, pt)
+        MMA6(72, 128, pt)
+        MMA6(16, 768, pt)
+        MMA6(48, 256, pt)
+        MMA6(16, 1280, pt)
+        MMA6(48, 768, pt)
+        MMA6(80, 256, pt)
+        MMA6(24, 896, pt)
+        MMA6(56, 384, pt)
+        MMA6(24, 1408, pt)
+        MMA6(56, 896, pt)
+        MMA6(88, 384, pt)
+        MMA6(0, 0, pt)
+        MMA6(8, 128, pt)
+        MMA6(16, 256, pt)
+        MMA6(24, 384, pt)
+        "}\n" ::"r"(d), "r"(a_tmem), "r"(bd.lo), "r"(bd.hi), "r"(id)
+        : "memory");
+  }
 }
+#undef MMA6
+#undef MMA_BLOCK_BEGIN
 
 // Named barriers 3 + q: the four softmax warps of TMEM lane quarter q (w % 4 == q), which hold
 // the same rows and exchange their row maxima. Every participant syncs, so no warp can run a
