@@ -166,6 +166,20 @@ __device__ __forceinline__ void issue6_tmem_a(uint32_t d, ACol acol, tc::Desc bd
     tc::mma_bf16_tmem_a_warp(d, acol(0, ks), blo + ((B_STEP * ks) >> 4), bd.hi, idesc, 1);
 }
 
+constexpr float LOG2E = 1.4426950408889634f;  // log2(e), rounded to fp32
+
+// Packed fp32 pairs (tc::pack2 / unpack2), one instruction a pair.
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma2v(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
 // atomicAdd with acquire-release semantics at GPU scope.
 __device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
   int old;
@@ -357,6 +371,8 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
 
   bool err = err0;
   const int key = k0 + row;
+  const uint64_t nsc2 = tc::pack2(-a.scale, -a.scale);     // L - s scale = fma(s, -scale, L)
+  const uint64_t nl2e2 = tc::pack2(-LOG2E, -LOG2E);        // e^-y = 2^(-y log2 e)
   float dv[16], dk[16];  // compute threads: dV, dK of the key row, this thread's 16 dims
 #pragma unroll
   for (int c = 0; c < 16; ++c) dv[c] = dk[c] = 0.0f;
@@ -429,13 +445,24 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
         tc::tmem_wait_ld();
         float ds[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int ql = col + u, qi = q0 + ql;
-          // P = e^(s * scale - L), one rounding of the argument (as bwd_ffma.cu).
-          float p = expf(fmaf(sb[u], a.scale, -Lt[ql]));
-          if (edge && !(qi < S && key < S && !(CAUSAL && key > qi))) p = 0.0f;
-          pr[8 * h8 + u] = p;
-          ds[u] = p * (gb[u] - Dt[ql]);
+        for (int u = 0; u < 8; u += 2) {
+          const int ql = col + u;
+          // P = e^(s * scale - L): the argument with one rounding (L - s scale by one fma, so the
+          // cancellation is exact), then 2^(arg log2 e) on the SFU (ex2.approx, max relative
+          // error about 2^-22); dS = P (dP - D). Pairs of queries in packed fp32.
+          const uint64_t l2 = *reinterpret_cast<const uint64_t*>(Lt + ql);
+          const uint64_t d2 = *reinterpret_cast<const uint64_t*>(Dt + ql);
+          float x0, x1;
+          tc::unpack2(mul2(fma2v(tc::pack2(sb[u], sb[u + 1]), nsc2, l2), nl2e2), x0, x1);
+          float p0 = ex2(x0), p1 = ex2(x1);
+          if (edge) {
+            if (!(q0 + ql < S && key < S && !(CAUSAL && key > q0 + ql))) p0 = 0.0f;
+            if (!(q0 + ql + 1 < S && key < S && !(CAUSAL && key > q0 + ql + 1))) p1 = 0.0f;
+          }
+          pr[8 * h8 + u] = p0;
+          pr[8 * h8 + u + 1] = p1;
+          tc::unpack2(mul2(tc::pack2(p0, p1), tc::sub2(tc::pack2(gb[u], gb[u + 1]), d2)), ds[u],
+                      ds[u + 1]);
         }
         store_parts(dSp, PART_K, kmaj_off(row, 2 * cg + h8), ds);
       }
