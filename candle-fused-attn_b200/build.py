@@ -21,7 +21,8 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 OUT = PKG / "candle_fused_attn" / "libcfa.so"
-SOURCES = ["fwd_ffma.cu", "fwd_tc.cu", "bwd_ffma.cu", "bwd_tc.cu", "hd_ffma.cu", "cfa_abi.cu", "cfa_noalloc.cu"]
+SOURCES = ["fwd_ffma.cu", "fwd_tc.cu", "bwd_ffma.cu", "bwd_tc.cu", "hd_ffma.cu", "linear_tc.cu",
+           "cfa_abi.cu", "cfa_noalloc.cu"]
 HOST_DIR = PKG / "host"
 HOST_OUT = PKG / "candle_fused_attn" / "libcfa_host.so"
 HOST_SOURCES = ["tensor.cu", "candle_fused_attn.cpp"]

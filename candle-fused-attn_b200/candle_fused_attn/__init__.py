@@ -24,6 +24,11 @@ Device only: the CUDA kernels are the product; the reference's CPU composed path
 test oracle (oracle/), never here. A CPU tensor, a dtype other than float32, a head_dim not in
 `HEAD_DIMS`, or a missing libcfa.so raise `FusedAttentionError` / `ImportError`.
 
+Next to the path, the projection of the reference's training step (examples/tutorial.rs:103-118):
+- `broadcast_matmul(x, w)`: candle's `Tensor::broadcast_matmul` as the step uses it, x [..., k] times
+  w [k, n], differentiable in both (dx = dy w^T, dw = x^T dy), on the tensor-core GEMM of the C ABI
+  (`cfa_matmul_f32`); `matmul(a, b)` is the 2-D product itself.
+
 Failure detection: every device-side wait of the kernels is bounded. An expired wait (results
 invalid) is written by the kernel into a page-locked host flag this module registers with the C
 ABI (`cfa_error_sink`), so the next call of any function here raises `FusedAttentionError`
@@ -49,6 +54,8 @@ __all__ = [
     "qkv_geometry",
     "attention_forward",
     "attention_backward",
+    "matmul",
+    "broadcast_matmul",
     "HostPipeline",
 ]
 
@@ -308,6 +315,63 @@ def fused_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
     strides -> [batch, heads, seq, d] (a transposed view of a dense [batch, seq, heads, d] buffer)."""
     q, k, v = _float4_rows(q), _float4_rows(k), _float4_rows(v)
     return _FusedAttention.apply(q, k, v, float(scale), bool(causal)).transpose(1, 2)
+
+
+# ---------------------------------------------------------------------------------------------
+# The projection next to the path (examples/tutorial.rs:103-118): candle's broadcast_matmul
+# ---------------------------------------------------------------------------------------------
+
+def matmul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """C = a b for 2-D f32 CUDA tensors (a [m, k], b [k, n], any strides: transposed and strided
+    views are read in place) on the tensor-core GEMM: three bf16 parts per operand, fp32 sums,
+    bit-identical across reruns."""
+    dev = _check_device(a, b, who="matmul")
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
+        raise FusedAttentionError(
+            f"matmul: shape mismatch {tuple(a.shape)} x {tuple(b.shape)}")
+    _raise_if_expired()
+    m, k = a.shape
+    n = b.shape[1]
+    ldc = (n + 3) // 4 * 4  # 16-byte rows
+    c = torch.empty((m, ldc), dtype=torch.float32, device=dev)
+    ws_bytes = _abi.matmul_workspace_bytes(m, n, k)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
+    with torch.cuda.device(dev):
+        st = _abi.matmul(a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(), b.stride(0),
+                         b.stride(1), c.data_ptr(), ldc, m, n, k,
+                         ws.data_ptr() if ws is not None else None, ws_bytes, _stream(dev))
+    if st != _abi.CFA_OK:
+        raise FusedAttentionError(f"matmul: {_abi.strerror(st)}")
+    return c if ldc == n else c[:, :n]
+
+
+class _Matmul(torch.autograd.Function):
+    """a [m, k] b [k, n]; the backward's two products run on the same kernel, reading the saved
+    operands transposed in place: da = dc b^T, db = a^T dc."""
+
+    @staticmethod
+    def forward(ctx, a, b):
+        ctx.save_for_backward(a, b)
+        return matmul(a, b)
+
+    @staticmethod
+    def backward(ctx, grad):
+        a, b = ctx.saved_tensors
+        da = matmul(grad, b.t()) if ctx.needs_input_grad[0] else None
+        db = matmul(a.t(), grad) if ctx.needs_input_grad[1] else None
+        return da, db
+
+
+def broadcast_matmul(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """candle's `Tensor::broadcast_matmul(x, w)` as the reference's training step uses it
+    (examples/tutorial.rs:110): x [..., k] times a 2-D w [k, n] -> [..., n], f32 on CUDA, with
+    gradients for both (the step trains w: tutorial.rs:113-117)."""
+    if w.dim() != 2 or x.dim() < 1 or x.shape[-1] != w.shape[0]:
+        raise FusedAttentionError(
+            f"broadcast_matmul: shape mismatch {tuple(x.shape)} x {tuple(w.shape)}")
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    return _Matmul.apply(x2, w).reshape(*lead, w.shape[1])
 
 
 from .host_pipeline import HostPipeline  # noqa: E402  (uses _abi; public host-buffer API)

@@ -47,6 +47,9 @@ EXPORTS = (
     "cfa_bwd_f32_d64_ffma",
     "cfa_bwd_noalloc_status",
     "cfa_error_sink",
+    "cfa_matmul_workspace_bytes",
+    "cfa_matmul_f32",
+    "cfa_matmul_status",
 )
 
 # Head dims the generic entry points (cfa_fwd_f32, cfa_bwd_f32) take; the _d64 ones take 64 only,
@@ -113,6 +116,13 @@ def load() -> ctypes.CDLL:
     lib.cfa_error_sink.argtypes = [_p]
     lib.cfa_fwd_status.restype = ctypes.c_int
     lib.cfa_fwd_status.argtypes = [_p]
+    lib.cfa_matmul_workspace_bytes.restype = ctypes.c_size_t
+    lib.cfa_matmul_workspace_bytes.argtypes = [_i64, _i64, _i64]
+    lib.cfa_matmul_f32.restype = ctypes.c_int
+    lib.cfa_matmul_f32.argtypes = [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i64,
+                                   _p, ctypes.c_size_t, _p]
+    lib.cfa_matmul_status.restype = ctypes.c_int
+    lib.cfa_matmul_status.argtypes = [_p]
     for name in ("cfa_bwd_workspace_bytes_hd", "cfa_bwd_workspace_bytes_fast_hd"):
         fn = getattr(lib, name)
         fn.restype = ctypes.c_size_t
@@ -241,3 +251,19 @@ def bwd_noalloc(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, do_ptr, dos, dq
     return fn(q_ptr, strides3(qs), k_ptr, strides3(ks), v_ptr, strides3(vs), o_ptr, lse_ptr,
               do_ptr, strides3(dos), dqkv_ptr, b, h, s, d, ctypes.c_float(scale),
               int(bool(causal)), stream)
+
+
+def matmul_workspace_bytes(m, n, k) -> int:
+    return int(load().cfa_matmul_workspace_bytes(m, n, k))
+
+
+def matmul(a_ptr, a_rs, a_cs, b_ptr, b_rs, b_cs, c_ptr, c_rs, m, n, k, ws_ptr, ws_bytes,
+           stream) -> int:
+    """cfa_matmul_f32: C (m x n, rows c_rs apart) = A (m x k) B (k x n), each operand through its
+    (row, column) strides; returns the status."""
+    return load().cfa_matmul_f32(a_ptr, a_rs, a_cs, b_ptr, b_rs, b_cs, c_ptr, c_rs, m, n, k,
+                                 ws_ptr, ws_bytes, stream)
+
+
+def matmul_status(stream) -> int:
+    return load().cfa_matmul_status(stream)

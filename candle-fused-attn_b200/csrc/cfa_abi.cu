@@ -225,7 +225,7 @@ int* error_sink() { return g_sink.load(std::memory_order_relaxed); }
 
 extern "C" {
 
-int cfa_abi_version(void) { return (2 << 16) | 0; }
+int cfa_abi_version(void) { return (2 << 16) | 1; }
 
 const char* cfa_strerror(int status) {
   switch (status) {
@@ -320,6 +320,75 @@ int cfa_bwd_f32(const float* q, const int64_t q_strides[3], const float* k,
   return bwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, d_o, do_strides, dqkv,
                   workspace, workspace_bytes, batch, heads, seq, head_dim, scale, causal, stream,
                   true, Pair::kTensorCore);
+}
+
+// The projection GEMM: any strides for A and B (the split pass gathers them; K-contiguous rows
+// that are 16-byte aligned are read 16 bytes at a time), 16-byte rows for C.
+namespace {
+DeviceOnce g_linear_once[kMaxDevices];
+
+// M, N and K up to 2^30: every tile, chunk and K index the kernels form fits int32.
+constexpr int64_t kLinMax = int64_t(1) << 30;
+}  // namespace
+
+size_t cfa_matmul_workspace_bytes(int64_t m, int64_t n, int64_t k) {
+  if (m <= 0 || n <= 0 || k <= 0 || m > kLinMax || n > kLinMax || k > kLinMax) return 0;
+  return cfa::linear_plan(m, n, k).ws_bytes;
+}
+
+int cfa_matmul_f32(const float* a, int64_t a_row_stride, int64_t a_col_stride, const float* b,
+                   int64_t b_row_stride, int64_t b_col_stride, float* c, int64_t c_row_stride,
+                   int64_t m, int64_t n, int64_t k, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  if (m < 0 || n < 0 || k < 0) return CFA_ERR_SHAPE;
+  if (m == 0 || n == 0) return CFA_OK;
+  if (m > kLinMax || n > kLinMax || k > kLinMax) return CFA_ERR_OVERFLOW;
+  if (!c || (k > 0 && (!a || !b || !workspace))) return CFA_ERR_NULL;
+  if (!aligned16(c) || (m > 1 && c_row_stride % 4 != 0)) return CFA_ERR_ALIGNMENT;
+  cfa::LinArgs args{};
+  cfa::LinPlan p{};
+  if (k > 0) {
+    p = cfa::linear_plan(m, n, k);
+    if (workspace_bytes < p.ws_bytes) return CFA_ERR_WORKSPACE;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return CFA_ERR_WORKSPACE;
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    args.pa = ws + p.pa_off;
+    args.pb = ws + p.pb_off;
+    args.part = reinterpret_cast<float*>(ws + p.part_off);
+    args.a_k_contig = a_col_stride == 1;
+    args.b_k_contig = b_row_stride == 1;
+    args.a_vec = args.a_k_contig && aligned16(a) && (m == 1 || a_row_stride % 4 == 0);
+    args.b_vec = args.b_k_contig && aligned16(b) && (n == 1 || b_col_stride % 4 == 0);
+  }
+  const int st = setup(g_linear_once, cfa::setup_linear_attributes);
+  if (st != CFA_OK) return st;
+  args.a = a;
+  args.a_sm = a_row_stride;
+  args.a_sk = a_col_stride;
+  args.b = b;
+  args.b_sk = b_row_stride;
+  args.b_sn = b_col_stride;
+  args.c = c;
+  args.c_sm = c_row_stride;
+  args.M = static_cast<int>(m);
+  args.N = static_cast<int>(n);
+  args.K = static_cast<int>(k);
+  args.tiles_m = p.tiles_m;
+  args.tiles_n = p.tiles_n;
+  args.ksplit = p.ksplit;
+  args.chunk_steps = p.chunk_steps;
+  args.nks = p.nks;
+  args.ldp = p.ldp;
+  args.sink = g_sink.load(std::memory_order_relaxed);
+  const cudaError_t e = cfa::launch_linear_tc(args, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CFA_OK : CFA_ERR_LAUNCH;
+}
+
+int cfa_matmul_status(void* stream) {
+  if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return CFA_ERR_CUDA;
+  int flag = 0;
+  if (cfa::linear_status(&flag) != cudaSuccess) return CFA_ERR_CUDA;
+  return flag != 0 ? CFA_ERR_TIMEOUT : CFA_OK;
 }
 
 int cfa_selftest_bounded_wait(void* workspace, int64_t timeout_ns, int blocks, void* stream) {

@@ -136,6 +136,45 @@ cudaError_t launch_hd_fwd(const FwdArgs& a, int head_dim, int causal, cudaStream
 cudaError_t launch_hd_bwd_prep(const PrepArgs& a, int head_dim, cudaStream_t stream);
 cudaError_t launch_hd_bwd(const BwdArgs& a, int head_dim, int causal, cudaStream_t stream);
 
+// The projection GEMM (linear_tc.cu): C = A B over fp32 on the tensor cores (split bf16 parts).
+// A(m, k) = a[m a_sm + k a_sk], B(k, n) = b[k b_sk + n b_sn] (any strides), C(m, n) = c[m c_sm +
+// n] (16-byte rows). A split pass writes each operand's bf16 parts into the workspace, the product
+// kernel reads them with bulk copies.
+constexpr int LIN_SMS = 148;  // the B200's SM count: fixes the K-chunk count, never read off a device
+
+struct LinPlan {
+  int tiles_m, tiles_n;  // 128 x 128 output tiles
+  int ksplit;            // K chunks (partial tiles summed in chunk order when > 1)
+  int chunk_steps;       // K-steps of 16 per chunk (a multiple of 4)
+  int nks;               // K-steps of the split parts (ksplit * chunk_steps; zero past K)
+  int ldp;               // row length of the partial tiles (N rounded up to 4)
+  size_t pa_off, pb_off, part_off;  // workspace: A's parts, B's parts, the partial tiles
+  size_t ws_bytes;                  // workspace bytes in all
+};
+LinPlan linear_plan(int64_t M, int64_t N, int64_t K);
+
+struct LinArgs {
+  const float* a;
+  int64_t a_sm, a_sk;
+  const float* b;
+  int64_t b_sk, b_sn;
+  float* c;
+  int64_t c_sm;
+  unsigned char* pa;  // A's parts: [tiles_m][nks] blocks of 3 x 128 x 16 bf16
+  unsigned char* pb;  // B's parts: [tiles_n][nks] blocks
+  float* part;        // [ksplit][M][ldp] partial tiles, when ksplit > 1
+  int M, N, K;
+  int tiles_m, tiles_n, ksplit, chunk_steps, nks, ldp;
+  int n_items;  // set by the launcher
+  int a_k_contig, b_k_contig;  // the operand's K stride is 1
+  int a_vec, b_vec;            // ... and its rows are 16-byte aligned (16-byte loads)
+  int* sink;    // host-visible error flag (cfa_error_sink) or nullptr
+};
+cudaError_t setup_linear_attributes();
+cudaError_t launch_linear_tc(const LinArgs& a, cudaStream_t stream);
+// Reads and clears the projection kernel's device error flag (1: a wait expired).
+cudaError_t linear_status(int* flag);
+
 // The failure-detection self-test (cfa_selftest_bounded_wait).
 cudaError_t launch_selftest_wait(int* ws, uint64_t short_ns, int blocks, int* sink,
                                  cudaStream_t stream);

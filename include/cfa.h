@@ -24,6 +24,9 @@
  *                                          its CPU path (src/lib.rs:241-299) takes any head dim
  *   cfa_error_sink             has no counterpart: a host-visible flag that every bounded-wait
  *                                          expiry reaches without a synchronisation
+ *   cfa_matmul_f32,            the projection next to the path: candle's broadcast_matmul of
+ *   cfa_matmul_workspace_bytes           the training step (examples/tutorial.rs:103-118) as a
+ *   cfa_matmul_status                    tensor-core kernel
  *
  * Head dim 64 runs one kernel pair, as the reference does (src/cuda.rs:140-260): the tensor-core
  * pair (csrc/fwd_tc.cu, csrc/bwd_tc.cu). A backward must run on the forward's L of the same pair
@@ -220,10 +223,37 @@ int cfa_selftest_bounded_wait(void* workspace, int64_t timeout_ns, int blocks, v
  * it registered can run. Has no counterpart in the reference, whose waits have no bound. */
 int cfa_error_sink(int* host_flag);
 
+/* The projection next to the attention: C = A B over fp32 on the tensor cores (three bf16 parts
+ * per operand, six products, fp32 sums per 64-element window) -- the contraction of candle's
+ * `Tensor::broadcast_matmul` in the reference's training step (examples/tutorial.rs:110: qkv =
+ * x W_qkv feeding fused_attention_qkv; the step's gradient of W_qkv is x^T dqkv, tutorial.rs:113).
+ * In candle that matmul is cuBLAS SGEMM on the GPU and the gemm crate on the CPU (candle-core's
+ * matmul, not in the crate); this entry point is the B200 kernel for it.
+ *   A(i, p) = a[i a_row_stride + p a_col_stride], i < m, p < k
+ *   B(p, j) = b[p b_row_stride + j b_col_stride], j < n
+ *   C(i, j) = c[i c_row_stride + j]
+ * A and B may have any strides (x W, dY W^T and x^T dY need no copy; rows with the K stride 1 and
+ * 16-byte alignment are read fastest); c and c_row_stride keep C's rows 16-byte aligned (a
+ * multiple of 4 floats) -- else CFA_ERR_ALIGNMENT. m, n, k <= 2^30. m or n = 0: CFA_OK, nothing
+ * launched; k = 0: C = 0. For k > 0 the call needs cfa_matmul_workspace_bytes(m, n, k) bytes of
+ * 256-byte-aligned device workspace: each operand's bf16 parts (6 bytes an element, padded to
+ * 128 x 16 blocks) and, when the output has few 128 x 128 tiles and K is cut into chunks, their
+ * partial tiles. Bit-identical across reruns and GPUs; asynchronous on `stream`. */
+size_t cfa_matmul_workspace_bytes(int64_t m, int64_t n, int64_t k);
+int cfa_matmul_f32(const float* a, int64_t a_row_stride, int64_t a_col_stride,
+                   const float* b, int64_t b_row_stride, int64_t b_col_stride,
+                   float* c, int64_t c_row_stride, int64_t m, int64_t n, int64_t k,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Synchronises `stream` and returns CFA_ERR_TIMEOUT if a bounded wait of a cfa_matmul_f32 kernel
+ * since the last call expired (its output is then invalid), else CFA_OK; clears the flag. */
+int cfa_matmul_status(void* stream);
+
 /* A static description of a status code. */
 const char* cfa_strerror(int status);
 
-/* ABI version: (major << 16) | minor (2.0: one kernel pair per entry point, the error sink). */
+/* ABI version: (major << 16) | minor (2.0: one kernel pair per entry point, the error sink;
+ * 2.1: the projection GEMM). */
 int cfa_abi_version(void);
 
 #ifdef __cplusplus

@@ -13,6 +13,8 @@
 //                                           dq = (ds k) * scale, dk = (ds^T q) * scale
 //   cpu_output         src/lib.rs:318-323   O written [b, s, h, d]
 //   qkv bwd concat     src/lib.rs:581-588   dq, dk, dv interleaved as [b, s, 3, h, d]
+//   matmul             examples/tutorial.rs:110, :113   the training step's projection
+//                                           x.broadcast_matmul(w_qkv) and its weight gradient
 // in fp32 (the parity target and the timed CPU baseline) and fp64 (the accuracy reference of
 // bench/compare.py:506-536). Same operation order as the composed graph: each matmul sums over its
 // inner index in increasing order; the scale multiplies the finished product.
@@ -234,6 +236,28 @@ void run_backward(const float* q, const int64_t qs[3], const float* k, const int
   });
 }
 
+// C = A B, the contraction of candle's broadcast_matmul in the reference's training step
+// (examples/tutorial.rs:110; the step's weight gradient x^T dqkv is the same product on transposed
+// operands). candle-core 0.11.0 computes it on the CPU with the gemm crate (0.18.2 / 0.19.0 in
+// Cargo.lock): FMA micro-kernels whose blocking order cannot be reproduced without that crate, so
+// this restates the product itself -- every C(i, j) sums its k products in increasing k order, one
+// fused multiply-add per product, in T. Rows of C run in parallel; the order within a row does not
+// depend on the thread count. A(i, p) = a[i a_rs + p a_cs], B(p, j) = b[p b_rs + j b_cs], C dense.
+template <typename T>
+void run_matmul(const float* a, int64_t a_rs, int64_t a_cs, const float* b, int64_t b_rs,
+                int64_t b_cs, T* c, int64_t m, int64_t n, int64_t k, int threads) {
+  parallel_slices(0, m, threads, [&](int64_t i) {
+    T* row = c + i * n;
+    std::vector<T> brow(static_cast<size_t>(n));
+    for (int64_t j = 0; j < n; ++j) row[j] = T(0);
+    for (int64_t p = 0; p < k; ++p) {
+      const T x = static_cast<T>(a[i * a_rs + p * a_cs]);
+      for (int64_t j = 0; j < n; ++j) brow[j] = static_cast<T>(b[p * b_rs + j * b_cs]);
+      for (int64_t j = 0; j < n; ++j) row[j] = std::fma(x, brow[j], row[j]);
+    }
+  });
+}
+
 }  // namespace
 
 extern "C" {
@@ -274,6 +298,17 @@ void oracle_bwd_f64(const float* q, const int64_t* qs, const float* k, const int
                     int64_t bh_begin, int64_t bh_end) {
   run_backward<double>(q, qs, k, ks, v, vs, o, lse, dout, dos, B, H, S, D, scale, causal, dqkv,
                        threads, bh_begin, bh_end);
+}
+
+// C [m, n] dense = A B over fp32 inputs through (row, column) strides, in fp32 or fp64.
+void oracle_matmul_f32(const float* a, int64_t a_rs, int64_t a_cs, const float* b, int64_t b_rs,
+                       int64_t b_cs, float* c, int64_t m, int64_t n, int64_t k, int threads) {
+  run_matmul<float>(a, a_rs, a_cs, b, b_rs, b_cs, c, m, n, k, threads);
+}
+
+void oracle_matmul_f64(const float* a, int64_t a_rs, int64_t a_cs, const float* b, int64_t b_rs,
+                       int64_t b_cs, double* c, int64_t m, int64_t n, int64_t k, int threads) {
+  run_matmul<double>(a, a_rs, a_cs, b, b_rs, b_cs, c, m, n, k, threads);
 }
 
 int oracle_max_threads(void) {

@@ -10,6 +10,8 @@ Two independent restatements of the reference's CPU semantics:
   composed_forward / composed_backward (src/lib.rs:241-299) with gather_cpu (src/lib.rs:223-238)
   and the output layouts (src/lib.rs:318-323, :581-588), in fp32 or fp64, multithreaded over
   (batch, head) slices.
+- `matmul`: the training step's projection (examples/tutorial.rs:110, :113), C = A B with every
+  output's products summed in k order by fused multiply-adds, fp32 or fp64.
 - `composed_autograd`: the composed attention differentiated by torch autograd on CPU, the role
   of the reference test's own independent reference (tests/parity.rs:54-75, :119-123), any dtype.
 
@@ -52,6 +54,10 @@ def load():
         fn = getattr(lib, name)
         fn.restype = None
         fn.argtypes = args
+    for name in ("oracle_matmul_f32", "oracle_matmul_f64"):
+        fn = getattr(lib, name)
+        fn.restype = None
+        fn.argtypes = [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, ctypes.c_int]
     lib.oracle_max_threads.restype = ctypes.c_int
     _lib = lib
     return lib
@@ -177,3 +183,16 @@ def normwise(got: torch.Tensor, ref: torch.Tensor) -> float:
 
 def env_threads() -> int:
     return int(os.environ.get("ORACLE_THREADS", "0"))
+
+
+def matmul(a: torch.Tensor, b: torch.Tensor, dtype=torch.float32, threads: int = 0) -> torch.Tensor:
+    """C = a b for 2-D fp32 CPU tensors (any strides), fp32 (`oracle_matmul_f32`) or fp64 output."""
+    assert a.dtype == torch.float32 and b.dtype == torch.float32 and a.device.type == "cpu"
+    assert a.dim() == 2 and b.dim() == 2 and a.shape[1] == b.shape[0]
+    m, k = a.shape
+    n = b.shape[1]
+    c = torch.empty((m, n), dtype=dtype)
+    fn = load().oracle_matmul_f32 if dtype == torch.float32 else load().oracle_matmul_f64
+    fn(a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(), b.stride(0), b.stride(1),
+       c.data_ptr(), m, n, k, threads or env_threads())
+    return c

@@ -182,3 +182,33 @@ def test_noalloc_checks_before_scratch_size():
     assert _abi.bwd_noalloc(*args(FAKE, -1, 6, 240, 64)) == _abi.CFA_ERR_SHAPE
     assert _abi.bwd_noalloc(*args(FAKE, 1 << 30, 1 << 30, 1 << 30, 64)) == _abi.CFA_ERR_OVERFLOW
     assert _abi.bwd_noalloc(*args(FAKE, 64, 64, 1024, 64)) == _abi.CFA_ERR_WORKSPACE
+
+
+def test_matmul_checks_arguments():
+    """cfa_matmul_f32's host-side checks (no launch): empty problems, negative or huge sizes, null
+    pointers, C's 16-byte rows, the workspace (size and 256-byte alignment)."""
+    need = _abi.matmul_workspace_bytes(300, 200, 100)
+    assert need > 0 and _abi.matmul_workspace_bytes(0, 5, 5) == 0
+
+    def call(m=300, n=200, k=100, a=FAKE, b=FAKE, c=FAKE, ldc=200, ws=FAKE, nbytes=need):
+        return _abi.matmul(a, 100, 1, b, 200, 1, c, ldc, m, n, k, ws, nbytes, None)
+
+    assert call(m=0) == _abi.CFA_OK and call(n=0, c=None) == _abi.CFA_OK
+    assert call(m=-1) == _abi.CFA_ERR_SHAPE
+    assert call(k=1 << 31) == _abi.CFA_ERR_OVERFLOW
+    assert call(a=None) == _abi.CFA_ERR_NULL and call(ws=None) == _abi.CFA_ERR_NULL
+    assert call(c=FAKE + 4) == _abi.CFA_ERR_ALIGNMENT
+    assert call(ldc=202) == _abi.CFA_ERR_ALIGNMENT
+    assert call(nbytes=need - 1) == _abi.CFA_ERR_WORKSPACE
+    assert call(ws=FAKE + 16) == _abi.CFA_ERR_WORKSPACE
+
+
+def test_matmul_workspace_grows_with_the_parts():
+    """The workspace holds both operands' bf16 parts (6 bytes an element, 128 x 16 blocks) and, when
+    K is cut into chunks (few output tiles), their partial tiles."""
+    m, n, k = 15360, 1152, 384
+    parts = (m // 128 + n // 128) * (k // 16) * 3 * 128 * 16 * 2
+    assert _abi.matmul_workspace_bytes(m, n, k) >= parts
+    m, n, k = 384, 1152, 15360  # 27 output tiles: K in chunks
+    parts = (m // 128 + n // 128) * (k // 16) * 3 * 128 * 16 * 2
+    assert _abi.matmul_workspace_bytes(m, n, k) >= parts + 2 * m * n * 4

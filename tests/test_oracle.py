@@ -108,3 +108,22 @@ def test_oracle_pinned_to_reference_kernel(path):
     assert (g - fx["dqkv"]).abs().max() < 5e-6
     assert oracle.normwise(o, fx["o"]) < 1e-5
     assert oracle.normwise(g, fx["dqkv"]) < 1e-5
+
+
+@pytest.mark.parametrize("m,n,k", [(5, 7, 3), (64, 48, 200), (33, 129, 1000)])
+@pytest.mark.parametrize("transposed", [False, True])
+def test_oracle_matmul_against_fp64(m, n, k, transposed):
+    """The projection's product (examples/tutorial.rs:110): the fp64 oracle equals torch's fp64
+    matmul to rounding, and the fp32 oracle (k fused multiply-adds in order) stays within
+    k 2^-24 |A||B| of it; strided (transposed) operands give the same bits as contiguous ones."""
+    g = torch.Generator().manual_seed(m * n + k)
+    a = torch.randn(m, k, generator=g)
+    b = torch.randn(k, n, generator=g)
+    at = a.t().contiguous().t() if transposed else a
+    ref = a.double() @ b.double()
+    c64 = oracle.matmul(at, b, dtype=torch.float64)
+    assert (c64 - ref).abs().max() <= 1e-12 * (a.abs().double() @ b.abs().double()).max()
+    c32 = oracle.matmul(at, b)
+    bound = k * 2.0 ** -24 * (a.abs().double() @ b.abs().double())
+    assert bool(((c32.double() - ref).abs() <= bound).all())
+    assert torch.equal(c32, oracle.matmul(a, b))
