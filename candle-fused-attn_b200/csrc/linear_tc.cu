@@ -63,10 +63,12 @@ constexpr int PRODUCER_WARP = NFOLD / 32;
 constexpr int MMA_WARP = PRODUCER_WARP + 1;
 constexpr int NTHR = NFOLD + 64;
 constexpr int FC = TN * TM / NFOLD;      // output columns per fold thread
-constexpr int OFF_BAR = NSLOT * SLOT;
+constexpr int OFF_OUT = NSLOT * SLOT;   // per fold warp: a 32 x 32 fp32 staging block (4 KB)
+constexpr int OUT_WARP = 32 * 32 * 4;
+constexpr int OFF_BAR = OFF_OUT + (NFOLD / 32) * OUT_WARP;
 constexpr int NBAR = 2 * NSLOT + 4;      // full[NSLOT], empty[NSLOT], accf[2], acce[2]
 constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;
-constexpr int SMEM_ALLOC = SMEM + 1024;
+constexpr int SMEM_ALLOC = SMEM + 128;   // room to align the base to 128 bytes
 constexpr uint32_t TMEM_COLS = 512;      // accumulator pair b: hi at 256 b, lo at 256 b + 128
 constexpr int SPLIT_THREADS = 256;       // one 8-element item of a block per thread
 static_assert(NSLOT % WIN_STEPS == 0, "a window's K-steps occupy whole slots");
@@ -191,9 +193,9 @@ __device__ __forceinline__ void item_geom(const LinArgs& a, int li, int& tm, int
 }
 
 __global__ void __launch_bounds__(NTHR, 1) linear_tc_kernel(const LinArgs a) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   const uint32_t raw = tc::smem_u32(smem_raw);
-  unsigned char* sm = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  unsigned char* sm = smem_raw + ((128u - (raw & 127u)) & 127u);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + OFF_BAR);  // [NSLOT]: the slot's parts landed
   uint64_t* empty = full + NSLOT;     // [NSLOT]: the slot's MMAs completed
   uint64_t* accf = full + 2 * NSLOT;  // [2]: the window's products completed
@@ -309,30 +311,46 @@ __global__ void __launch_bounds__(NTHR, 1) linear_tc_kernel(const LinArgs a) {
       if ((wl + 1) % wins_per_item == 0) {
         int tm, tn, chunk;
         item_geom(a, wl / wins_per_item, tm, tn, chunk);
-        const int m = tm * TM + 32 * q + lane;
         const int nb = tn * TN + FC * half;
-        if (!err && m < a.M) {
-          // The output (one chunk: C; several: this chunk's partial tile, rows ldp apart).
-          float* dst = a.ksplit == 1
-                           ? a.c + static_cast<int64_t>(m) * a.c_sm
-                           : a.part + (static_cast<int64_t>(chunk) * a.M + m) * a.ldp;
+        if (!err) {
+          // The output (one chunk: C; several: this chunk's partial tile, rows ldp apart), 32
+          // columns at a time through this warp's staging block: each lane writes its row's 32
+          // floats (16-byte chunk c of row r at chunk c ^ (r % 8): no bank conflict), then the
+          // warp writes four whole 128-byte rows per instruction.
+          float* const out_rows = a.ksplit == 1 ? a.c : a.part + static_cast<int64_t>(chunk) * a.M * a.ldp;
+          const int64_t ld = a.ksplit == 1 ? a.c_sm : a.ldp;
           const int n_end = a.ksplit == 1 ? a.N : a.ldp;
-          if (nb + FC <= n_end) {
+          float4* stage = reinterpret_cast<float4*>(sm + OFF_OUT + w * OUT_WARP);
+          const int m0 = tm * TM + 32 * q;  // the warp's first row
 #pragma unroll
-            for (int c4 = 0; c4 < FC / 4; ++c4) {
+          for (int h2 = 0; h2 < FC / 32; ++h2) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
               float x0, x1, x2, x3;
-              tc::unpack2(acc[2 * c4], x0, x1);
-              tc::unpack2(acc[2 * c4 + 1], x2, x3);
-              reinterpret_cast<float4*>(dst + nb)[c4] = make_float4(x0, x1, x2, x3);
+              tc::unpack2(acc[16 * h2 + 2 * c], x0, x1);
+              tc::unpack2(acc[16 * h2 + 2 * c + 1], x2, x3);
+              stage[lane * 8 + (c ^ (lane & 7))] = make_float4(x0, x1, x2, x3);
             }
-          } else {  // the tile's right edge
+            __syncwarp();
+            const int c = lane & 7;
+            const int n = nb + 32 * h2 + 4 * c;
 #pragma unroll
-            for (int i = 0; i < FC / 2; ++i) {
-              float x0, x1;
-              tc::unpack2(acc[i], x0, x1);
-              if (nb + 2 * i < n_end) dst[nb + 2 * i] = x0;
-              if (nb + 2 * i + 1 < n_end) dst[nb + 2 * i + 1] = x1;
+            for (int i = 0; i < 8; ++i) {
+              const int r = 4 * i + (lane >> 3);
+              const float4 v = stage[r * 8 + (c ^ (r & 7))];
+              const int m = m0 + r;
+              if (m < a.M) {
+                float* dst = out_rows + static_cast<int64_t>(m) * ld + n;
+                if (n + 4 <= n_end) {
+                  *reinterpret_cast<float4*>(dst) = v;
+                } else if (n < n_end) {
+                  dst[0] = v.x;
+                  if (n + 1 < n_end) dst[1] = v.y;
+                  if (n + 2 < n_end) dst[2] = v.z;
+                }
+              }
             }
+            __syncwarp();
           }
         }
 #pragma unroll
