@@ -381,6 +381,82 @@ def waves(args):
                           "bwd_us": round(1000 * statistics.median(tb), 1)}), flush=True)
 
 
+def train(args):
+    """The reference's training step (examples/tutorial.rs:103-118) at the canvas: qkv =
+    x.broadcast_matmul(W_qkv) -> fused_attention_qkv -> mean-squared loss -> backward (the
+    attention's dqkv, then W's gradient x^T dqkv) -> W -= 0.1 dW, with x [64, 240, 384], W [384,
+    1152] * 0.02 and the target seeded N(0, 1). The projection and its gradient run on the
+    tensor-core GEMM (cfa_matmul_f32: split pass + product kernel, + the chunk sum for x^T dqkv),
+    the attention on the tensor-core pair; the loss and the update are torch elementwise ops.
+    CUDA events, L2 flushed between steps, median of `steps`. Also the two GEMM legs alone
+    (roofline against the split-bf16 ceiling) and torch's fp32 matmul (cuBLAS SGEMM, TF32 off) on
+    the same shapes. One JSON line."""
+    import candle_fused_attn as cfa
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
+    hid = H * D
+    gen = torch.Generator().manual_seed(0)
+    x = torch.randn(B_PER_GPU, S, hid, generator=gen).to(dev)
+    w = (torch.randn(hid, 3 * hid, generator=gen) * 0.02).to(dev).requires_grad_(True)
+    target = torch.randn(B_PER_GPU, S, hid, generator=gen).to(dev)
+
+    def step(_):
+        qkv = cfa.broadcast_matmul(x, w)
+        out = cfa.fused_attention_qkv(qkv, H, SCALE, CAUSAL)
+        loss = ((out - target) ** 2).mean()
+        loss.backward()
+        with torch.no_grad():
+            w.sub_(0.1 * w.grad)
+        w.grad = None
+        return loss
+
+    def median_ms(fn, steps):
+        ts = []
+        for i in range(steps):
+            flush.zero_()
+            ts.append(timed(fn, 1, stream))
+        return statistics.median(ts)
+
+    for i in range(args.warmup):
+        step(i)
+    step_ms = median_ms(step, args.steps)
+    cfa.check_status()
+
+    x2 = x.reshape(-1, hid)
+    dy = torch.randn(B_PER_GPU * S, 3 * hid, generator=gen).to(dev)
+    wd = w.detach()
+    legs = {}
+    m, k, n = x2.shape[0], hid, 3 * hid
+    gflop = 2.0 * m * k * n / 1e9
+    pk = peaks()
+    ceiling = pk["bf16_tflops"] / 6
+    for name, ours, theirs in (
+            ("projection x W", lambda i: cfa.matmul(x2, wd), lambda i: x2 @ wd),
+            ("weight gradient x^T dqkv", lambda i: cfa.matmul(x2.t(), dy), lambda i: x2.t() @ dy)):
+        for i in range(3):
+            ours(i), theirs(i)
+        t_o, t_r = median_ms(ours, args.steps), median_ms(theirs, args.steps)
+        tf = gflop / t_o
+        legs[name] = {"ms": t_o, "tflops": tf, "frac_of_split_ceiling": tf / ceiling,
+                      "cublas_fp32_ms": t_r, "speedup_vs_cublas_fp32": t_r / t_o}
+    cfa.check_status()
+    att = flops(B_PER_GPU, H, S, D, CAUSAL)
+    total = att + 2 * 2.0 * m * k * n
+    print(json.dumps({
+        "mode": "train", "metric": "tutorial training step (x W_qkv, fused attention, MSE, dW)",
+        "unit": "ms", "value": step_ms, "higher_is_better": False,
+        "tflops": total / (step_ms * 1e-3) / 1e12, "dtype": "f32",
+        "config": {"workload": "examples/tutorial.rs:103-118 at the canvas: x [64, 240, 384], "
+                               "W_qkv [384, 1152], 6 heads of 64, scale 0.125", "l2": "flushed"},
+        "data": "synthetic (seeded N(0,1) x and target, W N(0,1)*0.02)",
+        "gemm_legs": legs, "split_ceiling_tflops": ceiling,
+        "gpu_launches_per_step": 8,
+    }), flush=True)
+
+
 def config_of(world: int) -> dict:
     """The `config` of both arms' JSON lines (the same workload, the same keys)."""
     return {"workload": WORKLOAD, "global_batch": B_PER_GPU * world, "seq_len": S, "heads": H,
@@ -421,10 +497,12 @@ def main():
     ap.add_argument("--pair", choices=["tc", "ffma"], default="tc",
                     help="kernels mode: the head-dim-64 kernel pair of the fwd+bwd step (tc: the "
                          "tensor-core pair, the default; ffma: the CUDA-core pair)")
-    ap.add_argument("--mode", choices=["full", "kernels", "suite", "waves"], default="full",
+    ap.add_argument("--mode", choices=["full", "kernels", "suite", "waves", "train"],
+                    default="full",
                     help="kernels: warm-up + `steps` plain steps, no timing (for ncu); "
                          "suite: every BASELINE config, ours vs the reference kernel; "
-                         "waves: canvas-shaped fwd / bwd times over batches around 64")
+                         "waves: canvas-shaped fwd / bwd times over batches around 64; "
+                         "train: the reference's training step with its projection")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -437,6 +515,8 @@ def main():
         return suite(args)
     if args.mode == "waves":
         return waves(args)
+    if args.mode == "train":
+        return train(args)
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)

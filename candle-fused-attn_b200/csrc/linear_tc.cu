@@ -15,19 +15,19 @@
 // result and below, so they truncate at their own magnitude). Each window's hi + lo is added into
 // fp32 registers with round-to-nearest, windows in K order.
 //
-// Block (one per SM, persistent): 16 worker warps and 1 MMA warp; output tiles of 128 x 128,
-// K-steps of 16.
-//  - workers, each K-step: every thread copies (cp.async, zero-filled past the edges) one 8-float
-//    item of A (warps 0-7) or of B (warps 8-15) into slots of its own, DEPTH K-steps ahead, and
-//    splits the item copied DEPTH - 1 steps earlier into bf16 parts in a ring of NSLOT part
-//    buffers (no-swizzle core matrices, K-major when K is the operand's contiguous index,
-//    MN-major otherwise -- the instruction descriptor's transpose bits read either);
-//  - workers, each window, one window behind the split: thread (lane quarter q, column group g)
-//    adds the window's hi + lo of row 32 q + lane, columns 32 g .. + 31, into its 32 running sums
-//    and, after an output tile's last window, stores them;
-//  - MMA warp: six MMAs per K-step (M = N = 128, A and B from shared memory), a commit per ring
-//    slot, and one per window into the window's accumulator pair (two pairs: 512 TMEM columns),
-//    so the tensor core runs one window while the workers split the next and fold the last.
+// Two kernels. The split kernel writes each operand once, as bf16 parts, into the workspace in
+// the exact layout the MMA reads: blocks of 128 rows (M or N) x 16 K, three 4 KB parts each,
+// K-major no-swizzle core matrices -- whatever the operand's strides (transposed views and x^T
+// need no copy). The product kernel then does no CUDA-core work on the operands (one block per
+// SM, persistent; output tiles of 128 x 128):
+//  - producer warp: one lane issues two bulk copies per ring slot (two K-steps of A's blocks and
+//    of B's, 48 KB) into a ring of NSLOT slots, eight K-steps ahead of the tensor core;
+//  - MMA warp: twelve MMAs per slot (M = N = 128, A and B from shared memory) from one asm block,
+//    a commit per slot, and one per window into the window's accumulator pair (two pairs: 512
+//    TMEM columns), so the tensor core runs one window while the fold warps read the last;
+//  - fold warps: thread (lane quarter q, column half h) adds each window's hi + lo of row 32 q +
+//    lane, columns 64 h .. + 63, into its 64 running sums and, after an output tile's last
+//    window, writes them through a per-warp staging block as whole 128-byte rows.
 // Work items are (output tile, K chunk): when the output has fewer tiles than the GPU has SMs, K is
 // cut into chunks whose partial tiles a second kernel sums in chunk order. The chunk count is a
 // function of (M, N, K) alone, and every item's arithmetic is independent of where it runs, so the
@@ -56,8 +56,9 @@ constexpr int KS = 16;           // K per MMA step
 constexpr int WIN_STEPS = 4;     // K-steps per accumulation window (64 reduction elements)
 constexpr int PART = TM * KS * 2;        // one bf16 part of a 128 x 16 operand block
 constexpr int BLOCK = 3 * PART;          // the three parts of one operand block
-constexpr int SLOT = 2 * BLOCK;          // a ring slot: A's block, then B's
-constexpr int NSLOT = 8;                 // ring slots (two windows)
+constexpr int SLOT_STEPS = 2;            // K-steps per ring slot
+constexpr int SLOT = 2 * SLOT_STEPS * BLOCK;  // a ring slot: A's two blocks, then B's
+constexpr int NSLOT = 4;                 // ring slots (two windows)
 constexpr int NFOLD = 256;               // fold threads (warps 0-7)
 constexpr int PRODUCER_WARP = NFOLD / 32;
 constexpr int MMA_WARP = PRODUCER_WARP + 1;
@@ -71,7 +72,8 @@ constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;
 constexpr int SMEM_ALLOC = SMEM + 128;   // room to align the base to 128 bytes
 constexpr uint32_t TMEM_COLS = 512;      // accumulator pair b: hi at 256 b, lo at 256 b + 128
 constexpr int SPLIT_THREADS = 256;       // one 8-element item of a block per thread
-static_assert(NSLOT % WIN_STEPS == 0, "a window's K-steps occupy whole slots");
+static_assert(WIN_STEPS % SLOT_STEPS == 0 && (NSLOT * SLOT_STEPS) % WIN_STEPS == 0,
+              "a window's K-steps occupy whole slots");
 static_assert(SMEM_ALLOC <= 232448, "shared memory per block");
 static_assert(TM * KS / 8 == SPLIT_THREADS, "items of a block");
 static_assert(NFOLD % 128 == 0, "fold warp w covers TMEM lane quarter w % 4");
@@ -144,35 +146,53 @@ __global__ void __launch_bounds__(SPLIT_THREADS) linear_split_kernel(const LinAr
 // The product: bulk copies of the parts, six MMAs a K-step, fp32 folds a window.
 // ---------------------------------------------------------------------------------------------
 
-// The six products of one K-step (A's parts at descriptor words a_lo + 256 i, B's at b_lo +
-// 256 j: parts PART bytes apart): the five small ones into `lo`, A0B0 into `hi`. acc = 0 starts
-// both accumulators afresh (the window's first K-step). One asm block for the warp: one
-// elect.sync, immediate offsets.
+// The six products of each of a slot's two K-steps (A's parts of K-step t at descriptor words
+// a_lo + 768 t + 256 i, B's at b_lo + 768 t + 256 j: parts PART bytes, blocks BLOCK bytes apart):
+// the five small ones into `lo`, A0B0 into `hi`. acc = 0 starts both accumulators afresh (the
+// slot opens a window). Two asm blocks for the warp, each with one elect.sync and immediate
+// offsets: the first ten MMAs, then (issue_slot_tail) the last two -- the MMA warp waits for the
+// next slot between them, while the tensor core still has queued work.
 #define LMMA(D, AO, BO, P)                                                  \
   "add.u32 al, %2, " #AO ";\n\t"                                            \
   "add.u32 bl, %4, " #BO ";\n\t"                                            \
   "mov.b64 ad, {al, %3};\n\t"                                               \
   "mov.b64 bd, {bl, %5};\n\t"                                               \
   "@e tcgen05.mma.cta_group::1.kind::f16 [" D "], ad, bd, %6, " #P ";\n\t"
-static_assert(PART >> 4 == 256, "part stride in descriptor units");
-__device__ __forceinline__ void issue_kstep(uint32_t d_hi, uint32_t d_lo, uint32_t a_lo,
-                                            uint32_t a_hi, uint32_t b_lo, uint32_t b_hi,
-                                            uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred e, pa, pt;\n\t.reg .b32 al, bl;\n\t.reg .b64 ad, bd;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "setp.ne.b32 pa, %7, 0;\n\tsetp.eq.b32 pt, %7, %7;\n\t"
+#define LMMA_BEGIN                                                          \
+  "{\n\t.reg .pred e, pa, pt;\n\t.reg .b32 al, bl;\n\t.reg .b64 ad, bd;\n\t"   \
+  "elect.sync _|e, 0xffffffff;\n\t"                                         \
+  "setp.ne.b32 pa, %7, 0;\n\tsetp.eq.b32 pt, %7, %7;\n\t"
+static_assert(PART >> 4 == 256 && BLOCK >> 4 == 768 && SLOT_STEPS == 2, "descriptor offsets");
+__device__ __forceinline__ void issue_slot_head(uint32_t d_hi, uint32_t d_lo, uint32_t a_lo,
+                                                uint32_t a_hi, uint32_t b_lo, uint32_t b_hi,
+                                                uint32_t idesc, uint32_t acc) {
+  asm volatile(LMMA_BEGIN
       LMMA("%1", 0, 256, pa)
       LMMA("%1", 256, 0, pt)
       LMMA("%1", 0, 512, pt)
       LMMA("%1", 256, 256, pt)
       LMMA("%1", 512, 0, pt)
       LMMA("%0", 0, 0, pa)
+      LMMA("%1", 768, 1024, pt)
+      LMMA("%1", 1024, 768, pt)
+      LMMA("%1", 768, 1280, pt)
+      LMMA("%1", 1024, 1024, pt)
       "}\n" ::"r"(d_hi), "r"(d_lo), "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc),
       "r"(acc)
       : "memory");
 }
+__device__ __forceinline__ void issue_slot_tail(uint32_t d_hi, uint32_t d_lo, uint32_t a_lo,
+                                                uint32_t a_hi, uint32_t b_lo, uint32_t b_hi,
+                                                uint32_t idesc) {
+  asm volatile(LMMA_BEGIN
+      LMMA("%1", 1280, 768, pt)
+      LMMA("%0", 768, 768, pt)
+      "}\n" ::"r"(d_hi), "r"(d_lo), "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc),
+      "r"(1u)
+      : "memory");
+}
 #undef LMMA
+#undef LMMA_BEGIN
 
 __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   uint64_t d;
@@ -239,23 +259,23 @@ __global__ void __launch_bounds__(NTHR, 1) linear_tc_kernel(const LinArgs a) {
       const unsigned char* pa = nullptr;
       const unsigned char* pb = nullptr;
       int left = 0, li = 0;
-      for (int g = 0; g < total; ++g) {
+      for (int g = 0; g < total / SLOT_STEPS; ++g) {  // g: slot use
         if (left == 0) {  // the block's next item
           int tm, tn, chunk;
           item_geom(a, li++, tm, tn, chunk);
           const int64_t k0 = static_cast<int64_t>(chunk) * a.chunk_steps;
           pa = a.pa + (static_cast<int64_t>(tm) * a.nks + k0) * BLOCK;
           pb = a.pb + (static_cast<int64_t>(tn) * a.nks + k0) * BLOCK;
-          left = a.chunk_steps;
+          left = a.chunk_steps / SLOT_STEPS;
         }
         const int slot = g % NSLOT;
         if (g >= NSLOT) err |= !tc::mbar_wait(empty + slot, ((g / NSLOT) - 1) & 1, wait_ns(err));
         unsigned char* dst = sm + slot * SLOT;
         tc::mbar_arrive_expect_tx(full + slot, SLOT);
-        tc::bulk_load(dst, pa, BLOCK, full + slot);
-        tc::bulk_load(dst + BLOCK, pb, BLOCK, full + slot);
-        pa += BLOCK;
-        pb += BLOCK;
+        tc::bulk_load(dst, pa, SLOT_STEPS * BLOCK, full + slot);
+        tc::bulk_load(dst + SLOT_STEPS * BLOCK, pb, SLOT_STEPS * BLOCK, full + slot);
+        pa += SLOT_STEPS * BLOCK;
+        pb += SLOT_STEPS * BLOCK;
         --left;
       }
     }
@@ -265,20 +285,30 @@ __global__ void __launch_bounds__(NTHR, 1) linear_tc_kernel(const LinArgs a) {
     const uint32_t idesc = tc::idesc_f32acc(1, TM, TN);
     const uint32_t s0 = tc::smem_u32(sm);
     const tc::Desc ad = tc::split_desc(tc::desc_kmajor(s0, 128, 256));
-    const tc::Desc bd = tc::split_desc(tc::desc_kmajor(s0 + BLOCK, 128, 256));
-    for (int g = 0; g < total; ++g) {
-      const int ks = g % WIN_STEPS, wl = g / WIN_STEPS, b = wl & 1;
-      if (ks == 0 && wl >= 2) {  // the fold warps have read this pair's window wl - 2
-        err |= !tc::mbar_wait(acce + b, ((wl >> 1) - 1) & 1, wait_ns(err));
-      }
-      const int slot = g % NSLOT;
-      err |= !tc::mbar_wait(full + slot, (g / NSLOT) & 1, wait_ns(err));
+    const tc::Desc bd = tc::split_desc(tc::desc_kmajor(s0 + SLOT_STEPS * BLOCK, 128, 256));
+    constexpr int SLOTS_PER_WIN = WIN_STEPS / SLOT_STEPS;
+    const int uses = total / SLOT_STEPS;
+    // Slot use g's operands in place (and, when g opens window wl >= 2, the fold warps done with
+    // window wl - 2's accumulator pair).
+    auto wait_use = [&](int g) {
+      const int wl = g / SLOTS_PER_WIN;
+      if (g % SLOTS_PER_WIN == 0 && wl >= 2)
+        err |= !tc::mbar_wait(acce + (wl & 1), ((wl >> 1) - 1) & 1, wait_ns(err));
+      err |= !tc::mbar_wait(full + g % NSLOT, (g / NSLOT) & 1, wait_ns(err));
       tc::fence_after_sync();
+    };
+    wait_use(0);
+    for (int g = 0; g < uses; ++g) {  // g: slot use
+      const int js = g % SLOTS_PER_WIN, wl = g / SLOTS_PER_WIN, b = wl & 1;
+      const int slot = g % NSLOT;
       const uint32_t so = static_cast<uint32_t>(slot * (SLOT >> 4));
-      issue_kstep(tbase + 256u * b, tbase + 256u * b + 128u, tc::opaque(ad.lo + so), ad.hi,
-                  tc::opaque(bd.lo + so), bd.hi, idesc, ks != 0);
+      const uint32_t d_hi = tbase + 256u * b, d_lo = d_hi + 128u;
+      const uint32_t a_lo = tc::opaque(ad.lo + so), b_lo = tc::opaque(bd.lo + so);
+      issue_slot_head(d_hi, d_lo, a_lo, ad.hi, b_lo, bd.hi, idesc, js != 0);
+      if (g + 1 < uses) wait_use(g + 1);
+      issue_slot_tail(d_hi, d_lo, a_lo, ad.hi, b_lo, bd.hi, idesc);
       tc::commit_warp(empty + slot);
-      if (ks == WIN_STEPS - 1) tc::commit_warp(accf + b);
+      if (js == SLOTS_PER_WIN - 1) tc::commit_warp(accf + b);
     }
   } else {
     // ---- fold warps: thread (lane quarter q, column half h) owns row 32 q + lane, columns
@@ -371,7 +401,8 @@ __global__ void __launch_bounds__(NTHR, 1) linear_tc_kernel(const LinArgs a) {
     }
     // The producer's last copies complete on their slots' full barriers.
     if (w == PRODUCER_WARP && lane == 0) {
-      for (int g = max(0, total - NSLOT); g < total; ++g)
+      const int uses = total / SLOT_STEPS;
+      for (int g = max(0, uses - NSLOT); g < uses; ++g)
         tc::mbar_wait(full + g % NSLOT, (g / NSLOT) & 1, WAIT_TIMEOUT_NS);
     }
   }
