@@ -3,8 +3,8 @@
 // The projection next to the attention on the tensor cores: C = A B over fp32, the contraction of
 // candle's `broadcast_matmul` in the reference's training step (examples/tutorial.rs:103-118:
 // qkv = x W_qkv feeds fused_attention_qkv, and the step's gradient of W_qkv is x^T dqkv). Any
-// orientation: A(m, k) and B(k, n) are read through (row, column) strides of which one is 1, so
-// x W, dY W^T and x^T dY all run on this kernel without a transposed copy.
+// orientation: A(m, k) and B(k, n) are read through (row, column) strides (any values), so x W,
+// dY W^T and x^T dY all run on this kernel without a transposed copy.
 //
 // fp32 products from bf16 parts, as in the attention kernels: every fp32 operand x is split into
 // x0 + x1 + x2, three bf16 (each part the round-to-nearest bf16 of what the previous ones leave;
@@ -22,9 +22,10 @@
 // SM, persistent; output tiles of 128 x 128):
 //  - producer warp: one lane issues two bulk copies per ring slot (two K-steps of A's blocks and
 //    of B's, 48 KB) into a ring of NSLOT slots, eight K-steps ahead of the tensor core;
-//  - MMA warp: twelve MMAs per slot (M = N = 128, A and B from shared memory) from one asm block,
-//    a commit per slot, and one per window into the window's accumulator pair (two pairs: 512
-//    TMEM columns), so the tensor core runs one window while the fold warps read the last;
+//  - MMA warp: twelve MMAs per slot (M = N = 128, A and B from shared memory) from two asm blocks
+//    with the wait for the next slot between them, a commit per slot, and one per window into the
+//    window's accumulator pair (two pairs: 512 TMEM columns), so the tensor core runs one window
+//    while the fold warps read the last;
 //  - fold warps: thread (lane quarter q, column half h) adds each window's hi + lo of row 32 q +
 //    lane, columns 64 h .. + 63, into its 64 running sums and, after an output tile's last
 //    window, writes them through a per-warp staging block as whole 128-byte rows.
