@@ -50,6 +50,8 @@ EXPORTS = (
     "cfa_matmul_workspace_bytes",
     "cfa_matmul_f32",
     "cfa_matmul_status",
+    "cfa_fwd_f32_ffma",
+    "cfa_bwd_f32_ffma",
 )
 
 # Head dims the generic entry points (cfa_fwd_f32, cfa_bwd_f32) take; the _d64 ones take 64 only,
@@ -110,6 +112,10 @@ def load() -> ctypes.CDLL:
     lib.cfa_fwd_f32_d64_ffma.argtypes = lib.cfa_fwd_f32_d64.argtypes
     lib.cfa_bwd_f32_d64_ffma.restype = ctypes.c_int
     lib.cfa_bwd_f32_d64_ffma.argtypes = lib.cfa_bwd_f32_d64.argtypes
+    lib.cfa_fwd_f32_ffma.restype = ctypes.c_int
+    lib.cfa_fwd_f32_ffma.argtypes = lib.cfa_fwd_f32_d64.argtypes
+    lib.cfa_bwd_f32_ffma.restype = ctypes.c_int
+    lib.cfa_bwd_f32_ffma.argtypes = lib.cfa_bwd_f32_d64.argtypes
     lib.cfa_bwd_noalloc_status.restype = ctypes.c_int
     lib.cfa_bwd_noalloc_status.argtypes = [_p]
     lib.cfa_error_sink.restype = ctypes.c_int
@@ -189,6 +195,23 @@ def bwd_ffma(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, do_ptr, dos, dqkv_
              ws_bytes, b, h, s, d, scale, causal, stream) -> int:
     """cfa_bwd_f32_d64_ffma (the CUDA-core pair's backward; L from fwd_ffma); the status."""
     return load().cfa_bwd_f32_d64_ffma(
+        q_ptr, strides3(qs), k_ptr, strides3(ks), v_ptr, strides3(vs), o_ptr, lse_ptr,
+        do_ptr, strides3(dos), dqkv_ptr, ws_ptr, ws_bytes, b, h, s, d,
+        ctypes.c_float(scale), int(bool(causal)), stream)
+
+
+def fwd_hd_ffma(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, b, h, s, d, scale, causal,
+                stream) -> int:
+    """cfa_fwd_f32_ffma (the CUDA-core pair at head dim d in HEAD_DIMS); returns the status."""
+    return load().cfa_fwd_f32_ffma(
+        q_ptr, strides3(qs), k_ptr, strides3(ks), v_ptr, strides3(vs), o_ptr, lse_ptr,
+        b, h, s, d, ctypes.c_float(scale), int(bool(causal)), stream)
+
+
+def bwd_hd_ffma(q_ptr, qs, k_ptr, ks, v_ptr, vs, o_ptr, lse_ptr, do_ptr, dos, dqkv_ptr, ws_ptr,
+                ws_bytes, b, h, s, d, scale, causal, stream) -> int:
+    """cfa_bwd_f32_ffma (L from fwd_hd_ffma); returns the status."""
+    return load().cfa_bwd_f32_ffma(
         q_ptr, strides3(qs), k_ptr, strides3(ks), v_ptr, strides3(vs), o_ptr, lse_ptr,
         do_ptr, strides3(dos), dqkv_ptr, ws_ptr, ws_bytes, b, h, s, d,
         ctypes.c_float(scale), int(bool(causal)), stream)

@@ -89,11 +89,14 @@ __device__ __forceinline__ void row_item(int c, int& r, int& kc) {
   kc = (c >> 3) & 7;
 }
 
+// (Head dim 32: the row's chunks past the head dim are zero-filled, so the parts are those of a
+// 64-wide row whose upper half is zero.)
+template <int HD>
 __device__ __forceinline__ void stage_row_item(unsigned char* st, int slot, int c, const float* src,
                                                int64_t stride, int r0, int seq) {
   int r, kc;
   row_item(c, r, kc);
-  const bool ok = r0 + r < seq;
+  const bool ok = r0 + r < seq && 8 * kc < HD;
   const float* g = src + static_cast<int64_t>(ok ? r0 + r : 0) * stride + 8 * kc;
   cp_async16(st + 16 * ((2 * slot) * NT + threadIdx.x), g, ok ? 16 : 0);
   cp_async16(st + 16 * ((2 * slot + 1) * NT + threadIdx.x), g + 4, ok ? 16 : 0);
@@ -109,14 +112,15 @@ __device__ __forceinline__ void split_row_item(unsigned char* parts, int part_by
   store_parts(parts, part_bytes, kmaj_off(r, kc), x);
 }
 
-// Row item c of a row-major staging area with rows of 68 floats (rows >= valid read as zeros) into
-// the K-major parts at part_bytes apart.
+// Row item c of a row-major staging area with rows of 68 floats (rows >= valid and columns >= HD
+// read as zeros) into the K-major parts at part_bytes apart.
+template <int HD>
 __device__ __forceinline__ void split_staged_row(unsigned char* parts, int part_bytes,
                                                  const float* rows, int c, int valid) {
   int r, kc;
   row_item(c, r, kc);
   float x[8];
-  if (r < valid) {
+  if (r < valid && 8 * kc < HD) {
     const float4 u = reinterpret_cast<const float4*>(rows + r * 68 + 8 * kc)[0];
     const float4 v = reinterpret_cast<const float4*>(rows + r * 68 + 8 * kc)[1];
     x[0] = u.x, x[1] = u.y, x[2] = u.z, x[3] = u.w, x[4] = v.x, x[5] = v.y, x[6] = v.z, x[7] = v.w;
@@ -152,17 +156,17 @@ __device__ __forceinline__ void issue6(uint32_t d, tc::Desc ad, tc::Desc bd, uin
 }
 
 // The same window with the A operand in TMEM: part i of K-step ks at column acol(i, ks).
-template <int B_PART, int B_STEP, typename ACol>
+template <int B_PART, int B_STEP, typename ACol, int STEPS = 4>
 __device__ __forceinline__ void issue6_tmem_a(uint32_t d, ACol acol, tc::Desc bd, uint32_t idesc) {
   const uint32_t blo = tc::opaque(bd.lo);
 #pragma unroll
-  for (int ks = 0; ks < 4; ++ks)
+  for (int ks = 0; ks < STEPS; ++ks)
 #pragma unroll
     for (int p = 1; p < 6; ++p)
       tc::mma_bf16_tmem_a_warp(d, acol(P0(p), ks), blo + ((P1(p) * B_PART + B_STEP * ks) >> 4),
                                bd.hi, idesc, ks > 0 || p > 1);
 #pragma unroll
-  for (int ks = 0; ks < 4; ++ks)
+  for (int ks = 0; ks < STEPS; ++ks)
     tc::mma_bf16_tmem_a_warp(d, acol(0, ks), blo + ((B_STEP * ks) >> 4), bd.hi, idesc, 1);
 }
 
@@ -192,8 +196,10 @@ __device__ __forceinline__ void bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-template <bool CAUSAL>
+template <bool CAUSAL, int HD>
 __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
+  static_assert(HD == 64 || HD == 32, "head dims of the tensor-core backward");
+  constexpr int KSD = HD / 16;  // K-steps of the products that reduce over the head dim
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = tc::smem_u32(smem_raw);
   unsigned char* sm = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -244,8 +250,8 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
   const float* dp = a.dsum + static_cast<int64_t>(bh) * S;
   const int t_begin = CAUSAL ? k0 / QT : 0;  // queries before the block's first key see none
   int* turn = a.turn + static_cast<int64_t>(bh) * a.n_qtiles;  // turn chain: per 64-query tile
-  const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * 64;  // dqkv floats per (b, s)
-  float* dq_base = a.dqkv + static_cast<int64_t>(b) * S * row_stride + h * 64;
+  const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * HD;  // dqkv floats per (b, s)
+  float* dq_base = a.dqkv + static_cast<int64_t>(b) * S * row_stride + h * HD;
   const int N = (S + QT - 1) / QT - t_begin;  // query tiles, >= 1 (k0 < S)
   bool err0 = false;
 
@@ -256,7 +262,7 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
     tc::mbar_init(bar_q, NT / 32);
     tc::mbar_init(bar_ld, 1);
     tc::fence_mbar_init();
-    tc::mbar_arrive_expect_tx(bar_ld, 256u * (2 * min(KB, S - k0) + 2 * min(QT, S - t_begin * QT)));
+    tc::mbar_arrive_expect_tx(bar_ld, 4u * HD * (2 * min(KB, S - k0) + 2 * min(QT, S - t_begin * QT)));
   }
   griddep_launch_dependents();
 
@@ -272,8 +278,8 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
   };
   auto stage_tile = [&](int n) {
     const int q0 = (t_begin + n) * QT;
-    stage_row_item(st, 0, tid, qp, a.q_ss, q0, S);
-    stage_row_item(st, 1, tid, gp, a.do_ss, q0, S);
+    stage_row_item<HD>(st, 0, tid, qp, a.q_ss, q0, S);
+    stage_row_item<HD>(st, 1, tid, gp, a.do_ss, q0, S);
     stage_ld(n);
   };
   // The block one wave later (work item + a.wave_ctas) starts by reading its key block's K, V rows
@@ -292,7 +298,7 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
     else if (tid < 2 * KB) src = a.v + nb_b * a.v_sb + nb_h * a.v_sh + static_cast<int64_t>(row) * a.v_ss;
     else if (tid < 2 * KB + QT) src = a.q + nb_b * a.q_sb + nb_h * a.q_sh + static_cast<int64_t>(row) * a.q_ss;
     else src = a.d_o + nb_b * a.do_sb + nb_h * a.do_sh + static_cast<int64_t>(row) * a.do_ss;
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], 256;" ::"l"(src) : "memory");
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "n"(4 * HD) : "memory");
   };
   auto split_tile = [&](int n) {
     split_row_item(Qp + (n & 1) * 3 * PART_Q, PART_Q, st, 0, tid);
@@ -323,14 +329,14 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
     if (tid < 2 * KB + 2 * QT) {
       const int r = tid < 2 * KB ? (tid & (KB - 1)) : (tid & (QT - 1));
       if (tid < KB) {
-        if (r < nk) tc::bulk_load(k_rows + r * LDP, kp + static_cast<int64_t>(k0 + r) * a.k_ss, 256, bar_ld);
+        if (r < nk) tc::bulk_load(k_rows + r * LDP, kp + static_cast<int64_t>(k0 + r) * a.k_ss, 4 * HD, bar_ld);
       } else if (tid < 2 * KB) {
-        if (r < nk) tc::bulk_load(v_rows + r * LDP, vp + static_cast<int64_t>(k0 + r) * a.v_ss, 256, bar_ld);
+        if (r < nk) tc::bulk_load(v_rows + r * LDP, vp + static_cast<int64_t>(k0 + r) * a.v_ss, 4 * HD, bar_ld);
       } else if (tid < 2 * KB + QT) {
         if (r < nq)
-          tc::bulk_load(q_rows + r * LDP, qp + static_cast<int64_t>(t_begin * QT + r) * a.q_ss, 256, bar_ld);
+          tc::bulk_load(q_rows + r * LDP, qp + static_cast<int64_t>(t_begin * QT + r) * a.q_ss, 4 * HD, bar_ld);
       } else if (r < nq) {
-        tc::bulk_load(o_rows + r * LDP, gp + static_cast<int64_t>(t_begin * QT + r) * a.do_ss, 256, bar_ld);
+        tc::bulk_load(o_rows + r * LDP, gp + static_cast<int64_t>(t_begin * QT + r) * a.do_ss, 4 * HD, bar_ld);
       }
     }
     griddep_wait();  // L, D, the cleared counters: the prep kernel's writes
@@ -338,14 +344,15 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
     cp_async_commit();
     err0 = !tc::mbar_wait(bar_ld, 0, WAIT_TIMEOUT_NS);
     cp_async_wait_all();
-    split_staged_row(Kp, PART_K, k_rows, tid, nk);
-    split_staged_row(Kp, PART_K, k_rows, tid + NT, nk);
-    split_staged_row(Qp, PART_Q, q_rows, tid, nq);
-    split_staged_row(dOp, PART_Q, o_rows, tid, nq);
+    split_staged_row<HD>(Kp, PART_K, k_rows, tid, nk);
+    split_staged_row<HD>(Kp, PART_K, k_rows, tid + NT, nk);
+    split_staged_row<HD>(Qp, PART_Q, q_rows, tid, nq);
+    split_staged_row<HD>(dOp, PART_Q, o_rows, tid, nq);
 #pragma unroll
     for (int c4 = 0; c4 < 4; ++c4) {
-      const float4 u = row < nk ? reinterpret_cast<const float4*>(v_rows + row * LDP + 16 * cg)[c4]
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 u = row < nk && 16 * cg < HD
+                           ? reinterpret_cast<const float4*>(v_rows + row * LDP + 16 * cg)[c4]
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
       vx[4 * c4] = u.x;
       vx[4 * c4 + 1] = u.y;
       vx[4 * c4 + 2] = u.z;
@@ -378,20 +385,20 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
   for (int c = 0; c < 16; ++c) dv[c] = dk[c] = 0.0f;
   if (mma_warp) {
     {  // every lane runs the loop (warp-uniform); one elected lane issues each MMA and commit
-      const uint32_t id128 = tc::idesc_f32acc(1, KB, QT);                       // M 128, N 64
-      const uint32_t id_mn = id128 | (1u << 16);                                 // B MN-major
-      const uint32_t id_dq = tc::idesc_f32acc(1, QT, 64) | (1u << 15) | (1u << 16);  // M 64
+      const uint32_t id128 = tc::idesc_f32acc(1, KB, QT);           // S^T, dP^T: M 128, N 64
+      const uint32_t id_mn = tc::idesc_f32acc(1, KB, HD) | (1u << 16);  // dV, dK: N = d, B MN
+      const uint32_t id_dq = tc::idesc_f32acc(1, QT, HD) | (1u << 15) | (1u << 16);  // M 64
       const uint32_t sK = tc::smem_u32(Kp), sS = tc::smem_u32(dSp);
       // S^T (the forward's product order) and dP^T (A: V's parts in TMEM) of tile n.
       auto issue_t1 = [&](int n) {
         const uint32_t sQ = tc::smem_u32(Qp + (n & 1) * 3 * PART_Q);
         const uint32_t sO = tc::smem_u32(dOp + (n & 1) * 3 * PART_Q);
-        issue6<4, PART_K, PART_Q, 256, 256, true>(tbase + T_S,
+        issue6<KSD, PART_K, PART_Q, 256, 256, true>(tbase + T_S,
                                                   tc::split_desc(tc::desc_kmajor(sK, 128, 1024)),
                                                   tc::split_desc(tc::desc_kmajor(sQ, 128, 1024)), id128);
-        issue6_tmem_a<PART_Q, 256>(
-            tbase + T_DP, [&](int i, int ks) { return tbase + T_V + 32 * i + 8 * ks; },
-            tc::split_desc(tc::desc_kmajor(sO, 128, 1024)), id128);
+        auto vcol = [&](int i, int ks) { return tbase + T_V + 32 * i + 8 * ks; };
+        issue6_tmem_a<PART_Q, 256, decltype(vcol), KSD>(
+            tbase + T_DP, vcol, tc::split_desc(tc::desc_kmajor(sO, 128, 1024)), id128);
         tc::commit_warp(bar_s);
       };
       // dV (A: P^T's parts in TMEM), dK, dQ (two windows of 64 keys) of tile n.
@@ -499,10 +506,12 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
       tc::tmem_ld16(tbase + lane_sel + T_DV + 16 * cg, xb);
       tc::tmem_ld16(tbase + lane_sel + T_DK + 16 * cg, xs);
       tc::tmem_wait_ld();
+      if (16 * cg < HD) {  // dV, dK have HD columns
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        dv[c] += xb[c];
-        dk[c] += xs[c];
+        for (int c = 0; c < 16; ++c) {
+          dv[c] += xb[c];
+          dk[c] += xs[c];
+        }
       }
       // dQ (M = 64): query row 16 (w % 4) + lane in lanes 0-15 of each quarter; the two windows.
       tc::tmem_ld16(tbase + lane_sel + T_DQ0 + 16 * cg, xb);
@@ -510,8 +519,8 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
       tc::tmem_wait_ld();
       const int qi = q0 + 16 * (w & 3) + lane;
       if (!chain) {
-        if (lane < 16 && qi < S && !err) {
-          float* dst = a.dq_part + ((static_cast<int64_t>(bh) * nkb + kb) * S + qi) * 64 + 16 * cg;
+        if (lane < 16 && qi < S && 16 * cg < HD && !err) {
+          float* dst = a.dq_part + ((static_cast<int64_t>(bh) * nkb + kb) * S + qi) * HD + 16 * cg;
 #pragma unroll
           for (int c4 = 0; c4 < 4; ++c4)
             __stcg(reinterpret_cast<float4*>(dst) + c4,
@@ -536,7 +545,7 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
           bar_sync(1, NT);
           go = s_int[2 + (n & 1)] != 0;
         }
-        if (go && lane < 16 && qi < S) {
+        if (go && lane < 16 && qi < S && 16 * cg < HD) {
           float4* dst = reinterpret_cast<float4*>(dq_base + qi * row_stride + 16 * cg);
 #pragma unroll
           for (int c4 = 0; c4 < 4; ++c4) {
@@ -590,11 +599,12 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
     }
     if (tid == 0) s_int[0] = chain ? -1 : atom_add_acq_rel(a.turn + bh, 1);
     __syncthreads();
-    const int64_t part_bytes = static_cast<int64_t>(nkb) * S * 64 * 4;
+    constexpr int C4 = HD / 4;  // float4 columns of a dQ, dK or dV row
+    const int64_t part_bytes = static_cast<int64_t>(nkb) * S * HD * 4;
     if (s_int[0] == nkb - 1 && part_bytes <= OFF_DS) {
       // The (b, h)'s partials, contiguous [nkb][S][64], as one bulk copy into shared memory (the
       // part buffers, free since the last T2; the dS^T buffer holds dV, dK), then summed there.
-      const float* part = a.dq_part + static_cast<int64_t>(bh) * nkb * S * 64;
+      const float* part = a.dq_part + static_cast<int64_t>(bh) * nkb * S * HD;
       const float* sp = reinterpret_cast<const float*>(sm);
       if (tid == 0) {
         tc::fence_async_global();  // the partials the count made visible, for the copy engine
@@ -602,15 +612,15 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
         tc::bulk_load(sm, part, static_cast<uint32_t>(part_bytes), bar_ld);
       }
       const bool ok = tc::mbar_wait(bar_ld, 1, WAIT_TIMEOUT_NS);
-      const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * 64;
-      float* dq_base = a.dqkv + static_cast<int64_t>(b) * S * row_stride + h * 64;
+      const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * HD;
+      float* dq_base = a.dqkv + static_cast<int64_t>(b) * S * row_stride + h * HD;
       // DETERMINISM: dQ = (((p0 + p1) + p2) + ...) * scale, as below.
-      for (int idx = tid; idx < S * 16 && ok; idx += NB) {
-        const int i = idx >> 4, c4 = idx & 15;
+      for (int idx = tid; idx < S * C4 && ok; idx += NB) {
+        const int i = idx / C4, c4 = idx % C4;
         const int last = CAUSAL ? min(nkb - 1, i / KB) : nkb - 1;
-        float4 v = reinterpret_cast<const float4*>(sp + i * 64)[c4];
+        float4 v = reinterpret_cast<const float4*>(sp + i * HD)[c4];
         for (int j = 1; j <= last; ++j) {
-          const float4 q = reinterpret_cast<const float4*>(sp + (j * S + i) * 64)[c4];
+          const float4 q = reinterpret_cast<const float4*>(sp + (j * S + i) * HD)[c4];
           v = make_float4(v.x + q.x, v.y + q.y, v.z + q.z, v.w + q.w);
         }
         reinterpret_cast<float4*>(dq_base + i * row_stride)[c4] =
@@ -618,25 +628,25 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
       }
       if (!ok && tid == 0) flag_timeout(a.err, a.sink);
     } else if (s_int[0] == nkb - 1) {
-      const float* part = a.dq_part + static_cast<int64_t>(bh) * nkb * S * 64;
-      const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * 64;
-      float* dq_base = a.dqkv + static_cast<int64_t>(b) * S * row_stride + h * 64;
+      const float* part = a.dq_part + static_cast<int64_t>(bh) * nkb * S * HD;
+      const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * HD;
+      float* dq_base = a.dqkv + static_cast<int64_t>(b) * S * row_stride + h * HD;
       // DETERMINISM: dQ = (((p0 + p1) + p2) + ...) * scale over the key blocks holding a key <=
       // the row (causal) or all of them. Eight float4 items per thread at a time, each key
       // block's loads for the eight issued together.
       constexpr int U = 8;
-      const int items = S * 16;
+      const int items = S * C4;
       for (int base = tid; base < items; base += U * NB) {
         float4 v[U];
         int last[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           const int idx = base + u * NB;
-          const int i = idx >> 4;
+          const int i = idx / C4;
           last[u] = idx < items ? (CAUSAL ? min(nkb - 1, i / KB) : nkb - 1) : -1;
           v[u] = last[u] >= 0
-                     ? __ldcg(reinterpret_cast<const float4*>(part + static_cast<int64_t>(i) * 64) +
-                              (idx & 15))
+                     ? __ldcg(reinterpret_cast<const float4*>(part + static_cast<int64_t>(i) * HD) +
+                              (idx % C4))
                      : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         for (int j = 1; j < nkb; ++j) {
@@ -645,8 +655,8 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
           for (int u = 0; u < U; ++u) {
             const int idx = base + u * NB;
             p[u] = j <= last[u] ? __ldcg(reinterpret_cast<const float4*>(
-                                             part + (static_cast<int64_t>(j) * S + (idx >> 4)) * 64) +
-                                         (idx & 15))
+                                             part + (static_cast<int64_t>(j) * S + idx / C4) * HD) +
+                                         (idx % C4))
                                 : make_float4(0.f, 0.f, 0.f, 0.f);
           }
 #pragma unroll
@@ -658,7 +668,7 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
         for (int u = 0; u < U; ++u) {
           const int idx = base + u * NB;
           if (last[u] >= 0)
-            reinterpret_cast<float4*>(dq_base + (idx >> 4) * row_stride)[idx & 15] =
+            reinterpret_cast<float4*>(dq_base + (idx / C4) * row_stride)[idx % C4] =
                 make_float4(v[u].x * a.scale, v[u].y * a.scale, v[u].z * a.scale,
                             v[u].w * a.scale);
         }
@@ -666,12 +676,12 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
     }
     // dV, dK rows out of shared memory: every 16 threads store one whole row.
     {
-      const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * 64;
-      for (int f = tid; f < 2 * KB * 16; f += NB) {
-        const int which = f / (KB * 16), r = (f >> 4) & (KB - 1), c4 = f & 15;
+      const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * HD;
+      for (int f = tid; f < 2 * KB * C4; f += NB) {
+        const int which = f / (KB * C4), r = (f / C4) % KB, c4 = f % C4;
         if (k0 + r < S) {
           float* dst = a.dqkv + (static_cast<int64_t>(b) * S + k0 + r) * row_stride +
-                       (2 - which) * a.H * 64 + h * 64;
+                       (2 - which) * a.H * HD + h * HD;
           reinterpret_cast<float4*>(dst)[c4] =
               reinterpret_cast<const float4*>((which ? sk : sv) + r * LDS)[c4];
         }
@@ -687,14 +697,19 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
 }  // namespace
 
 cudaError_t setup_bwd_tc_attributes() {
-  cudaError_t e = cudaFuncSetAttribute(bwd_tc_kernel<false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(bwd_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              SMEM_ALLOC);
+  const void* kernels[] = {reinterpret_cast<const void*>(bwd_tc_kernel<false, 64>),
+                           reinterpret_cast<const void*>(bwd_tc_kernel<true, 64>),
+                           reinterpret_cast<const void*>(bwd_tc_kernel<false, 32>),
+                           reinterpret_cast<const void*>(bwd_tc_kernel<true, 32>)};
+  for (const void* k : kernels) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
-cudaError_t launch_bwd_tc(const BwdArgs& args, int causal, cudaStream_t stream) {
+cudaError_t launch_bwd_tc(const BwdArgs& args, int head_dim, int causal, cudaStream_t stream) {
   BwdArgs a = args;
   a.n_kblocks = (a.S + KB - 1) / KB;
   int dev = 0, sms = 0;  // one block per SM: a wave is the SM count
@@ -704,8 +719,12 @@ cudaError_t launch_bwd_tc(const BwdArgs& args, int causal, cudaStream_t stream) 
   else
     a.wave_ctas = 0;
   const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(a.n_kblocks) * a.B * a.H));
-  if (causal) return launch_pdl(bwd_tc_kernel<true>, grid, dim3(NB), SMEM_ALLOC, stream, a);
-  return launch_pdl(bwd_tc_kernel<false>, grid, dim3(NB), SMEM_ALLOC, stream, a);
+  if (head_dim == 32) {
+    if (causal) return launch_pdl(bwd_tc_kernel<true, 32>, grid, dim3(NB), SMEM_ALLOC, stream, a);
+    return launch_pdl(bwd_tc_kernel<false, 32>, grid, dim3(NB), SMEM_ALLOC, stream, a);
+  }
+  if (causal) return launch_pdl(bwd_tc_kernel<true, 64>, grid, dim3(NB), SMEM_ALLOC, stream, a);
+  return launch_pdl(bwd_tc_kernel<false, 64>, grid, dim3(NB), SMEM_ALLOC, stream, a);
 }
 
 }  // namespace cfa

@@ -84,7 +84,8 @@ int fwd_impl(const float* q, const int64_t q_strides[3], const float* k,
   if (!strides_ok(q_strides) || !strides_ok(k_strides) || !strides_ok(v_strides))
     return CFA_ERR_ALIGNMENT;
   const bool d64 = head_dim == 64;
-  const bool tc = d64 && pair == Pair::kTensorCore;
+  // The tensor-core pair takes head dims 64 and 32; 128 runs on the CUDA-core kernels.
+  const bool tc = (d64 || head_dim == 32) && pair == Pair::kTensorCore;
   st = tc    ? setup(g_fwd_tc_once, cfa::setup_fwd_tc_attributes)
        : d64 ? setup(g_fwd_once, cfa::setup_fwd_attributes)
              : setup(g_hd_once, cfa::setup_hd_attributes);
@@ -113,7 +114,7 @@ int fwd_impl(const float* q, const int64_t q_strides[3], const float* k,
   const int bm = d64 ? cfa::fwd_tile_rows(seq) : cfa::hd_fwd_rows(static_cast<int>(head_dim), seq);
   a.n_qtiles = static_cast<int>((seq + bm - 1) / bm);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const cudaError_t e = tc    ? cfa::launch_fwd_tc(a, causal != 0, s)
+  const cudaError_t e = tc    ? cfa::launch_fwd_tc(a, static_cast<int>(head_dim), causal != 0, s)
                         : d64 ? cfa::launch_fwd(a, causal != 0, s)
                               : cfa::launch_hd_fwd(a, static_cast<int>(head_dim), causal != 0, s);
   return e == cudaSuccess ? CFA_OK : CFA_ERR_LAUNCH;
@@ -144,7 +145,7 @@ int bwd_impl(const float* q, const int64_t q_strides[3], const float* k,
   // The tensor-core backward pairs with the tensor-core forward (the scores it recomputes are the
   // forward's, bit for bit), at every length: its dQ takes the no-wait partials when the
   // workspace holds them, else the turn chain (the same sums, bit for bit).
-  const bool tc = d64 && pair == Pair::kTensorCore;
+  const bool tc = (d64 || head_dim == 32) && pair == Pair::kTensorCore;
   st = tc    ? setup(g_bwd_tc_once, cfa::setup_bwd_tc_attributes)
        : d64 ? setup(g_bwd_once, cfa::setup_bwd_attributes)
              : setup(g_hd_once, cfa::setup_hd_attributes);
@@ -211,7 +212,7 @@ int bwd_impl(const float* q, const int64_t q_strides[3], const float* k,
   a.dq_part = (lay.total_fast > lay.total && workspace_bytes >= lay.total_fast)
                   ? reinterpret_cast<float*>(ws + lay.part_off)
                   : nullptr;
-  e = tc    ? cfa::launch_bwd_tc(a, causal != 0, s)
+  e = tc    ? cfa::launch_bwd_tc(a, static_cast<int>(head_dim), causal != 0, s)
       : d64 ? cfa::launch_bwd(a, causal != 0, s)
             : cfa::launch_hd_bwd(a, static_cast<int>(head_dim), causal != 0, s);
   return e == cudaSuccess ? CFA_OK : CFA_ERR_LAUNCH;
@@ -225,7 +226,7 @@ int* error_sink() { return g_sink.load(std::memory_order_relaxed); }
 
 extern "C" {
 
-int cfa_abi_version(void) { return (2 << 16) | 1; }
+int cfa_abi_version(void) { return (2 << 16) | 2; }
 
 const char* cfa_strerror(int status) {
   switch (status) {
@@ -309,6 +310,25 @@ int cfa_bwd_f32_d64_ffma(const float* q, const int64_t q_strides[3], const float
   return bwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, d_o, do_strides, dqkv,
                   workspace, workspace_bytes, batch, heads, seq, head_dim, scale, causal, stream,
                   false, Pair::kFfma);
+}
+
+int cfa_fwd_f32_ffma(const float* q, const int64_t q_strides[3], const float* k,
+                     const int64_t k_strides[3], const float* v, const int64_t v_strides[3],
+                     float* o, float* lse, int64_t batch, int64_t heads, int64_t seq,
+                     int64_t head_dim, float scale, int causal, void* stream) {
+  return fwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, batch, heads, seq, head_dim,
+                  scale, causal, stream, true, Pair::kFfma);
+}
+
+int cfa_bwd_f32_ffma(const float* q, const int64_t q_strides[3], const float* k,
+                     const int64_t k_strides[3], const float* v, const int64_t v_strides[3],
+                     const float* o, const float* lse, const float* d_o,
+                     const int64_t do_strides[3], float* dqkv, void* workspace,
+                     size_t workspace_bytes, int64_t batch, int64_t heads, int64_t seq,
+                     int64_t head_dim, float scale, int causal, void* stream) {
+  return bwd_impl(q, q_strides, k, k_strides, v, v_strides, o, lse, d_o, do_strides, dqkv,
+                  workspace, workspace_bytes, batch, heads, seq, head_dim, scale, causal, stream,
+                  true, Pair::kFfma);
 }
 
 int cfa_bwd_f32(const float* q, const int64_t q_strides[3], const float* k,

@@ -117,13 +117,14 @@ size_t bwd_smem_bytes();
 
 // Launchers (return a cudaError_t from the launch). launch_fwd sets the query-tile count itself.
 cudaError_t launch_fwd(const FwdArgs& a, int causal, cudaStream_t stream);
-// The tensor-core forward (fwd_tc.cu): 128-query tiles, sets the query-tile count itself.
-cudaError_t launch_fwd_tc(const FwdArgs& a, int causal, cudaStream_t stream);
+// The tensor-core forward (fwd_tc.cu): 128-query tiles, head dim 64 or 32; sets the query-tile
+// count itself.
+cudaError_t launch_fwd_tc(const FwdArgs& a, int head_dim, int causal, cudaStream_t stream);
 // Reads and clears the tensor-core forward's device error flag (1: an MMA wait expired).
 cudaError_t fwd_tc_status(int* flag);
-// The tensor-core backward (bwd_tc.cu): 128-key blocks, the no-wait dQ path only (dq_part set);
-// sets the key-block count itself.
-cudaError_t launch_bwd_tc(const BwdArgs& a, int causal, cudaStream_t stream);
+// The tensor-core backward (bwd_tc.cu): 128-key blocks, head dim 64 or 32; dQ by the partials
+// (dq_part set) or the turn chain; sets the key-block count itself.
+cudaError_t launch_bwd_tc(const BwdArgs& a, int head_dim, int causal, cudaStream_t stream);
 cudaError_t launch_bwd_prep(const PrepArgs& a, cudaStream_t stream);
 cudaError_t launch_bwd(const BwdArgs& a, int causal, cudaStream_t stream);
 

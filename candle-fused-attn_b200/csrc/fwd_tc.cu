@@ -110,13 +110,15 @@ __device__ __forceinline__ void row_item(int c, int& r, int& kc) {
   kc = (c >> 3) & 7;
 }
 
-// Copy this thread's row item of a strided [seq, 64] operand, rows from r0 (rows past the end
-// are zero-filled: source size 0, address clamped to row 0).
+// Copy this thread's row item of a strided [seq, HD] operand, rows from r0, as part of a 64-wide
+// row (rows past the end and, for HD = 32, chunks past the head dim are zero-filled: source size
+// 0, address clamped to row 0).
+template <int HD>
 __device__ __forceinline__ void stage_item(unsigned char* st, const float* src, int64_t stride,
                                            int r0, int seq) {
   int r, kc;
   row_item(threadIdx.x, r, kc);
-  const bool ok = r0 + r < seq;
+  const bool ok = r0 + r < seq && 8 * kc < HD;
   const float* g = src + static_cast<int64_t>(ok ? r0 + r : 0) * stride + 8 * kc;
   cp_async16(st + 16 * threadIdx.x, g, ok ? 16 : 0);
   cp_async16(st + 16 * (NSM + threadIdx.x), g + 4, ok ? 16 : 0);
@@ -158,6 +160,29 @@ __device__ __forceinline__ void cp_async_wait_group() {
   "elect.sync _|e, 0xffffffff;\n\t"                                       \
   "setp.ne.b32 pf, %1, %1;\n\tsetp.eq.b32 pt, %1, %1;\n\t"
 static_assert(PART >> 4 == 512, "part stride in descriptor units");
+
+// Head dim 32 (S = Q K^T over 32 dims): the K-steps 0 and 1 of the same window -- the parts of
+// K-steps 2 and 3 are zero (the rows are zero-filled past the head dim), and adding exact zeros
+// leaves the accumulator unchanged, so these twelve MMAs give the bits of the twenty-four.
+__device__ __forceinline__ void issue_split_mma_d32(uint32_t d, uint32_t a_tmem, uint32_t b_base,
+                                                    uint32_t idesc) {
+  const tc::Desc bd = tc::split_desc(tc::desc_kmajor(b_base, 128, 1024));
+  asm volatile(MMA_BLOCK_BEGIN
+      MMA6(0, 512, pf)
+      MMA6(32, 0, pt)
+      MMA6(0, 1024, pt)
+      MMA6(32, 512, pt)
+      MMA6(64, 0, pt)
+      MMA6(8, 528, pt)
+      MMA6(40, 16, pt)
+      MMA6(8, 1040, pt)
+      MMA6(40, 528, pt)
+      MMA6(72, 16, pt)
+      MMA6(0, 0, pt)
+      MMA6(8, 16, pt)
+      "}\n" ::"r"(d), "r"(a_tmem), "r"(bd.lo), "r"(bd.hi), "r"(idesc)
+      : "memory");
+}
 
 template <bool B_MN>
 __device__ __forceinline__ void issue_split_mma(uint32_t d, uint32_t a_tmem, uint32_t b_base,
@@ -280,8 +305,9 @@ struct RowState {
   float m, lpart, alpha_prev;
 };
 
-template <bool CAUSAL>
+template <bool CAUSAL, int HD>
 __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
+  static_assert(HD == 64 || HD == 32, "head dims of the tensor-core forward");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = tc::smem_u32(smem_raw);
   unsigned char* sm = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -346,9 +372,9 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
   // into TMEM; K(2), V(1) left in flight. Then the MMA warp issues S0(0) and S1(0).
   float qx[NTILE][CW];
   if (!mma_warp) {
-    stage_item(Kst, kp, a.k_ss, 0, S);
-    if (T > 1) stage_item(Kp + 2 * PARTS, kp, a.k_ss, KT, S);
-    stage_item(Vst, vp, a.v_ss, 0, S);
+    stage_item<HD>(Kst, kp, a.k_ss, 0, S);
+    if (T > 1) stage_item<HD>(Kp + 2 * PARTS, kp, a.k_ss, KT, S);
+    stage_item<HD>(Vst, vp, a.v_ss, 0, S);
     cp_async_commit();
 #pragma unroll
     for (int t = 0; t < NTILE; ++t) {
@@ -356,7 +382,7 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
       const float4* src = reinterpret_cast<const float4*>(qp + static_cast<int64_t>(qi) * a.q_ss + CW * cq);
 #pragma unroll
       for (int c4 = 0; c4 < CW / 4; ++c4) {
-        const float4 u = qi < S ? __ldg(src + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 u = qi < S && CW * cq < HD ? __ldg(src + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
         qx[t][4 * c4] = u.x;
         qx[t][4 * c4 + 1] = u.y;
         qx[t][4 * c4 + 2] = u.z;
@@ -384,9 +410,9 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
     split_item(Vp, Vst);
     tc::fence_async_smem();
     // In flight during key tile 0: K(2), then V(1) (two cp.async groups, in that order).
-    if (T > 2) stage_item(Kst, kp, a.k_ss, 2 * KT, S);
+    if (T > 2) stage_item<HD>(Kst, kp, a.k_ss, 2 * KT, S);
     cp_async_commit();
-    if (T > 1) stage_item(Vst, vp, a.v_ss, KT, S);
+    if (T > 1) stage_item<HD>(Vst, vp, a.v_ss, KT, S);
     cp_async_commit();
   }
   tc::fence_before_sync();
@@ -398,12 +424,14 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
     // Per key tile n and tile t: once P(t, n) is in TMEM (and V(n) in place), P V(t, n); once that
     // has completed -- S(t, n + 1) overwrites P(t, n) -- and K(n + 1) is in place, S(t, n + 1).
     // The whole warp runs the issue code (warp-uniform operands); one elected lane issues.
-    const uint32_t idesc = tc::idesc_f32acc(1, QT, KT);
+    const uint32_t idesc = tc::idesc_f32acc(1, QT, KT);     // S: N = 64 keys
+    const uint32_t idesc_pv = tc::idesc_f32acc(1, QT, HD);  // P V: N = the head dim
     const uint32_t sK = tc::smem_u32(Kp), sV = tc::smem_u32(Vp);
 #pragma unroll
     for (int t = 0; t < NTILE; ++t)
       if (Tt[t] > 0) {
-        issue_split_mma<false>(tbase + T_SP(t), tbase + T_Q(t), sK, idesc);
+        if constexpr (HD == 32) issue_split_mma_d32(tbase + T_SP(t), tbase + T_Q(t), sK, idesc);
+        else issue_split_mma<false>(tbase + T_SP(t), tbase + T_Q(t), sK, idesc);
         tc::commit_warp(bar_s + t);
       }
     for (int n = 0; n < T; ++n) {
@@ -417,7 +445,7 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
           v_ready = true;
         }
         tc::fence_after_sync();
-        issue_split_mma<true>(tbase + T_O(t), tbase + T_SP(t), sV + PARTS * (n & 1), idesc);
+        issue_split_mma<true>(tbase + T_O(t), tbase + T_SP(t), sV + PARTS * (n & 1), idesc_pv);
         tc::commit_warp(bar_o + t);
         if (n + 1 < Tt[t]) {
           err |= !tc::mbar_wait(bar_o + t, n & 1, wait_ns(err));
@@ -426,8 +454,11 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
             k_ready = true;
           }
           tc::fence_after_sync();
-          issue_split_mma<false>(tbase + T_SP(t), tbase + T_Q(t), sK + PARTS * ((n + 1) % 3),
-                                 idesc);
+          if constexpr (HD == 32)
+            issue_split_mma_d32(tbase + T_SP(t), tbase + T_Q(t), sK + PARTS * ((n + 1) % 3), idesc);
+          else
+            issue_split_mma<false>(tbase + T_SP(t), tbase + T_Q(t), sK + PARTS * ((n + 1) % 3),
+                                   idesc);
           tc::commit_warp(bar_s + t);
         }
       }
@@ -461,7 +492,7 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
       r = tid - BQ - 2 * KT;
       src = a.v + nb_b * a.v_sb + nb_h * a.v_sh + static_cast<int64_t>(r) * a.v_ss;
     }
-    if (r < S) asm volatile("cp.async.bulk.prefetch.L2.global [%0], 256;" ::"l"(src) : "memory");
+    if (r < S) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "n"(4 * HD) : "memory");
   };
 
   const uint64_t sc2 = tc::pack2(a.scale, a.scale);
@@ -489,12 +520,14 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
     if (n > 0) {  // O = O * alpha(n - 1) + P V(t, n - 1)
       err |= !tc::mbar_wait(bar_o + t, (n - 1) & 1, wait_ns(err));
       tc::fence_after_sync();
-      float ob[CW];
-      tmem_ld1(tbase + lane_sel + T_O(t) + CW * cq, ob);
-      const uint64_t al2 = tc::pack2(rs.alpha_prev, rs.alpha_prev);
+      if (CW * cq < HD) {  // O has HD columns
+        float ob[CW];
+        tmem_ld1(tbase + lane_sel + T_O(t) + CW * cq, ob);
+        const uint64_t al2 = tc::pack2(rs.alpha_prev, rs.alpha_prev);
 #pragma unroll
-      for (int c = 0; c < CW; c += 2)
-        fma2x(rs.acc[c], rs.acc[c + 1], al2, tc::pack2(ob[c], ob[c + 1]));
+        for (int c = 0; c < CW; c += 2)
+          fma2x(rs.acc[c], rs.acc[c + 1], al2, tc::pack2(ob[c], ob[c + 1]));
+      }
     }
     if (n == Tn) return;
     const int k0 = n * KT;
@@ -569,7 +602,7 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(bar_k + (n & 1));
     }
-    if (n + 3 < T) stage_item(Kst, kp, a.k_ss, (n + 3) * KT, S);
+    if (n + 3 < T) stage_item<HD>(Kst, kp, a.k_ss, (n + 3) * KT, S);
     cp_async_commit();
   };
   // V(n + 1) into V buffer (n + 1) % 2 (it held V(n - 1): both P V(t, n - 1) have completed --
@@ -582,7 +615,7 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(bar_v + ((n + 1) & 1));
     }
-    if (n + 2 < T) stage_item(Vst, vp, a.v_ss, (n + 2) * KT, S);
+    if (n + 2 < T) stage_item<HD>(Vst, vp, a.v_ss, (n + 2) * KT, S);
     cp_async_commit();
   };
 
@@ -632,10 +665,11 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
       }
     }
     __syncthreads();
-    for (int f = tid; f < BQ * 16; f += NBLK) {
-      const int r = f >> 4, c4 = f & 15;
+    constexpr int C4 = HD / 4;  // float4 columns of an O row [b, s, h, HD]
+    for (int f = tid; f < BQ * C4; f += NBLK) {
+      const int r = f / C4, c4 = f % C4;
       if (q0 + r < S)
-        reinterpret_cast<float4*>(a.o + ((static_cast<int64_t>(b) * S + q0 + r) * a.H + h) * 64)[c4] =
+        reinterpret_cast<float4*>(a.o + ((static_cast<int64_t>(b) * S + q0 + r) * a.H + h) * HD)[c4] =
             reinterpret_cast<const float4*>(o_rows + r * LDO)[c4];
     }
   }
@@ -648,14 +682,19 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
 }  // namespace
 
 cudaError_t setup_fwd_tc_attributes() {
-  cudaError_t e = cudaFuncSetAttribute(fwd_tc_kernel<false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(fwd_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              SMEM_ALLOC);
+  const void* kernels[] = {reinterpret_cast<const void*>(fwd_tc_kernel<false, 64>),
+                           reinterpret_cast<const void*>(fwd_tc_kernel<true, 64>),
+                           reinterpret_cast<const void*>(fwd_tc_kernel<false, 32>),
+                           reinterpret_cast<const void*>(fwd_tc_kernel<true, 32>)};
+  for (const void* k : kernels) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
-cudaError_t launch_fwd_tc(const FwdArgs& args, int causal, cudaStream_t stream) {
+cudaError_t launch_fwd_tc(const FwdArgs& args, int head_dim, int causal, cudaStream_t stream) {
   FwdArgs a = args;
   a.n_qtiles = (a.S + BQ - 1) / BQ;  // blocks of 256 queries per (batch, head)
   int dev = 0, sms = 0;  // one block per SM: a wave is the SM count
@@ -665,8 +704,12 @@ cudaError_t launch_fwd_tc(const FwdArgs& args, int causal, cudaStream_t stream) 
   else
     a.wave_ctas = 0;
   const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(a.n_qtiles) * a.B * a.H));
-  if (causal) return launch_pdl(fwd_tc_kernel<true>, grid, dim3(NBLK), SMEM_ALLOC, stream, a);
-  return launch_pdl(fwd_tc_kernel<false>, grid, dim3(NBLK), SMEM_ALLOC, stream, a);
+  if (head_dim == 32) {
+    if (causal) return launch_pdl(fwd_tc_kernel<true, 32>, grid, dim3(NBLK), SMEM_ALLOC, stream, a);
+    return launch_pdl(fwd_tc_kernel<false, 32>, grid, dim3(NBLK), SMEM_ALLOC, stream, a);
+  }
+  if (causal) return launch_pdl(fwd_tc_kernel<true, 64>, grid, dim3(NBLK), SMEM_ALLOC, stream, a);
+  return launch_pdl(fwd_tc_kernel<false, 64>, grid, dim3(NBLK), SMEM_ALLOC, stream, a);
 }
 
 cudaError_t fwd_tc_status(int* flag) {

@@ -32,7 +32,8 @@
  * pair (csrc/fwd_tc.cu, csrc/bwd_tc.cu). A backward must run on the forward's L of the same pair
  * (it recomputes the forward's scores bit for bit); the entry points fix the pair, so there is
  * no process-wide setting two users could disagree on. The CUDA-core pair stays available under
- * its own names (cfa_fwd_f32_d64_ffma, cfa_bwd_f32_d64_ffma) for comparison.
+ * its own names (cfa_fwd_f32_d64_ffma, cfa_bwd_f32_d64_ffma; cfa_fwd_f32_ffma, cfa_bwd_f32_ffma
+ * at every head dim) for comparison.
  *
  * Conventions (the reference's, src/cuda.rs:60-67 and src/lib.rs:165-188):
  *  - Every pointer is a device pointer at the operand's first element, on the current device.
@@ -115,9 +116,11 @@ int cfa_bwd_f32_d64(const float* q, const int64_t q_strides[3],
 
 /* Head dims 32, 64 and 128 (no counterpart in the reference's CUDA path, which takes 64 only).
  * The same arguments, layouts (with 64 replaced by head_dim), orders of summation and results as
- * the _d64 entry points; for head_dim 64 they ARE those entry points. Any other head_dim returns
- * CFA_ERR_HEAD_DIM. Workspace sizes take the head dim because the dQ partials hold head_dim floats
- * per row (the rest of the workspace does not depend on it). */
+ * the _d64 entry points; for head_dim 64 they ARE those entry points. Head dims 64 and 32 run the
+ * tensor-core pair (32: the head-dim-64 kernels on rows zero-filled past the head dim, the
+ * all-zero K-steps skipped), 128 the CUDA-core kernels of csrc/hd_ffma.cu. Any other head_dim
+ * returns CFA_ERR_HEAD_DIM. Workspace sizes take the head dim because the dQ partials hold
+ * head_dim floats per row (the rest of the workspace does not depend on it). */
 int cfa_fwd_f32(const float* q, const int64_t q_strides[3],
                 const float* k, const int64_t k_strides[3],
                 const float* v, const int64_t v_strides[3],
@@ -160,6 +163,25 @@ int cfa_bwd_f32_d64_ffma(const float* q, const int64_t q_strides[3],
                          float* dqkv, void* workspace, size_t workspace_bytes,
                          int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                          float scale, int causal, void* stream);
+
+/* The CUDA-core pair at head dims 32, 64 and 128 (the cfa_fwd_f32 / cfa_bwd_f32 contract): for 64
+ * the _d64_ffma entry points, for 32 and 128 csrc/hd_ffma.cu. At 128 it is what cfa_fwd_f32 runs;
+ * at 32 it stays for comparison with the tensor-core pair. The same pairing rule applies. */
+int cfa_fwd_f32_ffma(const float* q, const int64_t q_strides[3],
+                     const float* k, const int64_t k_strides[3],
+                     const float* v, const int64_t v_strides[3],
+                     float* o, float* lse,
+                     int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                     float scale, int causal, void* stream);
+
+int cfa_bwd_f32_ffma(const float* q, const int64_t q_strides[3],
+                     const float* k, const int64_t k_strides[3],
+                     const float* v, const int64_t v_strides[3],
+                     const float* o, const float* lse,
+                     const float* d_o, const int64_t do_strides[3],
+                     float* dqkv, void* workspace, size_t workspace_bytes,
+                     int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                     float scale, int causal, void* stream);
 
 /* Size of the static scratch of cfa_bwd_f32_d64_noalloc (4 MiB per GPU that loads the library). */
 #define CFA_NOALLOC_SCRATCH_BYTES (4u << 20)
@@ -253,7 +275,7 @@ int cfa_matmul_status(void* stream);
 const char* cfa_strerror(int status);
 
 /* ABI version: (major << 16) | minor (2.0: one kernel pair per entry point, the error sink;
- * 2.1: the projection GEMM). */
+ * 2.1: the projection GEMM; 2.2: head dim 32 on the tensor cores, the generic CUDA-core pair). */
 int cfa_abi_version(void);
 
 #ifdef __cplusplus
