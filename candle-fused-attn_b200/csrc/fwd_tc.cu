@@ -643,7 +643,7 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
     for (int t = 0; t < NTILE; ++t)
       if (Tt[t] > 0) tc::mbar_wait(bar_o + t, (Tt[t] - 1) & 1, WAIT_TIMEOUT_NS);
   } else {
-    // O = acc / l through shared memory (the K part buffers: every MMA has completed), rows of
+    // O = acc * (1 / l) through shared memory (the K part buffers: every MMA has completed), rows of
     // LDO floats (a 16-byte rotation per row keeps both passes conflict-free); then every 16
     // threads store one whole row of O [b, s, h, 64].
     float* o_rows = reinterpret_cast<float*>(sm + OFF_K);
@@ -655,11 +655,14 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
 #pragma unroll
         for (int g = 1; g < NQ; ++g) l += lr[g];
         float* orow = o_rows + (t * QT + row) * LDO + CW * cq;
+        // O = acc * RN(1 / l): one IEEE reciprocal a row, then products (a rounding more than a
+        // division per element, 4 µs less per canvas forward; O stays below the FFMA pair's error).
+        const float rl = __frcp_rn(l);
 #pragma unroll
         for (int c4 = 0; c4 < CW / 4; ++c4)
           reinterpret_cast<float4*>(orow)[c4] =
-              make_float4(__fdiv_rn(st[t].acc[4 * c4], l), __fdiv_rn(st[t].acc[4 * c4 + 1], l),
-                          __fdiv_rn(st[t].acc[4 * c4 + 2], l), __fdiv_rn(st[t].acc[4 * c4 + 3], l));
+              make_float4(st[t].acc[4 * c4] * rl, st[t].acc[4 * c4 + 1] * rl,
+                          st[t].acc[4 * c4 + 2] * rl, st[t].acc[4 * c4 + 3] * rl);
         const int qi = q0 + QT * t + row;
         if (cq == 0 && qi < S) a.lse[static_cast<int64_t>(bh) * S + qi] = st[t].m + logf(l);
       }
