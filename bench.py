@@ -535,7 +535,8 @@ def main():
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
     if args.mode == "kernels" and args.head_dim != D:
-        # the canvas-shaped projection [64, 240, 1152] as 384 / d heads of d (csrc/hd_ffma.cu)
+        # the canvas-shaped projection [64, 240, 1152] as 384 / d heads of d (d = 32: the
+        # tensor-core pair; d = 128: csrc/hd_ffma.cu)
         from oracle import oracle
         d = args.head_dim
         h = H * D // d
