@@ -33,6 +33,16 @@
 // S^T takes its six products in the forward kernel's order (A and B swapped), so the scores match
 // fwd_tc.cu's and the recomputed P matches the forward's L.
 //
+// Split tail. With one block per SM, a grid of U key blocks runs in waves of P (the SM count); the
+// R = U mod P key blocks of the partial last wave would hold R SMs for a whole block's time while
+// the others idle. On the no-wait path (non-causal), the launcher runs each of them as k blocks
+// (k = min(query tiles, P / R)), part p taking the p-th contiguous range of query tiles: the
+// helpers (p >= 1) store each tile's dV, dK TMEM windows -- the values one block would fold --
+// in workspace space the 128-key blocks leave unused, and raise a flag; the first part folds its
+// own tiles, then the helpers' windows in tile order, so dV, dK are the one-block sums bit for
+// bit, and only it writes dV, dK and counts the key block in. The helpers never wait on anyone,
+// so the first part's bounded wait always ends.
+//
 // Every mbarrier wait is bounded; an expired wait sets the workspace error flag
 // (cfa_bwd_status reads it) and the block writes nothing.
 #include <cuda_bf16.h>
@@ -73,6 +83,18 @@ static_assert(SMEM_ALLOC <= 232448, "shared memory per block");
 constexpr uint32_t T_V = 0, T_S = 96, T_DP = 160, T_DV = 224, T_DK = 288, T_DQ0 = 352,
                    T_DQ1 = 416;
 constexpr uint32_t TMEM_COLS = 512;
+
+// A split tail's window of one query tile (dV, dK sums of the tile as TMEM holds them, before the
+// fold): WIN floats as float4 items [which: dV, dK][c4][column group][key row], so a warp's 32
+// rows of one item are 512 contiguous bytes (coalesced stores, conflict-free shared-memory reads).
+template <int HD>
+struct TailWindow {
+  static constexpr int WIN = 2 * KB * HD;
+  static constexpr int CG = HD / 16;  // column groups of 16 floats
+  __host__ __device__ static constexpr int item(int which, int c4, int cg, int row) {
+    return ((which * 4 + c4) * CG + cg) * KB + row;
+  }
+};
 
 // P^T part i of K-step ks (queries 16 ks .. 16 ks + 15: the columns of group ks): parts 0, 1 over
 // that group's S^T columns, part 2 over its first 8 dP^T columns.
@@ -200,6 +222,8 @@ template <bool CAUSAL, int HD>
 __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
   static_assert(HD == 64 || HD == 32, "head dims of the tensor-core backward");
   constexpr int KSD = HD / 16;  // K-steps of the products that reduce over the head dim
+  constexpr int WIN = TailWindow<HD>::WIN;
+  constexpr auto win4 = TailWindow<HD>::item;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = tc::smem_u32(smem_raw);
   unsigned char* sm = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -238,6 +262,20 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
     __syncthreads();
     ticket = s_int[1];
   }
+  // Split tail (no-wait path): the key blocks from a.tail_base on -- the grid's last partial wave
+  // -- run as a.tail_parts blocks each, part p taking the p-th contiguous range of the query tiles.
+  // The helpers (parts >= 1, first in the grid) leave their tiles' dV, dK windows in a.tail_win;
+  // the first part (last in the grid) adds them after its own, in tile order: the same sums as one
+  // block, bit for bit. Only the first part writes dV, dK and counts the key block in.
+  int part = 0, nparts = 1, tail_r = 0;
+  if (!CAUSAL && !chain && a.tail_parts > 1 && ticket >= a.tail_base) {
+    const int j = ticket - a.tail_base;
+    const int g = j / a.tail_units;
+    tail_r = j - g * a.tail_units;
+    nparts = a.tail_parts;
+    part = g + 1 < nparts ? g + 1 : 0;
+    ticket = a.tail_base + tail_r;
+  }
   const int kb = chain ? ticket / BH : ticket % nkb;
   const int bh = chain ? ticket % BH : ticket / nkb;
   const int b = bh / a.H, h = bh % a.H;
@@ -248,11 +286,14 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
   const float* gp = a.d_o + b * a.do_sb + h * a.do_sh;
   const float* lp = a.lse + static_cast<int64_t>(bh) * S;
   const float* dp = a.dsum + static_cast<int64_t>(bh) * S;
-  const int t_begin = CAUSAL ? k0 / QT : 0;  // queries before the block's first key see none
+  const int t_first = CAUSAL ? k0 / QT : 0;  // queries before the block's first key see none
+  const int n_all = (S + QT - 1) / QT - t_first;  // the key block's query tiles, >= 1 (k0 < S)
+  const int n_lo = part * n_all / nparts, n_hi = (part + 1) * n_all / nparts;
+  const int t_begin = t_first + n_lo;  // this block's first query tile
   int* turn = a.turn + static_cast<int64_t>(bh) * a.n_qtiles;  // turn chain: per 64-query tile
   const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * HD;  // dqkv floats per (b, s)
   float* dq_base = a.dqkv + static_cast<int64_t>(b) * S * row_stride + h * HD;
-  const int N = (S + QT - 1) / QT - t_begin;  // query tiles, >= 1 (k0 < S)
+  const int N = n_hi - n_lo;  // this block's query tiles, >= 1 (a.tail_parts <= n_all)
   bool err0 = false;
 
   if (tid == 0) {
@@ -287,7 +328,7 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
   // this wave computes and HBM is otherwise idle (one 256-byte row per thread).
   auto prefetch_next_wave = [&]() {
     const int nb = ticket + a.wave_ctas;
-    if (a.wave_ctas <= 0 || nb >= static_cast<int>(gridDim.x) || tid >= 2 * KB + 2 * QT) return;
+    if (a.wave_ctas <= 0 || nparts > 1 || nb >= nkb * BH || tid >= 2 * KB + 2 * QT) return;
     const int nkb2 = chain ? nb / BH : nb % nkb, nbh = chain ? nb % BH : nb / nkb;
     const int nb_b = nbh / a.H, nb_h = nbh % a.H;
     const int r = tid < 2 * KB ? (tid & (KB - 1)) : (tid & (QT - 1));
@@ -377,6 +418,7 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
   tc::fence_after_sync();
 
   bool err = err0;
+  uint32_t ld_phase = 1;  // bar_ld's next phase: the prologue's copies completed phase 0
   const int key = k0 + row;
   const uint64_t nsc2 = tc::pack2(-a.scale, -a.scale);     // L - s scale = fma(s, -scale, L)
   const uint64_t nl2e2 = tc::pack2(-LOG2E, -LOG2E);        // e^-y = 2^(-y log2 e)
@@ -507,10 +549,22 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
       tc::tmem_ld16(tbase + lane_sel + T_DK + 16 * cg, xs);
       tc::tmem_wait_ld();
       if (16 * cg < HD) {  // dV, dK have HD columns
+        if (part == 0) {
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          dv[c] += xb[c];
-          dk[c] += xs[c];
+          for (int c = 0; c < 16; ++c) {
+            dv[c] += xb[c];
+            dk[c] += xs[c];
+          }
+        } else {  // a split tail's helper: the tile's windows for the first part (win4)
+          float4* wv = reinterpret_cast<float4*>(a.tail_win) +
+                       (static_cast<int64_t>(tail_r) * n_all + n_lo + n) * (WIN / 4);
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            __stcg(wv + win4(0, c4, cg, row),
+                   make_float4(xb[4 * c4], xb[4 * c4 + 1], xb[4 * c4 + 2], xb[4 * c4 + 3]));
+            __stcg(wv + win4(1, c4, cg, row),
+                   make_float4(xs[4 * c4], xs[4 * c4 + 1], xs[4 * c4 + 2], xs[4 * c4 + 3]));
+          }
         }
       }
       // dQ (M = 64): query row 16 (w % 4) + lane in lanes 0-15 of each quarter; the two windows.
@@ -571,10 +625,63 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
     }
   }
   cp_async_wait_all();
+  if (part == 0 && nparts > 1) {
+    // The first part of a split key block: the helpers' tile windows, added after its own tiles'
+    // in tile order (dv = ((w0 + w1) + w2) + ..., as one block folds them).
+    if (tid == 0) {
+      bool ok = true;
+      for (int p = 1; p < nparts && ok; ++p)
+        ok = wait_turn_bounded(a.tail_flag + tail_r * nparts + p, 1, a.err, a.timeout_ns, a.sink);
+      s_int[2] = ok ? 1 : 0;
+      // ORDER: with the barrier below, extends thread 0's acquires to the block (the windows and
+      // the helpers' dQ partials; the count below passes the partials on to the summing block).
+      __threadfence();
+    }
+    __syncthreads();
+    const bool ok = s_int[2] != 0;
+    err |= !ok;
+    // The windows travel by bulk copy into shared memory (free since the last T2), up to WCH
+    // tiles at a time: loads a thread issued itself would each wait out the L2 round trip.
+    constexpr int WCH = OFF_BAR / (4 * WIN);
+    static_assert(WCH >= 1, "one tile's windows fit in shared memory");
+    const float4* wsm = reinterpret_cast<const float4*>(sm);
+    for (int t0 = n_hi; ok && t0 < n_all; t0 += WCH) {
+      const int nt = min(WCH, n_all - t0);
+      if (tid == 0) {
+        tc::fence_async_global();  // the windows the acquires made visible, for the copy engine
+        tc::mbar_arrive_expect_tx(bar_ld, static_cast<uint32_t>(4 * WIN * nt));
+        tc::bulk_load(sm, a.tail_win + (static_cast<int64_t>(tail_r) * n_all + t0) * WIN,
+                      static_cast<uint32_t>(4 * WIN * nt), bar_ld);
+      }
+      const bool got = tc::mbar_wait(bar_ld, ld_phase & 1, WAIT_TIMEOUT_NS);
+      ++ld_phase;
+      err |= !got;
+      if (got && !mma_warp && 16 * cg < HD) {
+        for (int t = 0; t < nt; ++t) {
+          const float4* wv = wsm + t * (WIN / 4);
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            const float4 x = wv[win4(0, c4, cg, row)];
+            const float4 y = wv[win4(1, c4, cg, row)];
+            dv[4 * c4] += x.x, dv[4 * c4 + 1] += x.y, dv[4 * c4 + 2] += x.z, dv[4 * c4 + 3] += x.w;
+            dk[4 * c4] += y.x, dk[4 * c4 + 1] += y.y, dk[4 * c4 + 2] += y.z, dk[4 * c4 + 3] += y.w;
+          }
+        }
+      }
+      // Every read of the chunk done before the next copy lands (and every thread leaves together).
+      if (!__syncthreads_and(got)) break;
+    }
+  }
   err = __syncthreads_or(err);  // any expired wait in the block: nothing is written
   if (err) {
     if (tid == 0) flag_timeout(a.err, a.sink);
     tc::mbar_wait(bar_t2, (N - 1) & 1, WAIT_TIMEOUT_NS);  // no MMA left in flight
+  } else if (part != 0) {
+    // A helper of a split key block: its windows and dQ partials are written; hand them to the
+    // first part (ORDER: every thread's stores are visible GPU-wide before thread 0's release).
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) st_release_gpu(a.tail_flag + tail_r * nparts + part, 1);
   } else {
     // The dQ partials' hand-off: after the barrier above, thread 0's acquire-release count
     // publishes every thread's partial stores (the barrier orders them before it) and, for the
@@ -611,7 +718,7 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
         tc::mbar_arrive_expect_tx(bar_ld, static_cast<uint32_t>(part_bytes));
         tc::bulk_load(sm, part, static_cast<uint32_t>(part_bytes), bar_ld);
       }
-      const bool ok = tc::mbar_wait(bar_ld, 1, WAIT_TIMEOUT_NS);
+      const bool ok = tc::mbar_wait(bar_ld, ld_phase & 1, WAIT_TIMEOUT_NS);
       const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * HD;
       float* dq_base = a.dqkv + static_cast<int64_t>(b) * S * row_stride + h * HD;
       // DETERMINISM: dQ = (((p0 + p1) + p2) + ...) * scale, as below.
@@ -718,7 +825,32 @@ cudaError_t launch_bwd_tc(const BwdArgs& args, int head_dim, int causal, cudaStr
     a.wave_ctas = sms;
   else
     a.wave_ctas = 0;
-  const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(a.n_kblocks) * a.B * a.H));
+  const int64_t BH = static_cast<int64_t>(a.B) * a.H;
+  const int64_t units = static_cast<int64_t>(a.n_kblocks) * BH;  // key blocks
+  int64_t blocks = units;
+  // Split tail (non-causal, no-wait dQ path): the R key blocks past the last full wave of P blocks
+  // would hold R SMs for a whole block's time while the rest idle; run each as k blocks of
+  // consecutive query tiles instead (k = min(tiles, P / R), so they run side by side). The
+  // helpers' windows take the part of the dQ-partial region that 128-key blocks leave unused (the
+  // workspace sizes it for 64-key blocks), their flags the turn counters that the no-wait path
+  // leaves unused (cleared by the prep kernel). Without room for either, no split.
+  a.tail_parts = 0;
+  if (a.dq_part != nullptr && !causal && a.wave_ctas > 0) {
+    const int64_t P = a.wave_ctas, R = units % P;
+    const int64_t n = (a.S + QT - 1) / QT;  // query tiles of every key block
+    const int64_t k = R > 0 ? std::min<int64_t>(n, P / R) : 0;
+    const int64_t nkb64 = (a.S + BWD_BN - 1) / BWD_BN;  // key blocks the partials are sized for
+    const int64_t spare = (nkb64 - a.n_kblocks) * BH * a.S * head_dim;  // floats
+    if (k >= 2 && R * n * 2 * KB * head_dim <= spare && BH + R * k <= BH * a.n_qtiles) {
+      a.tail_base = static_cast<int>(units - R);
+      a.tail_units = static_cast<int>(R);
+      a.tail_parts = static_cast<int>(k);
+      a.tail_win = a.dq_part + static_cast<int64_t>(a.n_kblocks) * BH * a.S * head_dim;
+      a.tail_flag = a.turn + BH;
+      blocks = units - R + R * k;
+    }
+  }
+  const dim3 grid(static_cast<unsigned>(blocks));
   if (head_dim == 32) {
     if (causal) return launch_pdl(bwd_tc_kernel<true, 32>, grid, dim3(NB), SMEM_ALLOC, stream, a);
     return launch_pdl(bwd_tc_kernel<false, 32>, grid, dim3(NB), SMEM_ALLOC, stream, a);

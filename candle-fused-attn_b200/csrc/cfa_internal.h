@@ -73,6 +73,13 @@ struct BwdArgs {
   int wave_ctas;  // tensor-core backward: blocks resident at once (one per SM); 0: none
   uint64_t timeout_ns;
   int* sink;      // host-visible error flag (cfa_error_sink) or nullptr
+  // Tensor-core backward, split tail (set by its launcher; tail_parts <= 1: none). The key blocks
+  // from tail_base on (tail_units of them, the last partial wave) each run as tail_parts blocks,
+  // one per contiguous range of query tiles; the helpers leave their tiles' dV, dK windows in
+  // tail_win and raise tail_flag, the first part adds them in tile order.
+  int tail_base, tail_units, tail_parts;
+  float* tail_win;  // [tail_units][query tiles][2][128][D] window sums
+  int* tail_flag;   // [tail_units][tail_parts], cleared by the prep kernel
 };
 
 struct PrepArgs {

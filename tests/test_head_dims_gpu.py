@@ -101,9 +101,12 @@ def _abi_bwd(qkv, dout, h, d, causal, ws_bytes, dev):
 
 
 @pytest.mark.parametrize("d", HEAD_DIMS)
-@pytest.mark.parametrize("bhs_causal", [(2, 2, 1000, False), (3, 2, 1024, True), (2, 3, 240, False)])
+@pytest.mark.parametrize("bhs_causal", [(2, 2, 1000, False), (3, 2, 1024, True), (2, 3, 240, False),
+                                        (32, 12, 240, False)])
 def test_dq_paths_are_bit_identical(cuda, d, bhs_causal):
-    """The no-wait dQ path (partials + ordered sum) and the turn chain give the same bits."""
+    """The no-wait dQ path (partials + ordered sum) and the turn chain give the same bits (at
+    b32 h12 s240, d = 32, the tensor-core backward also splits its 28 tail key blocks in four on
+    148 SMs: dK and dV compared between a split and an unsplit run)."""
     b, h, s, causal = bhs_causal
     qkv, dout = oracle.seeded_inputs(b, h, s, 3, 0.5, d=d)
     small = _abi.bwd_workspace_bytes_hd(b, h, s, d)

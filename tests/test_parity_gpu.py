@@ -215,11 +215,17 @@ def test_no_wait_dq_path_equals_turn_chain(cuda, b, h, s, causal):
 
 @pytest.mark.parametrize("b,h,s,causal", [(64, 6, 240, False), (3, 2, 200, True),
                                           (2, 2, 512, True), (2, 3, 65, False),
-                                          (3, 4, 1024, True), (2, 2, 1000, False)])
+                                          (3, 4, 1024, True), (2, 2, 1000, False),
+                                          (89, 2, 240, False), (84, 2, 240, False),
+                                          (40, 4, 512, False)])
 def test_tc_no_wait_dq_path_equals_turn_chain(cuda, b, h, s, causal):
     """The tensor-core backward's two dQ orderings -- the key-block turn chain (the minimal
     workspace; the only one past s = 1024) and the partials summed by the last block
-    (cfa_bwd_workspace_bytes_fast) -- give the same bits."""
+    (cfa_bwd_workspace_bytes_fast) -- give the same bits. With the partials, the key blocks of a
+    partial last wave run split over several blocks (on 148 SMs: the canvas's 28 tail key blocks
+    in 4 parts of one query tile; 60 tail blocks of b89 h2 in 2 parts, 40 of b84 h2 in 3; b40 h4
+    s512's 48 tail blocks of 8 tiles in parts of 2, 3, 3), so dK and dV too are compared between a
+    split and an unsplit run."""
     _no_wait_vs_turn_chain(cuda, b, h, s, causal, "tc")
 
 
