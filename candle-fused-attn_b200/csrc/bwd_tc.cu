@@ -15,9 +15,9 @@
 // Per query tile n:
 //   T1:  S^T  = K Q^T      A: K parts (shared, K-major)   B: Q parts (K-major)        -> TMEM S
 //        dP^T = V dO^T     A: V parts (TMEM, loaded once)  B: dO parts                -> TMEM DP
-//   C1:  the threads form P^T = exp(S^T * scale - L) (masked) and dS^T = P^T o (dP^T - D), put
-//        P^T's parts into TMEM over the columns each has just read (the A operand of dV) and
-//        dS^T's into shared memory;
+//   C1a: (during dP^T) the threads form P^T = exp(S^T * scale - L) (masked) and put its parts
+//        into TMEM (the A operand of dV), over the S^T columns each has just read and in T_X;
+//   C1b: (during dV) dS^T = P^T o (dP^T - D), its parts into shared memory;
 //   T2:  dV  += P^T dO     A: P^T parts (TMEM)             B: dO parts read MN-major  -> TMEM DV
 //        dK  += dS^T Q     A: dS^T parts (K-major)         B: Q parts read MN-major   -> TMEM DK
 //        dQ_t = dS K       A: dS^T parts read MN-major (M = 64 queries)  B: K parts read MN-major,
@@ -25,11 +25,12 @@
 //   C3:  (during T2) the next tile's Q, dO into their parts -- two buffers, by tile parity;
 //   C2:  (during T1 of the next tile) dV, dK fold into fp32 registers; the tile's dQ partial goes
 //        to the workspace.
-// The hand-offs are mbarriers: T1 and T2 commit; the compute warps arrive (one per warp) when
-// C1's operands and the next tile's Q, dO parts are in place. The MMA warp issues T1(n + 1) once
-// T2(n) has completed (it reads P^T(n) from the columns T1(n + 1) writes). The block that finishes
-// last for its (batch, head) sums the dQ partials in key-block order (the no-wait path of
-// bwd_ffma.cu: bit-identical for every schedule).
+// The hand-offs are mbarriers: S^T, dP^T, dV and dK + dQ commit one by one; the compute warps
+// arrive (one per warp) when P^T's parts, dS^T's parts and the next tile's Q, dO parts are in
+// place. The MMA warp issues T1(n + 1) once dV(n) has completed (it reads P^T(n) from the columns
+// S^T(n + 1) writes), queued behind dK(n), dQ(n). The block that finishes last for its (batch,
+// head) sums the dQ partials in key-block order (the no-wait path of bwd_ffma.cu: bit-identical
+// for every schedule).
 // S^T takes its six products in the forward kernel's order (A and B swapped), so the scores match
 // fwd_tc.cu's and the recomputed P matches the forward's L.
 //
@@ -73,15 +74,16 @@ constexpr int OFF_DO = OFF_Q + 6 * PART_Q;    // dO parts [64 q][64 d], two tile
 constexpr int OFF_DS = OFF_DO + 6 * PART_Q;   // dS^T parts [128 keys][64 q] (first: K staged)
 constexpr int OFF_ST = OFF_DS + 3 * PART_K;   // staging: the next tile's Q, dO (fp32)
 constexpr int OFF_LD = OFF_ST + 2 * QT * 64 * 4;  // L, D of two tiles: float [2][2][64]
-constexpr int OFF_BAR = OFF_LD + 2 * 2 * QT * 4;  // five mbarriers, the TMEM base, two ints
-constexpr int SMEM = OFF_BAR + 64;
+constexpr int OFF_BAR = OFF_LD + 2 * 2 * QT * 4;  // eight mbarriers, the TMEM base, four ints
+constexpr int SMEM = OFF_BAR + 96;
 constexpr int SMEM_ALLOC = SMEM + 1024;
 static_assert(SMEM_ALLOC <= 232448, "shared memory per block");
 // TMEM columns (lane = key row). V's parts, the A operand of dP^T: part i, K-step ks (16 dims) in
 // the 8 columns T_V + 32 i + 8 ks. S^T, dP^T of the current tile; P^T's parts (the A operand of
-// dV) then over the columns each thread has read (pt_col); dV, dK; dQ's two 64-key windows (M = 64).
+// dV: pt_col) over the S^T columns each thread has read and in T_X; dV, dK; dQ's two 64-key
+// windows (M = 64).
 constexpr uint32_t T_V = 0, T_S = 96, T_DP = 160, T_DV = 224, T_DK = 288, T_DQ0 = 352,
-                   T_DQ1 = 416;
+                   T_DQ1 = 416, T_X = 480;
 constexpr uint32_t TMEM_COLS = 512;
 
 // A split tail's window of one query tile (dV, dK sums of the tile as TMEM holds them, before the
@@ -97,10 +99,12 @@ struct TailWindow {
 };
 
 // P^T part i of K-step ks (queries 16 ks .. 16 ks + 15: the columns of group ks): parts 0, 1 over
-// that group's S^T columns, part 2 over its first 8 dP^T columns.
+// that group's S^T columns, part 2 in T_X + 8 ks -- dP^T stays whole until dS^T is formed from
+// it, while dV already runs.
 __host__ __device__ constexpr uint32_t pt_col(int i, int ks) {
-  return i < 2 ? T_S + 16 * ks + 8 * i : T_DP + 16 * ks;
+  return i < 2 ? T_S + 16 * ks + 8 * i : T_X + 8 * ks;
 }
+static_assert(T_X + 32 == TMEM_COLS, "TMEM budget");
 
 // Row items (row r, elements 8 kc .. 8 kc + 7): item c takes row 8 (c / 64) + c % 8 and chunk
 // (c / 8) % 8 (a quarter-warp writes 8 rows of one chunk: 8 bank groups). Every thread copies
@@ -233,13 +237,17 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
   unsigned char* dSp = sm + OFF_DS;
   unsigned char* st = sm + OFF_ST;
   float* ld = reinterpret_cast<float*>(sm + OFF_LD);  // [buf][0: L, 1: D][64]
-  uint64_t* bar_s = reinterpret_cast<uint64_t*>(sm + OFF_BAR);  // S^T, dP^T of a tile done
-  uint64_t* bar_t2 = bar_s + 1;  // dV, dK, dQ of a tile done
-  uint64_t* bar_c1 = bar_s + 2;  // P^T, dS^T of a tile in place (one arrival per compute warp)
-  uint64_t* bar_q = bar_s + 3;   // Q, dO parts of the next tile in place (same)
-  uint64_t* bar_ld = bar_s + 4;  // the prologue's bulk row copies
-  uint32_t* tbase_p = reinterpret_cast<uint32_t*>(bar_s + 5);
-  int* s_int = reinterpret_cast<int*>(bar_s + 6);
+  // Commits (each covers every earlier MMA of the block) and arrivals (one per compute warp).
+  uint64_t* bar_s = reinterpret_cast<uint64_t*>(sm + OFF_BAR);  // S^T of a tile done
+  uint64_t* bar_t2 = bar_s + 1;  // dK, dQ of a tile done: every MMA of the tile
+  uint64_t* bar_c1 = bar_s + 2;  // dS^T of a tile in shared memory (arrivals)
+  uint64_t* bar_q = bar_s + 3;   // Q, dO parts of the next tile in place (arrivals)
+  uint64_t* bar_ld = bar_s + 4;  // bulk copies: the prologue's rows, then the tail's windows
+  uint64_t* bar_dp = bar_s + 5;  // dP^T of a tile done
+  uint64_t* bar_p = bar_s + 6;   // P^T's parts of a tile in TMEM (arrivals)
+  uint64_t* bar_dv = bar_s + 7;  // dV of a tile done
+  uint32_t* tbase_p = reinterpret_cast<uint32_t*>(bar_s + 8);
+  int* s_int = reinterpret_cast<int*>(bar_s + 9);
 
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
   const bool mma_warp = w == NT / 32;   // warp 16 issues every MMA
@@ -302,6 +310,9 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
     tc::mbar_init(bar_c1, NT / 32);
     tc::mbar_init(bar_q, NT / 32);
     tc::mbar_init(bar_ld, 1);
+    tc::mbar_init(bar_dp, 1);
+    tc::mbar_init(bar_p, NT / 32);
+    tc::mbar_init(bar_dv, 1);
     tc::fence_mbar_init();
     tc::mbar_arrive_expect_tx(bar_ld, 4u * HD * (2 * min(KB, S - k0) + 2 * min(QT, S - t_begin * QT)));
   }
@@ -431,24 +442,30 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
       const uint32_t id_mn = tc::idesc_f32acc(1, KB, HD) | (1u << 16);  // dV, dK: N = d, B MN
       const uint32_t id_dq = tc::idesc_f32acc(1, QT, HD) | (1u << 15) | (1u << 16);  // M 64
       const uint32_t sK = tc::smem_u32(Kp), sS = tc::smem_u32(dSp);
-      // S^T (the forward's product order) and dP^T (A: V's parts in TMEM) of tile n.
+      // S^T (the forward's product order) and dP^T (A: V's parts in TMEM) of tile n, committed
+      // one by one: the compute warps form P^T while dP^T runs.
       auto issue_t1 = [&](int n) {
         const uint32_t sQ = tc::smem_u32(Qp + (n & 1) * 3 * PART_Q);
         const uint32_t sO = tc::smem_u32(dOp + (n & 1) * 3 * PART_Q);
         issue6<KSD, PART_K, PART_Q, 256, 256, true>(tbase + T_S,
                                                   tc::split_desc(tc::desc_kmajor(sK, 128, 1024)),
                                                   tc::split_desc(tc::desc_kmajor(sQ, 128, 1024)), id128);
+        tc::commit_warp(bar_s);
         auto vcol = [&](int i, int ks) { return tbase + T_V + 32 * i + 8 * ks; };
         issue6_tmem_a<PART_Q, 256, decltype(vcol), KSD>(
             tbase + T_DP, vcol, tc::split_desc(tc::desc_kmajor(sO, 128, 1024)), id128);
-        tc::commit_warp(bar_s);
+        tc::commit_warp(bar_dp);
       };
-      // dV (A: P^T's parts in TMEM), dK, dQ (two windows of 64 keys) of tile n.
-      auto issue_t2 = [&](int n) {
-        const uint32_t sQ = tc::smem_u32(Qp + (n & 1) * 3 * PART_Q);
+      // dV (A: P^T's parts in TMEM) of tile n: it runs while the compute warps form dS^T.
+      auto issue_dv = [&](int n) {
         const uint32_t sO = tc::smem_u32(dOp + (n & 1) * 3 * PART_Q);
         issue6_tmem_a<PART_Q, 2048>(tbase + T_DV, [&](int i, int ks) { return tbase + pt_col(i, ks); },
                                     tc::split_desc(tc::desc_kmajor(sO, 1024, 128)), id_mn);
+        tc::commit_warp(bar_dv);
+      };
+      // dK, dQ (two windows of 64 keys) of tile n.
+      auto issue_t2 = [&](int n) {
+        const uint32_t sQ = tc::smem_u32(Qp + (n & 1) * 3 * PART_Q);
         issue6<4, PART_K, PART_Q, 256, 2048, false>(tbase + T_DK,
                                                     tc::split_desc(tc::desc_kmajor(sS, 128, 1024)),
                                                     tc::split_desc(tc::desc_kmajor(sQ, 1024, 128)), id_mn);
@@ -460,14 +477,20 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
             id_dq);
         tc::commit_warp(bar_t2);
       };
+      // The tensor core's order: S^T(n), dP^T(n), dV(n) once P^T(n) is in TMEM, dK(n), dQ(n)
+      // once dS^T(n) is in shared memory, then S^T(n + 1) -- over P^T(n)'s columns, once dV(n) has
+      // completed -- and dP^T(n + 1), queued behind dK(n), dQ(n).
       issue_t1(0);
       for (int n = 0; n < N; ++n) {
-        err |= !tc::mbar_wait(bar_c1, n & 1, WAIT_TIMEOUT_NS);
+        err |= !tc::mbar_wait(bar_p, n & 1, WAIT_TIMEOUT_NS);
+        tc::fence_after_sync();
+        issue_dv(n);
+        err |= !tc::mbar_wait(bar_c1, n & 1, WAIT_TIMEOUT_NS);  // dP^T(n) read, dS^T(n) stored
         tc::fence_after_sync();
         issue_t2(n);
         if (n + 1 < N) {
           err |= !tc::mbar_wait(bar_q, n & 1, WAIT_TIMEOUT_NS);
-          err |= !tc::mbar_wait(bar_t2, n & 1, WAIT_TIMEOUT_NS);  // T2(n) has read P^T(n)
+          err |= !tc::mbar_wait(bar_dv, n & 1, WAIT_TIMEOUT_NS);  // dV(n) has read P^T(n)
           tc::fence_after_sync();
           issue_t1(n + 1);
         }
@@ -478,44 +501,33 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
     cp_async_commit();
     for (int n = 0; n < N; ++n) {
       const int q0 = (t_begin + n) * QT;
-      // (C1) P^T and dS^T for this thread's 16 queries.
+      // (C1a) P^T for this thread's 16 queries, its parts into TMEM (pt_col) for dV -- while the
+      // tensor core computes dP^T.
       err |= !tc::mbar_wait(bar_s, n & 1, WAIT_TIMEOUT_NS);
       tc::fence_after_sync();
       const float* Lt = ld + (n & 1) * 128;
       const float* Dt = Lt + QT;
       const bool edge = (q0 + QT > S) || (k0 + KB > S) || (CAUSAL && k0 + KB - 1 > q0);
       float pr[16];
+      tc::tmem_ld16(tbase + lane_sel + T_S + 16 * cg, pr);
+      tc::tmem_wait_ld();
 #pragma unroll
-      for (int h8 = 0; h8 < 2; ++h8) {
-        const uint32_t col = 16 * cg + 8 * h8;
-        float sb[8], gb[8];
-        tmem_ld8(tbase + lane_sel + T_S + col, sb);
-        tmem_ld8(tbase + lane_sel + T_DP + col, gb);
-        tc::tmem_wait_ld();
-        float ds[8];
-#pragma unroll
-        for (int u = 0; u < 8; u += 2) {
-          const int ql = col + u;
-          // P = e^(s * scale - L): the argument with one rounding (L - s scale by one fma, so the
-          // cancellation is exact), then 2^(arg log2 e) on the SFU (ex2.approx, max relative
-          // error about 2^-22); dS = P (dP - D). Pairs of queries in packed fp32.
-          const uint64_t l2 = *reinterpret_cast<const uint64_t*>(Lt + ql);
-          const uint64_t d2 = *reinterpret_cast<const uint64_t*>(Dt + ql);
-          float x0, x1;
-          tc::unpack2(mul2(fma2v(tc::pack2(sb[u], sb[u + 1]), nsc2, l2), nl2e2), x0, x1);
-          float p0 = ex2(x0), p1 = ex2(x1);
-          if (edge) {
-            if (!(q0 + ql < S && key < S && !(CAUSAL && key > q0 + ql))) p0 = 0.0f;
-            if (!(q0 + ql + 1 < S && key < S && !(CAUSAL && key > q0 + ql + 1))) p1 = 0.0f;
-          }
-          pr[8 * h8 + u] = p0;
-          pr[8 * h8 + u + 1] = p1;
-          tc::unpack2(mul2(tc::pack2(p0, p1), tc::sub2(tc::pack2(gb[u], gb[u + 1]), d2)), ds[u],
-                      ds[u + 1]);
+      for (int u = 0; u < 16; u += 2) {
+        const int ql = 16 * cg + u;
+        // P = e^(s * scale - L): the argument with one rounding (L - s scale by one fma, so the
+        // cancellation is exact), then 2^(arg log2 e) on the SFU (ex2.approx, max relative error
+        // about 2^-22). Pairs of queries in packed fp32.
+        const uint64_t l2 = *reinterpret_cast<const uint64_t*>(Lt + ql);
+        float x0, x1;
+        tc::unpack2(mul2(fma2v(tc::pack2(pr[u], pr[u + 1]), nsc2, l2), nl2e2), x0, x1);
+        float p0 = ex2(x0), p1 = ex2(x1);
+        if (edge) {
+          if (!(q0 + ql < S && key < S && !(CAUSAL && key > q0 + ql))) p0 = 0.0f;
+          if (!(q0 + ql + 1 < S && key < S && !(CAUSAL && key > q0 + ql + 1))) p1 = 0.0f;
         }
-        store_parts(dSp, PART_K, kmaj_off(row, 2 * cg + h8), ds);
+        pr[u] = p0;
+        pr[u + 1] = p1;
       }
-      // P^T's parts over the S^T / dP^T columns this thread has just read (pt_col).
       {
         uint32_t pp[3][8];
         split16(pr, pp);
@@ -523,6 +535,29 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
         tmem_st8(tbase + lane_sel + pt_col(1, cg), pp[1]);
         tmem_st8(tbase + lane_sel + pt_col(2, cg), pp[2]);
         tc::tmem_wait_st();
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(bar_p);
+      // (C1b) dS^T = P^T o (dP^T - D), its parts into shared memory for dK, dQ -- while the tensor
+      // core computes dV.
+      err |= !tc::mbar_wait(bar_dp, n & 1, WAIT_TIMEOUT_NS);
+      tc::fence_after_sync();
+#pragma unroll
+      for (int h8 = 0; h8 < 2; ++h8) {
+        const uint32_t col = 16 * cg + 8 * h8;
+        float gb[8];
+        tmem_ld8(tbase + lane_sel + T_DP + col, gb);
+        tc::tmem_wait_ld();
+        float ds[8];
+#pragma unroll
+        for (int u = 0; u < 8; u += 2) {
+          const uint64_t d2 = *reinterpret_cast<const uint64_t*>(Dt + col + u);
+          tc::unpack2(mul2(tc::pack2(pr[8 * h8 + u], pr[8 * h8 + u + 1]),
+                           tc::sub2(tc::pack2(gb[u], gb[u + 1]), d2)),
+                      ds[u], ds[u + 1]);
+        }
+        store_parts(dSp, PART_K, kmaj_off(row, 2 * cg + h8), ds);
       }
       tc::fence_async_smem();
       tc::fence_before_sync();
