@@ -739,9 +739,27 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
                         dk[4 * c4 + 3] * a.scale);
       }
     }
-    if (tid == 0) s_int[0] = chain ? -1 : atom_add_acq_rel(a.turn + bh, 1);
-    __syncthreads();
+    __syncthreads();  // the dV, dK rows in place
     constexpr int C4 = HD / 4;  // float4 columns of a dQ, dK or dV row
+    // Thread 0's count -- an acquire-release round trip through L2 -- travels while the block
+    // stores the dV, dK rows.
+    int count = -1;
+    if (tid == 0 && !chain) count = atom_add_acq_rel(a.turn + bh, 1);
+    // dV, dK rows out of shared memory: every 16 threads store one whole row.
+    {
+      const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * HD;
+      for (int f = tid; f < 2 * KB * C4; f += NB) {
+        const int which = f / (KB * C4), r = (f / C4) % KB, c4 = f % C4;
+        if (k0 + r < S) {
+          float* dst = a.dqkv + (static_cast<int64_t>(b) * S + k0 + r) * row_stride +
+                       (2 - which) * a.H * HD + h * HD;
+          reinterpret_cast<float4*>(dst)[c4] =
+              reinterpret_cast<const float4*>((which ? sk : sv) + r * LDS)[c4];
+        }
+      }
+    }
+    if (tid == 0) s_int[0] = count;
+    __syncthreads();
     const int64_t part_bytes = static_cast<int64_t>(nkb) * S * HD * 4;
     if (s_int[0] == nkb - 1 && part_bytes <= OFF_DS) {
       // The (b, h)'s partials, contiguous [nkb][S][64], as one bulk copy into shared memory (the
@@ -813,19 +831,6 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
             reinterpret_cast<float4*>(dq_base + (idx / C4) * row_stride)[idx % C4] =
                 make_float4(v[u].x * a.scale, v[u].y * a.scale, v[u].z * a.scale,
                             v[u].w * a.scale);
-        }
-      }
-    }
-    // dV, dK rows out of shared memory: every 16 threads store one whole row.
-    {
-      const int64_t row_stride = 3 * static_cast<int64_t>(a.H) * HD;
-      for (int f = tid; f < 2 * KB * C4; f += NB) {
-        const int which = f / (KB * C4), r = (f / C4) % KB, c4 = f % C4;
-        if (k0 + r < S) {
-          float* dst = a.dqkv + (static_cast<int64_t>(b) * S + k0 + r) * row_stride +
-                       (2 - which) * a.H * HD + h * HD;
-          reinterpret_cast<float4*>(dst)[c4] =
-              reinterpret_cast<const float4*>((which ? sk : sv) + r * LDS)[c4];
         }
       }
     }
