@@ -41,8 +41,9 @@
 // helpers (p >= 1) store each tile's dV, dK TMEM windows -- the values one block would fold --
 // in workspace space the 128-key blocks leave unused, and raise a flag; the first part folds its
 // own tiles, then the helpers' windows in tile order, so dV, dK are the one-block sums bit for
-// bit, and only it writes dV, dK and counts the key block in. The helpers never wait on anyone,
-// so the first part's bounded wait always ends.
+// bit, and only it writes dV, dK and counts the key block in. The roles go by a ticket drawn at
+// the block's start, helpers first, and the helpers never wait on anyone, so a running first
+// part's bounded wait always ends.
 //
 // Every mbarrier wait is bounded; an expired wait sets the workspace error flag
 // (cfa_bwd_status reads it) and the block writes nothing.
@@ -272,12 +273,19 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
   }
   // Split tail (no-wait path): the key blocks from a.tail_base on -- the grid's last partial wave
   // -- run as a.tail_parts blocks each, part p taking the p-th contiguous range of the query tiles.
-  // The helpers (parts >= 1, first in the grid) leave their tiles' dV, dK windows in a.tail_win;
-  // the first part (last in the grid) adds them after its own, in tile order: the same sums as one
-  // block, bit for bit. Only the first part writes dV, dK and counts the key block in.
+  // The helpers (parts >= 1) leave their tiles' dV, dK windows in a.tail_win; the first part adds
+  // them after its own, in tile order: the same sums as one block, bit for bit. Only the first
+  // part writes dV, dK and counts the key block in. The roles go by a ticket drawn at the start,
+  // helpers first, so a first part that runs finds every helper running or done (no assumption
+  // on the order in which the hardware starts blocks): its wait always ends.
   int part = 0, nparts = 1, tail_r = 0;
   if (!CAUSAL && !chain && a.tail_parts > 1 && ticket >= a.tail_base) {
-    const int j = ticket - a.tail_base;
+    if (tid == 0) {
+      griddep_wait();  // the tail's ticket counter, cleared by the prep kernel
+      s_int[1] = atomicAdd(a.tail_flag + a.tail_units * a.tail_parts, 1);
+    }
+    __syncthreads();
+    const int j = s_int[1];
     const int g = j / a.tail_units;
     tail_r = j - g * a.tail_units;
     nparts = a.tail_parts;
@@ -872,8 +880,9 @@ cudaError_t launch_bwd_tc(const BwdArgs& args, int head_dim, int causal, cudaStr
   // would hold R SMs for a whole block's time while the rest idle; run each as k blocks of
   // consecutive query tiles instead (k = min(tiles, P / R), so they run side by side). The
   // helpers' windows take the part of the dQ-partial region that 128-key blocks leave unused (the
-  // workspace sizes it for 64-key blocks), their flags the turn counters that the no-wait path
-  // leaves unused (cleared by the prep kernel). Without room for either, no split.
+  // workspace sizes it for 64-key blocks), their flags and the tail's ticket counter the turn
+  // counters that the no-wait path leaves unused (cleared by the prep kernel). Without room for
+  // either, no split.
   a.tail_parts = 0;
   if (a.dq_part != nullptr && !causal && a.wave_ctas > 0) {
     const int64_t P = a.wave_ctas, R = units % P;
@@ -881,7 +890,7 @@ cudaError_t launch_bwd_tc(const BwdArgs& args, int head_dim, int causal, cudaStr
     const int64_t k = R > 0 ? std::min<int64_t>(n, P / R) : 0;
     const int64_t nkb64 = (a.S + BWD_BN - 1) / BWD_BN;  // key blocks the partials are sized for
     const int64_t spare = (nkb64 - a.n_kblocks) * BH * a.S * head_dim;  // floats
-    if (k >= 2 && R * n * 2 * KB * head_dim <= spare && BH + R * k <= BH * a.n_qtiles) {
+    if (k >= 2 && R * n * 2 * KB * head_dim <= spare && BH + R * k + 1 <= BH * a.n_qtiles) {
       a.tail_base = static_cast<int>(units - R);
       a.tail_units = static_cast<int>(R);
       a.tail_parts = static_cast<int>(k);

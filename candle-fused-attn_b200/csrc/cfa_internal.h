@@ -75,11 +75,13 @@ struct BwdArgs {
   int* sink;      // host-visible error flag (cfa_error_sink) or nullptr
   // Tensor-core backward, split tail (set by its launcher; tail_parts <= 1: none). The key blocks
   // from tail_base on (tail_units of them, the last partial wave) each run as tail_parts blocks,
-  // one per contiguous range of query tiles; the helpers leave their tiles' dV, dK windows in
-  // tail_win and raise tail_flag, the first part adds them in tile order.
+  // one per contiguous range of query tiles (the roles by a ticket, helpers first); the helpers
+  // leave their tiles' dV, dK windows in tail_win and raise tail_flag, the first part adds them in
+  // tile order.
   int tail_base, tail_units, tail_parts;
   float* tail_win;  // [tail_units][query tiles][2][128][D] window sums
-  int* tail_flag;   // [tail_units][tail_parts], cleared by the prep kernel
+  int* tail_flag;   // [tail_units][tail_parts] flags, then the tail's ticket counter (cleared by the
+                    // prep kernel)
 };
 
 struct PrepArgs {
