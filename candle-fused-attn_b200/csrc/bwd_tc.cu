@@ -211,6 +211,13 @@ __device__ __forceinline__ uint64_t fma2v(uint64_t a, uint64_t b, uint64_t c) {
   return d;
 }
 
+// Eight floats to global memory in one 32-byte store (address 32-byte aligned), cached in L2 only.
+__device__ __forceinline__ void st_cg_v8(float* p, const float (&v)[8]) {
+  asm volatile("st.global.cg.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "f"(v[0]),
+               "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+               : "memory");
+}
+
 // atomicAdd with acquire-release semantics at GPU scope.
 __device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
   int old;
@@ -617,12 +624,16 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
       const int qi = q0 + 16 * (w & 3) + lane;
       if (!chain) {
         if (lane < 16 && qi < S && 16 * cg < HD && !err) {
+          // Two 32-byte stores: whole L2 sectors (16-byte stores 256 bytes apart across the warp
+          // each wrote half of 16 sectors).
           float* dst = a.dq_part + ((static_cast<int64_t>(bh) * nkb + kb) * S + qi) * HD + 16 * cg;
 #pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4)
-            __stcg(reinterpret_cast<float4*>(dst) + c4,
-                   make_float4(xb[4 * c4] + xs[4 * c4], xb[4 * c4 + 1] + xs[4 * c4 + 1],
-                               xb[4 * c4 + 2] + xs[4 * c4 + 2], xb[4 * c4 + 3] + xs[4 * c4 + 3]));
+          for (int c8 = 0; c8 < 2; ++c8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = xb[8 * c8 + u] + xs[8 * c8 + u];
+            st_cg_v8(dst + 8 * c8, v);
+          }
         }
       } else {
         // Turn chain: query tile t's contributors are key blocks 0 .. last (causal: those holding
