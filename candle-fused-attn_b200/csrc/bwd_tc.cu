@@ -526,31 +526,36 @@ __global__ void __launch_bounds__(NB, 1) bwd_tc_kernel(const BwdArgs a) {
       float pr[16];
       tc::tmem_ld16(tbase + lane_sel + T_S + 16 * cg, pr);
       tc::tmem_wait_ld();
+      // Two halves of 8 queries, each half's parts stored (columns 4 h .. 4 h + 3 of its K-step)
+      // while the next half is formed: the stores' latency no longer trails the arithmetic.
 #pragma unroll
-      for (int u = 0; u < 16; u += 2) {
-        const int ql = 16 * cg + u;
-        // P = e^(s * scale - L): the argument with one rounding (L - s scale by one fma, so the
-        // cancellation is exact), then 2^(arg log2 e) on the SFU (ex2.approx, max relative error
-        // about 2^-22). Pairs of queries in packed fp32.
-        const uint64_t l2 = *reinterpret_cast<const uint64_t*>(Lt + ql);
-        float x0, x1;
-        tc::unpack2(mul2(fma2v(tc::pack2(pr[u], pr[u + 1]), nsc2, l2), nl2e2), x0, x1);
-        float p0 = ex2(x0), p1 = ex2(x1);
-        if (edge) {
-          if (!(q0 + ql < S && key < S && !(CAUSAL && key > q0 + ql))) p0 = 0.0f;
-          if (!(q0 + ql + 1 < S && key < S && !(CAUSAL && key > q0 + ql + 1))) p1 = 0.0f;
+      for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+        for (int u = 8 * hh; u < 8 * hh + 8; u += 2) {
+          const int ql = 16 * cg + u;
+          // P = e^(s * scale - L): the argument with one rounding (L - s scale by one fma, so the
+          // cancellation is exact), then 2^(arg log2 e) on the SFU (ex2.approx, max relative
+          // error about 2^-22). Pairs of queries in packed fp32.
+          const uint64_t l2 = *reinterpret_cast<const uint64_t*>(Lt + ql);
+          float x0, x1;
+          tc::unpack2(mul2(fma2v(tc::pack2(pr[u], pr[u + 1]), nsc2, l2), nl2e2), x0, x1);
+          float p0 = ex2(x0), p1 = ex2(x1);
+          if (edge) {
+            if (!(q0 + ql < S && key < S && !(CAUSAL && key > q0 + ql))) p0 = 0.0f;
+            if (!(q0 + ql + 1 < S && key < S && !(CAUSAL && key > q0 + ql + 1))) p1 = 0.0f;
+          }
+          pr[u] = p0;
+          pr[u + 1] = p1;
         }
-        pr[u] = p0;
-        pr[u + 1] = p1;
+        const float xh[8] = {pr[8 * hh], pr[8 * hh + 1], pr[8 * hh + 2], pr[8 * hh + 3],
+                             pr[8 * hh + 4], pr[8 * hh + 5], pr[8 * hh + 6], pr[8 * hh + 7]};
+        uint4 h0, h1, h2;
+        split8(xh, h0, h1, h2);
+        tc::tmem_st4(tbase + lane_sel + pt_col(0, cg) + 4 * hh, h0);
+        tc::tmem_st4(tbase + lane_sel + pt_col(1, cg) + 4 * hh, h1);
+        tc::tmem_st4(tbase + lane_sel + pt_col(2, cg) + 4 * hh, h2);
       }
-      {
-        uint32_t pp[3][8];
-        split16(pr, pp);
-        tmem_st8(tbase + lane_sel + pt_col(0, cg), pp[0]);
-        tmem_st8(tbase + lane_sel + pt_col(1, cg), pp[1]);
-        tmem_st8(tbase + lane_sel + pt_col(2, cg), pp[2]);
-        tc::tmem_wait_st();
-      }
+      tc::tmem_wait_st();
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(bar_p);

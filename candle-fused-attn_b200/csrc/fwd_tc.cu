@@ -566,24 +566,33 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
     const float alpha = ex2((rs.m - mu) * LOG2E);
     const uint64_t mu2 = tc::pack2(mu, mu);
     uint64_t ps2 = 0;  // (+0, +0)
+    // p into P's parts in TMEM (K-step cq of P V's A operand), in two halves of 8 keys (columns
+    // 4 h .. 4 h + 3 of the K-step): each half's stores travel while the next half is formed.
 #pragma unroll
-    for (int c = 0; c < CW; c += 2) {
-      float lo, hi;
-      tc::unpack2(mul2(tc::sub2(tc::pack2(sv[c], sv[c + 1]), mu2), l2e2), lo, hi);
-      sv[c] = ex2(lo);
-      sv[c + 1] = ex2(hi);
-      ps2 = add2(ps2, tc::pack2(sv[c], sv[c + 1]));
+    for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+      for (int c = 8 * hh; c < 8 * hh + 8; c += 2) {
+        float lo, hi;
+        tc::unpack2(mul2(tc::sub2(tc::pack2(sv[c], sv[c + 1]), mu2), l2e2), lo, hi);
+        sv[c] = ex2(lo);
+        sv[c + 1] = ex2(hi);
+        ps2 = add2(ps2, tc::pack2(sv[c], sv[c + 1]));
+      }
+      const float xh[8] = {sv[8 * hh], sv[8 * hh + 1], sv[8 * hh + 2], sv[8 * hh + 3],
+                           sv[8 * hh + 4], sv[8 * hh + 5], sv[8 * hh + 6], sv[8 * hh + 7]};
+      uint4 h0, h1, h2;
+      split8(xh, h0, h1, h2);
+      const uint32_t pc = tbase + lane_sel + T_SP(t) + 8 * cq + 4 * hh;
+      tc::tmem_st4(pc, h0);
+      tc::tmem_st4(pc + 32, h1);
+      tc::tmem_st4(pc + 64, h2);
     }
     float ps_lo, ps_hi;
     tc::unpack2(ps2, ps_lo, ps_hi);
     rs.lpart = fmaf(rs.lpart, alpha, ps_lo + ps_hi);
     rs.m = tmax;
     rs.alpha_prev = alpha;
-    // p into P's parts in TMEM (K-step cq of P V's A operand); hand the tile to the MMA warp.
-    uint32_t pparts[3][8];
-    split16(sv, pparts);
-#pragma unroll
-    for (int i = 0; i < 3; ++i) tmem_st8(tbase + lane_sel + T_SP(t) + 32 * i + 8 * cq, pparts[i]);
+    // Hand the tile to the MMA warp.
     tc::tmem_wait_st();
     tc::fence_before_sync();
     __syncwarp();
