@@ -124,6 +124,24 @@ __device__ __forceinline__ void stage_item(unsigned char* st, const float* src, 
   cp_async16(st + 16 * (NSM + threadIdx.x), g + 4, ok ? 16 : 0);
 }
 
+// Q of both query tiles into shared memory for the prologue: 16-byte chunks by consecutive
+// threads, so every warp copies whole rows (the rows a thread splits lie 32 rows apart in its
+// warp, and read one by one they cost a cache line per thread). Row r (0 .. BQ - 1) at 256 r
+// bytes, chunk c at 16 (c ^ (r % 8)): the eight rows a quarter-warp reads in one go fall into
+// eight different bank groups. Rows past the end are zero-filled (source size 0).
+template <int HD>
+__device__ __forceinline__ void stage_q(unsigned char* qs, const float* qp, int64_t stride, int q0,
+                                        int seq) {
+  constexpr int CPR = HD / 4;  // 16-byte chunks of a row
+#pragma unroll
+  for (int j = threadIdx.x; j < BQ * CPR; j += NSM) {
+    const int r = j / CPR, c = j % CPR;
+    const bool ok = q0 + r < seq;
+    const float* g = qp + static_cast<int64_t>(ok ? q0 + r : 0) * stride + 4 * c;
+    cp_async16(qs + 256 * r + 16 * (c ^ (r & 7)), g, ok ? 16 : 0);
+  }
+}
+
 // This thread's staged row item into the K-major parts of one operand tile.
 __device__ __forceinline__ void split_item(unsigned char* parts, const unsigned char* st) {
   int r, kc;
@@ -367,28 +385,18 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
     tc::tmem_relinquish();
   }
 
-  // Prologue: K(0), K(1), V(0) into their parts (K(1) staged in K part buffer 2, free until the
-  // first loop step), Q of both tiles (this thread's row and 16 dims: K-step cq of S's A operand)
-  // into TMEM; K(2), V(1) left in flight. Then the MMA warp issues S0(0) and S1(0).
-  float qx[NTILE][CW];
+  // Prologue: Q of both tiles staged in the K part buffers (stage_q), K(0), K(1), V(0) as row
+  // items (K(1) in V part buffer 2, free until the first loop step); Q (this thread's row and 16
+  // dims: K-step cq of S's A operand) into TMEM, then K(0), K(1), V(0) into their parts -- over
+  // the staged Q, once every thread has read its rows; K(2), V(1) left in flight. Then the MMA warp
+  // issues S0(0) and S1(0).
+  static_assert(BQ * 256 <= 3 * PARTS, "Q of both tiles fits the K part buffers");
   if (!mma_warp) {
+    stage_q<HD>(Kp, qp, a.q_ss, q0, S);
     stage_item<HD>(Kst, kp, a.k_ss, 0, S);
-    if (T > 1) stage_item<HD>(Kp + 2 * PARTS, kp, a.k_ss, KT, S);
+    if (T > 1) stage_item<HD>(Vp + PARTS, kp, a.k_ss, KT, S);
     stage_item<HD>(Vst, vp, a.v_ss, 0, S);
     cp_async_commit();
-#pragma unroll
-    for (int t = 0; t < NTILE; ++t) {
-      const int qi = q0 + QT * t + row;
-      const float4* src = reinterpret_cast<const float4*>(qp + static_cast<int64_t>(qi) * a.q_ss + CW * cq);
-#pragma unroll
-      for (int c4 = 0; c4 < CW / 4; ++c4) {
-        const float4 u = qi < S && CW * cq < HD ? __ldg(src + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
-        qx[t][4 * c4] = u.x;
-        qx[t][4 * c4 + 1] = u.y;
-        qx[t][4 * c4 + 2] = u.z;
-        qx[t][4 * c4 + 3] = u.w;
-      }
-    }
   }
   tc::fence_before_sync();
   __syncthreads();  // the TMEM base
@@ -396,17 +404,31 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
   const uint32_t tbase = *tbase_p;
   const uint32_t lane_sel = static_cast<uint32_t>(32 * (w & 3)) << 16;
   if (!mma_warp) {
+    cp_async_wait_all();
+    bar_sync(1, NSM);  // every thread's share of Q in place
 #pragma unroll
     for (int t = 0; t < NTILE; ++t) {
+      const int r = QT * t + row;
+      float qx[CW];
+#pragma unroll
+      for (int c4 = 0; c4 < CW / 4; ++c4) {
+        const float4 u = CW * cq < HD ? *reinterpret_cast<const float4*>(
+                                            Kp + 256 * r + 16 * ((CW / 4 * cq + c4) ^ (r & 7)))
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        qx[4 * c4] = u.x;
+        qx[4 * c4 + 1] = u.y;
+        qx[4 * c4 + 2] = u.z;
+        qx[4 * c4 + 3] = u.w;
+      }
       uint32_t qparts[3][8];
-      split16(qx[t], qparts);
+      split16(qx, qparts);
 #pragma unroll
       for (int i = 0; i < 3; ++i) tmem_st8(tbase + lane_sel + T_Q(t) + 32 * i + 8 * cq, qparts[i]);
     }
     tc::tmem_wait_st();
-    cp_async_wait_all();
+    bar_sync(1, NSM);  // every thread has read its Q rows: the K part buffers are free
     split_item(Kp, Kst);
-    if (T > 1) split_item(Kp + PARTS, Kp + 2 * PARTS);
+    if (T > 1) split_item(Kp + PARTS, Vp + PARTS);
     split_item(Vp, Vst);
     tc::fence_async_smem();
     // In flight during key tile 0: K(2), then V(1) (two cp.async groups, in that order).
