@@ -431,15 +431,18 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
     if (T > 1) split_item(Kp + PARTS, Vp + PARTS);
     split_item(Vp, Vst);
     tc::fence_async_smem();
-    // In flight during key tile 0: K(2), then V(1) (two cp.async groups, in that order).
+  }
+  tc::fence_before_sync();
+  __syncthreads();  // K(0), K(1), V(0) parts and Q in place; K part buffer 2 free
+  tc::fence_after_sync();
+  if (!mma_warp) {
+    // In flight during key tile 0: K(2), then V(1) (two cp.async groups, in that order), issued
+    // while the tensor core computes the first S (each thread reuses staging slots only it read).
     if (T > 2) stage_item<HD>(Kst, kp, a.k_ss, 2 * KT, S);
     cp_async_commit();
     if (T > 1) stage_item<HD>(Vst, vp, a.v_ss, KT, S);
     cp_async_commit();
   }
-  tc::fence_before_sync();
-  __syncthreads();  // K(0), K(1), V(0) parts and Q in place; K part buffer 2 free
-  tc::fence_after_sync();
   bool err = false;
 
   if (mma_warp) {
