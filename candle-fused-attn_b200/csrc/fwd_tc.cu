@@ -86,7 +86,7 @@ constexpr int OFF_VST = OFF_KST + STG;            // fp32 V items in flight
 constexpr int OFF_RED = OFF_VST + STG;            // float [2][128][NQ]: row maxima per tile
 constexpr int OFF_LRED = OFF_RED + NTILE * QT * NQ * 4;  // float [2][128][NQ]: row sums
 constexpr int OFF_BAR = OFF_LRED + NTILE * QT * NQ * 4;  // mbarriers; the TMEM base
-constexpr int NBAR = 10;  // s[2], o[2], p[2], k[2], v[2]
+constexpr int NBAR = 11;  // s[2], o[2], p[2], k[2], v[2], q0
 constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;
 constexpr int SMEM_ALLOC = SMEM + 1024;  // room to align the base to 1024 bytes
 constexpr int LDO = 68;  // epilogue: O rows of 64 floats, 68 apart (in the K part buffers)
@@ -340,6 +340,7 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
   uint64_t* bar_p = bar_s + 4;  // [2]: P(t)'s parts in TMEM (one arrival per softmax warp)
   uint64_t* bar_k = bar_s + 6;  // [2]: K(j)'s parts in place, j >= 2, by j % 2 (same)
   uint64_t* bar_v = bar_s + 8;  // [2]: V(j)'s parts in place, j >= 1, by j % 2 (same)
+  uint64_t* bar_q0 = bar_s + 10;  // Q's parts in TMEM and K(0)'s in place (same)
   uint32_t* tbase_p = reinterpret_cast<uint32_t*>(bar_s + NBAR);
 
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
@@ -374,7 +375,7 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
 
   if (tid == 0) {
 #pragma unroll
-    for (int i = 0; i < NBAR; ++i) tc::mbar_init(bar_s + i, i < 4 ? 1 : NSM / 32);
+    for (int i = 0; i < NBAR; ++i) tc::mbar_init(bar_s + i, i < 4 ? 1 : NSM / 32);  // q0: 16
     tc::fence_mbar_init();
   }
   griddep_wait();  // q, k, v may come from the previous kernel on the stream
@@ -385,14 +386,17 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
     tc::tmem_relinquish();
   }
 
-  // Prologue: Q of both tiles staged in the K part buffers (stage_q), K(0), K(1), V(0) as row
-  // items (K(1) in V part buffer 2, free until the first loop step); Q (this thread's row and 16
-  // dims: K-step cq of S's A operand) into TMEM, then K(0), K(1), V(0) into their parts -- over
-  // the staged Q, once every thread has read its rows; K(2), V(1) left in flight. Then the MMA warp
-  // issues S0(0) and S1(0).
-  static_assert(BQ * 256 <= 3 * PARTS, "Q of both tiles fits the K part buffers");
+  // Prologue: Q of both tiles staged over K part buffers 1 and 2 and the first 16 KB of V part
+  // buffer 0 (stage_q), K(0), K(1), V(0) as row items (K(1) in V part buffer 1, free until the
+  // first loop step). K(0) into its parts (buffer 0, clear of the staged Q) and Q (this thread's row and 16
+  // dims: K-step cq of S's A operand) into TMEM release the first S at once (bar_q0); K(1), V(0)
+  // go into their parts -- over the staged Q, once every thread has read its rows -- while the
+  // tensor core runs it: every softmax thread has split them before its first P arrival, which
+  // the MMA warp awaits before the first P V and S(1). K(2), V(1) are left in flight.
+  unsigned char* qst = Kp + PARTS;
+  static_assert(PARTS + BQ * 256 <= OFF_V - OFF_K + PARTS, "the staged Q ends inside V part buffer 0");
   if (!mma_warp) {
-    stage_q<HD>(Kp, qp, a.q_ss, q0, S);
+    stage_q<HD>(qst, qp, a.q_ss, q0, S);
     stage_item<HD>(Kst, kp, a.k_ss, 0, S);
     if (T > 1) stage_item<HD>(Vp + PARTS, kp, a.k_ss, KT, S);
     stage_item<HD>(Vst, vp, a.v_ss, 0, S);
@@ -405,6 +409,8 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
   const uint32_t lane_sel = static_cast<uint32_t>(32 * (w & 3)) << 16;
   if (!mma_warp) {
     cp_async_wait_all();
+    split_item(Kp, Kst);  // K(0)
+    tc::fence_async_smem();
     bar_sync(1, NSM);  // every thread's share of Q in place
 #pragma unroll
     for (int t = 0; t < NTILE; ++t) {
@@ -413,7 +419,7 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
 #pragma unroll
       for (int c4 = 0; c4 < CW / 4; ++c4) {
         const float4 u = CW * cq < HD ? *reinterpret_cast<const float4*>(
-                                            Kp + 256 * r + 16 * ((CW / 4 * cq + c4) ^ (r & 7)))
+                                            qst + 256 * r + 16 * ((CW / 4 * cq + c4) ^ (r & 7)))
                                       : make_float4(0.f, 0.f, 0.f, 0.f);
         qx[4 * c4] = u.x;
         qx[4 * c4 + 1] = u.y;
@@ -426,16 +432,15 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
       for (int i = 0; i < 3; ++i) tmem_st8(tbase + lane_sel + T_Q(t) + 32 * i + 8 * cq, qparts[i]);
     }
     tc::tmem_wait_st();
-    bar_sync(1, NSM);  // every thread has read its Q rows: the K part buffers are free
-    split_item(Kp, Kst);
-    if (T > 1) split_item(Kp + PARTS, Vp + PARTS);
-    split_item(Vp, Vst);
+    tc::fence_before_sync();
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(bar_q0);  // the first S may start
+    bar_sync(1, NSM);  // every thread has read its Q rows: the buffers under the staged Q are free
+    if (T > 1) split_item(Kp + PARTS, Vp + PARTS);  // K(1)
+    split_item(Vp, Vst);                            // V(0)
     tc::fence_async_smem();
-  }
-  tc::fence_before_sync();
-  __syncthreads();  // K(0), K(1), V(0) parts and Q in place; K part buffer 2 free
-  tc::fence_after_sync();
-  if (!mma_warp) {
+    // Every thread's K(1) staging slots read before any V(1) part lands on them (split_v(0)).
+    bar_sync(1, NSM);
     // In flight during key tile 0: K(2), then V(1) (two cp.async groups, in that order), issued
     // while the tensor core computes the first S (each thread reuses staging slots only it read).
     if (T > 2) stage_item<HD>(Kst, kp, a.k_ss, 2 * KT, S);
@@ -452,6 +457,8 @@ __global__ void __launch_bounds__(NBLK, 1) fwd_tc_kernel(const FwdArgs a) {
     const uint32_t idesc = tc::idesc_f32acc(1, QT, KT);     // S: N = 64 keys
     const uint32_t idesc_pv = tc::idesc_f32acc(1, QT, HD);  // P V: N = the head dim
     const uint32_t sK = tc::smem_u32(Kp), sV = tc::smem_u32(Vp);
+    err |= !tc::mbar_wait(bar_q0, 0, wait_ns(err));  // Q in TMEM, K(0)'s parts in place
+    tc::fence_after_sync();
 #pragma unroll
     for (int t = 0; t < NTILE; ++t)
       if (Tt[t] > 0) {
